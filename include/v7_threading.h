@@ -1,0 +1,113 @@
+/* v7_threading.h -- the drop-in export surface of libv7_threading.so.
+ *
+ * The reference's host loader (src/v7_lib.h:585-739, v7_load) dlopens
+ * libv7_threading.so and resolves 99 names with dlsym, exiting on the first one
+ * missing.  Every function is called with the Microsoft x64 convention
+ * (src/v7_lib.h:40-46: __attribute__((ms_abi)) on Linux).  This library exports
+ * the same 99 names with the same convention, so the reference's loadtests and
+ * validators (tools/b_*_loadtest.cpp, tools/v_*_validate.cpp) run unchanged
+ * against it.
+ *
+ * The v7 hot path (the elementwise / reduction kernels) is implemented on the
+ * GPU: each entry accepts HOST or DEVICE pointers (decided per pointer with
+ * cudaPointerGetAttributes).  Device pointers are used in place; host buffers
+ * are staged through a device workspace.  Every call returns with its results
+ * written, as the reference's do.
+ *
+ * Everything outside that path (models, chat, tokenizer, attention, matmul,
+ * vision, SectorLogo, ...) is exported as a stub: it returns 0/NULL and marks
+ * the engine dead with a reason, which v7_engine_is_dead() /
+ * v7_get_death_reason() report (the reference's FATAL contract,
+ * src/v7_lib.h:179-184).  See v7_threading_stubs.h for that list.
+ */
+#ifndef V7_THREADING_H
+#define V7_THREADING_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__linux__) && defined(__x86_64__)
+#define V7_ABI __attribute__((ms_abi))
+#else
+#define V7_ABI
+#endif
+
+/* Data layouts shared with the reference (src/v7_lib.h:52-62). */
+typedef struct v7_q8_tensor {
+	char *q;  /* int8 codes */
+	float *s; /* one fp32 scale per 64-element group */
+} v7_q8_tensor;
+typedef struct v7_f32_tensor {
+	float *data;
+	float *scales;
+} v7_f32_tensor;
+/* Opaque here: only passed through by the stubs. */
+struct v7_run_state;
+struct v7_config;
+struct inference_context;
+struct v7_probindex;
+
+/* ---- hot path, implemented on the GPU --------------------------------- */
+
+/* src/v7_lib.h:270; rmsnorm_kernel.inc:12-75.  o = (x*scale)*w for one row;
+   size % 32 == 0.  eps = the library's RMS epsilon (v7g_set_rms_eps /
+   ht_add("__sys_rms_eps")). */
+V7_ABI void v7s_rmsnorm(float *o, float *x, float *weight, int size);
+/* src/v7_lib.h:271; add_kernel.inc:26-49.  x += y; n % 32 == 0. */
+V7_ABI void v7s_add_inplace(float *x, float *y, int n);
+/* src/v7_lib.h:272; add_rmsnorm_kernel.inc:15-129.  residual += add (in place),
+   o = rmsnorm(residual)*weight; dim % 8 == 0. */
+V7_ABI void v7s_fused_add_rmsnorm(float *o, float *residual, float *add, float *weight, int dim);
+/* src/v7_lib.h:273; rmsnorm_rope_dispatch.inc:11-52.  One token's n_heads
+   heads, in place, position pos; head_dim % 32 == 0. */
+V7_ABI void v7s_rmsnorm_rope_heads(float *buf, int n_heads, int head_dim, float *norm_weight, float *cos_table, float *sin_table, int pos, int rope_max_dim);
+/* src/v7_lib.h:123; utility_dispatch.inc:110-213.  Q8 quantisation of n floats. */
+V7_ABI void v7d_quantize(char *out_q, float *in_x, float *out_s, int n);
+/* src/v7_lib.h:124; rmsnorm_quantize_kernel.inc:60-218.  RMSNorm then Q8;
+   n % 64 == 0. */
+V7_ABI void v7s_rmsnorm_quantize(char *out_q, float *in_x, float *out_s, int n, float *weight);
+
+/* ---- runtime surface, implemented on the host ------------------------- */
+
+V7_ABI int v7_init(const char *db_path);                 /* src/v7_lib.h:167 */
+V7_ABI int v7_db_load(const char *path);                 /* :168 */
+V7_ABI int v7_db_save(const char *path);                 /* :169 */
+V7_ABI int v7_engine_is_dead(void);                      /* :183 */
+V7_ABI const char *v7_get_death_reason(void);            /* :184 */
+V7_ABI const char *v7_get_version(void);                 /* :185 */
+V7_ABI int v7_get_console_width(void);                   /* :189 */
+V7_ABI int v7_db_add(const char *key, const void *data, int len, unsigned int persist); /* :238 */
+V7_ABI void *v7_db_find(const char *key, unsigned long long *out_len);                 /* :239 */
+V7_ABI void v7_shutdown(void);                           /* :250 */
+V7_ABI void v7s_rope_init(int head_dim, float rope_base);/* :275 */
+V7_ABI void v7s_set_fused_rope(int pos, int head_dim);   /* :276 */
+V7_ABI void v7s_set_spin(int flag);                      /* :278 */
+V7_ABI void v7s_enable_thinking(int on);                 /* :279 */
+V7_ABI void v7s_shutdown(void);                          /* :280 */
+V7_ABI int v7s_get_num_workers(void);                    /* :281 */
+V7_ABI unsigned long long get_config_was_fixed(void);    /* :283 */
+V7_ABI void v7_do_fatal(const char *message);            /* :303 */
+V7_ABI void ht_init(void);                               /* :130 */
+V7_ABI void ht_destroy(void);                            /* :131 */
+V7_ABI int ht_add(const char *key, void *data, unsigned long long data_len, unsigned int persist); /* :132 */
+V7_ABI void *ht_find(const char *key, unsigned long long *out_len);                               /* :133 */
+V7_ABI int db_save(const char *filename);                /* :134 */
+V7_ABI int db_load(const char *filename);                /* :135 */
+V7_ABI void db_set_readonly(int flag);                   /* :138 */
+V7_ABI int v7sprintf(char *buffer, int buf_size, const char *format, ...); /* :318 */
+
+/* Exported data words (src/v7_lib.h:306-314). */
+extern int enable_token_dump;
+extern int enable_dump;
+extern int cpu_features_ok;
+
+#ifdef __cplusplus
+}
+#endif
+
+#include "v7_threading_stubs.h"
+
+#endif

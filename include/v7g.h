@@ -1,0 +1,113 @@
+/* v7g.h -- row-batched, device-resident C-ABI of the B200 (sm_100a) kernels.
+ *
+ * These entry points are the batched form of v7's per-vector kernels: where the
+ * reference normalises ONE row (or one token's heads) per call on the CPU, each
+ * entry here processes `rows` independent rows of device memory in one kernel
+ * launch on `stream` (a cudaStream_t passed as void*, NULL = legacy default
+ * stream).  All pointers are device pointers on the current CUDA device; the
+ * caller owns every buffer and nothing is allocated.  Calls are asynchronous:
+ * results are ready once `stream` has been synchronised.
+ *
+ * Layout (row-major, contiguous rows):
+ *   activations  float [rows, n]
+ *   gamma        float [n]           (shared by all rows / all heads)
+ *   Q8 codes     int8  [rows, n]     (v7_q8_tensor.q, src/v7_lib.h:52-56)
+ *   Q8 scales    float [rows, ceil(n/64)]  one absmax scale per 64-element
+ *                                    group, row order (src/q8_batch4.h:15-19)
+ *
+ * Return value: V7G_OK (0) or a V7G_ERR_* code; v7g_last_error() gives the
+ * message of the calling thread's last failure.  A contract violation is
+ * reported before anything is launched and leaves every output untouched.
+ *
+ * The arithmetic of every kernel reproduces the reference's AVX2 kernel
+ * operation for operation (same rounding steps, same reduction order), so the
+ * results match v7's own library bit for bit on the same input bytes.
+ */
+#ifndef V7G_H
+#define V7G_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum v7g_status {
+	V7G_OK = 0,
+	V7G_ERR_ARG = 1,         /* argument breaks the kernel contract */
+	V7G_ERR_CUDA = 2,        /* a CUDA runtime call failed */
+	V7G_ERR_UNSUPPORTED = 3, /* shape outside what this build implements */
+	V7G_ERR_NO_DEVICE = 4    /* no usable sm_100 device */
+};
+
+/* A1  RMSNorm rows: o[r] = (x[r] * s_r) * w with s_r = 1/sqrt(sum(x[r]^2)/n + eps).
+   Replaces a loop of v7s_rmsnorm (src/v7_lib.h:270, rmsnorm_kernel.inc:12-75).
+   Contract: n > 0, n % 32 == 0.  o may alias x. */
+int v7g_rmsnorm_rows(float *o, const float *x, const float *w, int64_t rows, int n, float eps, void *stream);
+
+/* A2  fused residual-add + RMSNorm rows: residual[r] += add[r] (written back),
+   o[r] = rmsnorm(residual[r]) * w.  Replaces a loop of v7s_fused_add_rmsnorm
+   (src/v7_lib.h:272, add_rmsnorm_kernel.inc:15-129).  Contract: n > 0, n % 8 == 0. */
+int v7g_fused_add_rmsnorm_rows(float *o, float *residual, const float *add, const float *w, int64_t rows, int n, float eps, void *stream);
+
+/* A3  per-head RMSNorm + NeoX half-split RoPE over GQA Q/K, in place.
+   q [tokens, n_q_heads, head_dim], k [tokens, n_kv_heads, head_dim]; token t is
+   at position pos0 + t and reads cos/sin row (pos0 + t) * rope_max_dim (first
+   head_dim/2 entries).  Position 0 normalises without rotating.  Replaces, per
+   token, v7s_rmsnorm_rope_heads on Q then on K (src/v7_lib.h:273,
+   rmsnorm_rope_dispatch.inc:11-52, forward_q8.inc:339-343).
+   Contract: head_dim % 32 == 0, 32 <= head_dim <= 1024, rope_max_dim >= head_dim/2.
+   Either tensor may be NULL with a head count of 0. */
+int v7g_rmsnorm_rope_rows(float *q, float *k, int64_t tokens, int n_q_heads, int n_kv_heads, int head_dim, const float *wq, const float *wk, const float *cos_table, const float *sin_table, int64_t pos0, int rope_max_dim, float eps, void *stream);
+
+/* A5  elementwise SwiGLU: out = (sigmoid(gate) * gate) * up over `count`
+   elements, with v7's polynomial sigmoid (EVAL_SIGMOID, v7_macros.inc:98-160)
+   and its product order (swiglu_q8_kernel.inc:204-209).  out may alias gate or up. */
+int v7g_swiglu(float *out, const float *gate, const float *up, int64_t count, void *stream);
+
+/* A8  SwiGLU then Q8 requantisation per row, the SwiGLU value never leaving
+   registers: codes [rows, n], scales [rows, n/64].  The quantiser follows
+   v7d_quantize (utility_dispatch.inc:110-213, quantize_kernel.inc:43-159).
+   Contract: n > 0, n % 64 == 0. */
+int v7g_swiglu_q8_rows(int8_t *codes, float *scales, const float *gate, const float *up, int64_t rows, int n, void *stream);
+
+/* A6  Q8 quantisation of `rows` vectors of n floats: codes [rows, n], scales
+   [rows, ceil(n/64)].  A trailing group shorter than 64 takes the reference's
+   scalar tail rule.  Replaces a loop of v7d_quantize (src/v7_lib.h:123). */
+int v7g_quantize_rows(int8_t *codes, float *scales, const float *x, int64_t rows, int n, void *stream);
+
+/* A7  x += y over `count` floats.  Replaces v7s_add_inplace (src/v7_lib.h:271,
+   add_kernel.inc:26-49). */
+int v7g_add_inplace(float *x, const float *y, int64_t count, void *stream);
+
+/* Fused RMSNorm -> Q8 per row (v7s_rmsnorm_quantize, src/v7_lib.h:124,
+   rmsnorm_quantize_kernel.inc:60-218): codes [rows, n], scales [rows, n/64].
+   Contract: n > 0, n % 64 == 0. */
+int v7g_rmsnorm_quantize_rows(int8_t *codes, float *scales, const float *x, const float *w, int64_t rows, int n, float eps, void *stream);
+
+/* ---- runtime ---------------------------------------------------------- */
+
+/* RMS epsilon used by the reference-ABI entries (v7s_rmsnorm & co.), which
+   take no eps argument.  The reference reads it from the BSS global g_rms_eps,
+   set from the DB key __sys_rms_eps (inf_microdb.inc:49-53); it is 0 until set. */
+void v7g_set_rms_eps(float eps);
+float v7g_get_rms_eps(void);
+
+/* Message of the calling thread's last failed call ("" when none). */
+const char *v7g_last_error(void);
+
+/* Number of kernels this library has launched in this process. */
+uint64_t v7g_launch_count(void);
+
+/* Library version string. */
+const char *v7g_version(void);
+
+/* Deterministic synthetic input: dst[r, j] ~ N(mean, std) for r in [0, rows),
+   j in [0, n), generated from (seed, row0 + r, j) alone, so any row shard of a
+   larger matrix is reproducible independently on any device. */
+int v7g_fill_normal(float *dst, int64_t rows, int64_t n, int64_t row0, uint64_t seed, float mean, float std, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

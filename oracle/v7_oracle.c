@@ -1,0 +1,566 @@
+/* v7_oracle.c -- CPU restatement of v7's elementwise / reduction kernels.
+ *
+ * TEST INFRASTRUCTURE ONLY (see v7_oracle.h): the parity checker for the
+ * sm_100a kernels, never a product code path.
+ *
+ * Written in plain C, scalar, with the reference's 8-lane YMM registers
+ * spelled out as float[8] arrays so the order of every rounding step is
+ * visible.  Build with -ffp-contract=off: a multiply followed by an add is two
+ * roundings unless fmaf() is written, exactly as in the reference where only
+ * vfmadd* fuse.  MXCSR FTZ+DAZ is switched on around the kernels the
+ * reference runs on its dispatched worker threads, so denormals behave as
+ * there.
+ */
+#include "v7_oracle.h"
+
+#include <math.h>
+#include <pthread.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+#include <xmmintrin.h>
+
+/* ------------------------------------------------------------------------ */
+/* x86 scalar semantics used by the reference                                */
+/* ------------------------------------------------------------------------ */
+
+/* MAXPS/MAXSS dst = max(a, b): returns b when either is NaN or both are zero. */
+static inline float x86_max(float a, float b) { return a > b ? a : b; }
+/* MINPS/MINSS dst = min(a, b): returns b when either is NaN or both are zero. */
+static inline float x86_min(float a, float b) { return a < b ? a : b; }
+
+/* CVTPS2DQ under round-to-nearest-even: NaN and out-of-range give INT_MIN. */
+static inline int32_t x86_cvtps2dq(float p)
+{
+	if (!(fabsf(p) < 2147483648.0f))
+		return INT32_MIN;
+	return (int32_t)rintf(p);
+}
+
+/* VPACKSSDW -> VPACKSSWB -> VPMAXSB(-127): int32 to int8 with saturation,
+   then the -128 code lifted to -127 (quantize_kernel.inc:100-103). */
+static inline int8_t x86_pack_q8(int32_t v)
+{
+	if (v > 32767)
+		v = 32767;
+	if (v < -32768)
+		v = -32768;
+	if (v > 127)
+		v = 127;
+	if (v < -128)
+		v = -128;
+	if (v < -127)
+		v = -127;
+	return (int8_t)v;
+}
+
+static inline float bits_to_float(uint32_t u)
+{
+	float f;
+	memcpy(&f, &u, 4);
+	return f;
+}
+
+#define MXCSR_FTZ_DAZ 0x8040u
+
+/* ------------------------------------------------------------------------ */
+/* shared pieces                                                             */
+/* ------------------------------------------------------------------------ */
+
+/* HADD_YMM (v7_macros.inc:38-45): low128 + high128, then (e0+e1) + (e2+e3). */
+static inline float hadd8(const float s[8])
+{
+	float t0 = s[0] + s[4], t1 = s[1] + s[5], t2 = s[2] + s[6], t3 = s[3] + s[7];
+	float u0 = t0 + t1, u1 = t2 + t3;
+	return u0 + u1;
+}
+
+/* (A+B)+(C+D) merge of the four accumulators (rmsnorm_kernel.inc:43-45),
+   then HADD_YMM. */
+static inline float merge4x8(float acc[4][8])
+{
+	float s[8];
+	for (int c = 0; c < 8; ++c) {
+		float ab = acc[0][c] + acc[1][c];
+		float cd = acc[2][c] + acc[3][c];
+		s[c] = ab + cd;
+	}
+	return hadd8(s);
+}
+
+/* Sum of squares, 8-float block b feeding accumulator b % 4 with FMA
+   (rmsnorm_kernel.inc:22-40; RMSNORM_ROPE_BODY v7_macros.inc:266-289;
+   rmsnorm_quantize_kernel.inc Phase 1).  n % 32 == 0. */
+static float sumsq_blocks(const float *x, int n)
+{
+	float acc[4][8];
+	memset(acc, 0, sizeof(acc));
+	int blocks = n / 8;
+	for (int b = 0; b < blocks; ++b)
+		for (int c = 0; c < 8; ++c) {
+			float v = x[8 * b + c];
+			acc[b & 3][c] = fmaf(v, v, acc[b & 3][c]);
+		}
+	return merge4x8(acc);
+}
+
+/* COMPUTE_RMS_SCALE (v7_macros.inc:348-354): four exact IEEE operations. */
+static inline float rms_scale(float ss, float nf, float eps)
+{
+	float mean = ss / nf;
+	float val = mean + eps;
+	float r = sqrtf(val);
+	return 1.0f / r;
+}
+
+/* EVAL_SIGMOID (v7_macros.inc:98-160), constants from math_data.inc:16-34
+   and sampler.inc:75.  Runs under the caller's MXCSR. */
+static const uint32_t SIG_C5 = 0x3AADD303u, SIG_C4 = 0x3C1E7411u, SIG_C3 = 0x3D635B9Bu, SIG_C2 = 0x3E75FCE0u, SIG_C1 = 0x3F317215u;
+static inline float sigmoid_v7(float g)
+{
+	float t = -g;                      /* sign flip (vxorps with the sign mask) */
+	t = x86_max(t, -80.0f);            /* vmaxps t, t, -80 */
+	t = x86_min(t, 80.0f);             /* vminps t, t, 80 */
+	float fx = t * 1.4426950408889634f; /* x * log2(e) */
+	float ip = rintf(fx);              /* vroundps mode 0 */
+	float f = fx - ip;
+	int32_t ipi = (int32_t)ip;         /* vcvttps2dq of an integral value */
+	float p = fmaf(bits_to_float(SIG_C5), f, bits_to_float(SIG_C4));
+	p = fmaf(p, f, bits_to_float(SIG_C3));
+	p = fmaf(p, f, bits_to_float(SIG_C2));
+	p = fmaf(p, f, bits_to_float(SIG_C1));
+	p = fmaf(p, f, 1.0f);
+	float two_ip = bits_to_float((uint32_t)(ipi + 127) << 23);
+	float e = two_ip * p;
+	float d = e + 1.0f;
+	return 1.0f / d;
+}
+
+/* SwiGLU product order (sig * g) * u (swiglu_q8_kernel.inc:204-209). */
+static inline float swiglu_v7(float g, float u)
+{
+	float sg = sigmoid_v7(g) * g;
+	return sg * u;
+}
+
+/* One full group of 64 values: absmax tree, scale, codes
+   (quantize_kernel.inc:62-106). */
+static void quantize_group64(int8_t *q, float *s, const float *x)
+{
+	float a[64];
+	for (int i = 0; i < 64; ++i)
+		a[i] = fabsf(x[i]);
+	float m[8];
+	for (int c = 0; c < 8; ++c) {
+		float m01 = x86_max(a[c], a[8 + c]);
+		float m23 = x86_max(a[16 + c], a[24 + c]);
+		float m03 = x86_max(m01, m23);
+		float m45 = x86_max(a[32 + c], a[40 + c]);
+		float m67 = x86_max(a[48 + c], a[56 + c]);
+		float m47 = x86_max(m45, m67);
+		m[c] = x86_max(m03, m47);
+	}
+	float v[4];
+	for (int j = 0; j < 4; ++j)
+		v[j] = x86_max(m[j], m[j + 4]);
+	float w0 = x86_max(v[0], v[2]);
+	float w1 = x86_max(v[1], v[3]);
+	float wmax = x86_max(w0, w1);
+	wmax = x86_max(wmax, ORC_Q8_WMAX_FLOOR);
+	float scale = wmax / 127.0f;
+	*s = scale;
+	float recip = 1.0f / scale;
+	for (int i = 0; i < 64; ++i)
+		q[i] = x86_pack_q8(x86_cvtps2dq(x[i] * recip));
+}
+
+/* A trailing group of r < 64 values: scalar path (quantize_kernel.inc:119-152). */
+static void quantize_tail(int8_t *q, float *s, const float *x, int r)
+{
+	float wmax = 0.0f;
+	for (int i = 0; i < r; ++i)
+		wmax = x86_max(fabsf(x[i]), wmax);
+	wmax = x86_max(wmax, ORC_Q8_WMAX_FLOOR);
+	float scale = wmax / 127.0f;
+	*s = scale;
+	float recip = 1.0f / scale;
+	for (int i = 0; i < r; ++i) {
+		float p = x[i] * recip;
+		p = x86_max(p, -127.0f);
+		p = x86_min(p, 127.0f);
+		q[i] = (int8_t)(int32_t)rintf(p);
+	}
+}
+
+static void quantize_vec(int8_t *q, float *s, const float *x, int n)
+{
+	int g = 0;
+	for (; (g + 1) * ORC_Q8_GS <= n; ++g)
+		quantize_group64(q + (int64_t)g * ORC_Q8_GS, s + g, x + (int64_t)g * ORC_Q8_GS);
+	int r = n - g * ORC_Q8_GS;
+	if (r > 0)
+		quantize_tail(q + (int64_t)g * ORC_Q8_GS, s + g, x + (int64_t)g * ORC_Q8_GS, r);
+}
+
+/* ------------------------------------------------------------------------ */
+/* row workers                                                               */
+/* ------------------------------------------------------------------------ */
+
+static void rmsnorm_row(float *o, const float *x, const float *w, int n, float eps)
+{
+	float scale = rms_scale(sumsq_blocks(x, n), (float)n, eps);
+	for (int i = 0; i < n; ++i) {
+		float t = x[i] * scale;
+		o[i] = t * w[i];
+	}
+}
+
+static void fused_add_rmsnorm_row(float *o, float *r, const float *a, const float *w, int n, float eps)
+{
+	float acc[4][8];
+	memset(acc, 0, sizeof(acc));
+	int blocks = n / 8;
+	int left = blocks & 3;
+	/* leftover blocks first, all into accumulator A */
+	for (int b = 0; b < left; ++b)
+		for (int c = 0; c < 8; ++c) {
+			float sv = r[8 * b + c] + a[8 * b + c];
+			r[8 * b + c] = sv;
+			acc[0][c] = fmaf(sv, sv, acc[0][c]);
+		}
+	for (int b = left; b < blocks; ++b)
+		for (int c = 0; c < 8; ++c) {
+			float sv = r[8 * b + c] + a[8 * b + c];
+			r[8 * b + c] = sv;
+			acc[(b - left) & 3][c] = fmaf(sv, sv, acc[(b - left) & 3][c]);
+		}
+	float scale = rms_scale(merge4x8(acc), (float)n, eps);
+	for (int i = 0; i < n; ++i) {
+		float t = r[i] * scale;
+		o[i] = t * w[i];
+	}
+}
+
+/* RMSNORM_ROPE_BODY (v7_macros.inc:263-339) for one head. */
+static void rmsnorm_rope_head(float *x, int head_dim, const float *w, const float *cs, const float *sn, int64_t pos, float eps)
+{
+	float scale = rms_scale(sumsq_blocks(x, head_dim), (float)head_dim, eps);
+	if (pos == 0) {
+		for (int i = 0; i < head_dim; ++i) {
+			float t = x[i] * scale;
+			x[i] = t * w[i];
+		}
+		return;
+	}
+	int half = head_dim / 2;
+	for (int j = 0; j < half; ++j) {
+		float e = (x[j] * scale) * w[j];
+		float o = (x[j + half] * scale) * w[j + half];
+		float ec = e * cs[j];
+		float es = e * sn[j];
+		x[j] = fmaf(-o, sn[j], ec);
+		x[j + half] = fmaf(o, cs[j], es);
+	}
+}
+
+static void rmsnorm_quantize_row(int8_t *q, float *s, const float *x, const float *w, int n, float eps)
+{
+	float scale = rms_scale(sumsq_blocks(x, n), (float)n, eps);
+	float norm[ORC_Q8_GS];
+	for (int g = 0; g < n / ORC_Q8_GS; ++g) {
+		const float *xg = x + g * ORC_Q8_GS;
+		const float *wg = w + g * ORC_Q8_GS;
+		for (int i = 0; i < ORC_Q8_GS; ++i) {
+			float t = scale * xg[i];
+			norm[i] = t * wg[i];
+		}
+		quantize_group64(q + g * ORC_Q8_GS, s + g, norm);
+	}
+}
+
+/* ------------------------------------------------------------------------ */
+/* row-parallel driver                                                       */
+/* ------------------------------------------------------------------------ */
+
+typedef struct job {
+	int kind;
+	int64_t r0, r1;
+	int ftz;
+	/* arguments */
+	float *fo;
+	float *fr;
+	const float *fx;
+	const float *fy;
+	const float *fw;
+	const float *fc;
+	const float *fs;
+	int8_t *q;
+	float *sc;
+	int64_t n64;
+	int n, heads, rope_max_dim;
+	int64_t pos0;
+	float eps;
+} job;
+
+enum { K_RMSNORM, K_ADD_RMSNORM, K_ROPE, K_SWIGLU, K_QUANT, K_SWIGLU_Q8, K_ADD, K_RMSNORM_Q8 };
+
+static void run_job(job *j)
+{
+	unsigned saved = _mm_getcsr();
+	if (j->ftz)
+		_mm_setcsr(saved | MXCSR_FTZ_DAZ);
+	else
+		_mm_setcsr(saved & ~MXCSR_FTZ_DAZ);
+	for (int64_t r = j->r0; r < j->r1; ++r) {
+		switch (j->kind) {
+		case K_RMSNORM:
+			rmsnorm_row(j->fo + r * j->n, j->fx + r * j->n, j->fw, j->n, j->eps);
+			break;
+		case K_ADD_RMSNORM:
+			fused_add_rmsnorm_row(j->fo + r * j->n, j->fr + r * j->n, j->fy + r * j->n, j->fw, j->n, j->eps);
+			break;
+		case K_ROPE: {
+			int64_t pos = j->pos0 + r;
+			float *tok = j->fr + r * (int64_t)j->heads * j->n;
+			const float *cs = j->fc + pos * j->rope_max_dim;
+			const float *sn = j->fs + pos * j->rope_max_dim;
+			for (int h = 0; h < j->heads; ++h)
+				rmsnorm_rope_head(tok + (int64_t)h * j->n, j->n, j->fw, cs, sn, pos, j->eps);
+			break;
+		}
+		case K_SWIGLU: /* rows here are chunks of 4096 elements */
+		{
+			int64_t b = r * 4096, e = b + 4096 < j->n64 ? b + 4096 : j->n64;
+			for (int64_t i = b; i < e; ++i)
+				j->fo[i] = swiglu_v7(j->fx[i], j->fy[i]);
+			break;
+		}
+		case K_QUANT: {
+			int64_t ng = (j->n + ORC_Q8_GS - 1) / ORC_Q8_GS;
+			quantize_vec(j->q + r * j->n, j->sc + r * ng, j->fx + r * j->n, j->n);
+			break;
+		}
+		case K_SWIGLU_Q8: {
+			float h[ORC_Q8_GS];
+			int64_t ng = j->n / ORC_Q8_GS;
+			for (int64_t g = 0; g < ng; ++g) {
+				int64_t off = r * j->n + g * ORC_Q8_GS;
+				for (int i = 0; i < ORC_Q8_GS; ++i)
+					h[i] = swiglu_v7(j->fx[off + i], j->fy[off + i]);
+				quantize_group64(j->q + off, j->sc + r * ng + g, h);
+			}
+			break;
+		}
+		case K_ADD: {
+			int64_t b = r * 4096, e = b + 4096 < j->n64 ? b + 4096 : j->n64;
+			for (int64_t i = b; i < e; ++i)
+				j->fo[i] = j->fo[i] + j->fy[i];
+			break;
+		}
+		case K_RMSNORM_Q8: {
+			int64_t ng = j->n / ORC_Q8_GS;
+			rmsnorm_quantize_row(j->q + r * j->n, j->sc + r * ng, j->fx + r * j->n, j->fw, j->n, j->eps);
+			break;
+		}
+		}
+	}
+	_mm_setcsr(saved);
+}
+
+static void *thread_main(void *p)
+{
+	run_job((job *)p);
+	return NULL;
+}
+
+static int run_rows(const job *proto, int64_t rows, int nthreads)
+{
+	if (rows <= 0)
+		return 0;
+	if (nthreads < 1)
+		nthreads = 1;
+	if (nthreads > 256)
+		nthreads = 256;
+	if (nthreads > rows)
+		nthreads = (int)rows;
+	if (nthreads == 1) {
+		job j = *proto;
+		j.r0 = 0;
+		j.r1 = rows;
+		run_job(&j);
+		return 0;
+	}
+	job jobs[256];
+	pthread_t tid[256];
+	for (int t = 0; t < nthreads; ++t) {
+		jobs[t] = *proto;
+		jobs[t].r0 = rows * t / nthreads;
+		jobs[t].r1 = rows * (t + 1) / nthreads;
+	}
+	for (int t = 1; t < nthreads; ++t) {
+		if (pthread_create(&tid[t], NULL, thread_main, &jobs[t]) != 0) {
+			/* run the chunk on this thread when no thread can be created */
+			run_job(&jobs[t]);
+			tid[t] = 0;
+		}
+	}
+	run_job(&jobs[0]);
+	for (int t = 1; t < nthreads; ++t)
+		if (tid[t])
+			pthread_join(tid[t], NULL);
+	return 0;
+}
+
+/* ------------------------------------------------------------------------ */
+/* public entry points                                                       */
+/* ------------------------------------------------------------------------ */
+
+int orc_rmsnorm_rows(float *o, const float *x, const float *w, int64_t rows, int n, float eps, int nthreads)
+{
+	if (n <= 0 || n % 32 != 0 || rows < 0)
+		return -1;
+	job j = { 0 };
+	j.kind = K_RMSNORM;
+	j.ftz = 0;
+	j.fo = o;
+	j.fx = x;
+	j.fw = w;
+	j.n = n;
+	j.eps = eps;
+	return run_rows(&j, rows, nthreads);
+}
+
+int orc_fused_add_rmsnorm_rows(float *o, float *residual, const float *add, const float *w, int64_t rows, int n, float eps, int nthreads)
+{
+	if (n <= 0 || n % 8 != 0 || rows < 0)
+		return -1;
+	job j = { 0 };
+	j.kind = K_ADD_RMSNORM;
+	j.ftz = 0;
+	j.fo = o;
+	j.fr = residual;
+	j.fy = add;
+	j.fw = w;
+	j.n = n;
+	j.eps = eps;
+	return run_rows(&j, rows, nthreads);
+}
+
+int orc_rmsnorm_rope_rows(float *buf, int64_t tokens, int n_heads, int head_dim, const float *w, const float *cos_table, const float *sin_table, int64_t pos0, int rope_max_dim, float eps, int nthreads)
+{
+	if (head_dim <= 0 || head_dim % 32 != 0 || n_heads < 0 || tokens < 0 || pos0 < 0 || rope_max_dim < head_dim / 2)
+		return -1;
+	job j = { 0 };
+	j.kind = K_ROPE;
+	j.ftz = 1;
+	j.fr = buf;
+	j.fw = w;
+	j.fc = cos_table;
+	j.fs = sin_table;
+	j.n = head_dim;
+	j.heads = n_heads;
+	j.pos0 = pos0;
+	j.rope_max_dim = rope_max_dim;
+	j.eps = eps;
+	return run_rows(&j, tokens, nthreads);
+}
+
+float orc_sigmoid(float g)
+{
+	unsigned saved = _mm_getcsr();
+	_mm_setcsr(saved | MXCSR_FTZ_DAZ);
+	float r = sigmoid_v7(g);
+	_mm_setcsr(saved);
+	return r;
+}
+
+int orc_swiglu(float *out, const float *g, const float *u, int64_t n, int nthreads)
+{
+	if (n < 0)
+		return -1;
+	job j = { 0 };
+	j.kind = K_SWIGLU;
+	j.ftz = 1;
+	j.fo = out;
+	j.fx = g;
+	j.fy = u;
+	j.n64 = n;
+	return run_rows(&j, (n + 4095) / 4096, nthreads);
+}
+
+int orc_quantize_rows(int8_t *q, float *s, const float *x, int64_t rows, int n, int nthreads)
+{
+	if (n <= 0 || rows < 0)
+		return -1;
+	job j = { 0 };
+	j.kind = K_QUANT;
+	j.ftz = 1;
+	j.q = q;
+	j.sc = s;
+	j.fx = x;
+	j.n = n;
+	return run_rows(&j, rows, nthreads);
+}
+
+int orc_swiglu_q8_rows(int8_t *q, float *s, const float *g, const float *u, int64_t rows, int n, int nthreads)
+{
+	if (n <= 0 || n % ORC_Q8_GS != 0 || rows < 0)
+		return -1;
+	job j = { 0 };
+	j.kind = K_SWIGLU_Q8;
+	j.ftz = 1;
+	j.q = q;
+	j.sc = s;
+	j.fx = g;
+	j.fy = u;
+	j.n = n;
+	return run_rows(&j, rows, nthreads);
+}
+
+int orc_add_inplace(float *x, const float *y, int64_t n, int nthreads)
+{
+	if (n < 0)
+		return -1;
+	job j = { 0 };
+	j.kind = K_ADD;
+	j.ftz = 0;
+	j.fo = x;
+	j.fy = y;
+	j.n64 = n;
+	return run_rows(&j, (n + 4095) / 4096, nthreads);
+}
+
+int orc_rmsnorm_quantize_rows(int8_t *q, float *s, const float *x, const float *w, int64_t rows, int n, float eps, int nthreads)
+{
+	if (n <= 0 || n % ORC_Q8_GS != 0 || rows < 0)
+		return -1;
+	job j = { 0 };
+	j.kind = K_RMSNORM_Q8;
+	j.ftz = 1;
+	j.q = q;
+	j.sc = s;
+	j.fx = x;
+	j.fw = w;
+	j.n = n;
+	j.eps = eps;
+	return run_rows(&j, rows, nthreads);
+}
+
+int orc_rope_tables(float *cos_table, float *sin_table, int64_t positions, int half, int stride, double base)
+{
+	if (half <= 0 || stride < half || positions < 0 || !(base > 0.0))
+		return -1;
+	for (int64_t p = 0; p < positions; ++p)
+		for (int j = 0; j < stride; ++j) {
+			if (j < half) {
+				double freq = pow(base, -(double)j / (double)half);
+				double ang = (double)p * freq;
+				cos_table[p * stride + j] = (float)cos(ang);
+				sin_table[p * stride + j] = (float)sin(ang);
+			} else {
+				cos_table[p * stride + j] = 0.0f;
+				sin_table[p * stride + j] = 0.0f;
+			}
+		}
+	return 0;
+}
