@@ -1,0 +1,570 @@
+#!/usr/bin/env python
+"""bench.py -- throughput of v7's fused elementwise/reduction path on B200.
+
+Workload (the largest and the one sharded over GPUs):
+C5 SwiGLU + Q8 requantisation, gate/up [16384, 12288] fp32 ~ N(0, 2) ->
+int8 codes [16384, 12288] + fp32 scales [16384, 192].  The 16384 rows are
+split into contiguous shards, one per GPU (rank r takes rows
+[r*R/N, (r+1)*R/N)), with no collective on the timed path (rows are
+independent): total work is fixed, so scaling is strong.  A step is one launch
+of the fused kernel over the rank's shard.
+
+Reported (one JSON line from rank 0):
+  value      whole-job algorithmic GB/s (inputs read once + outputs written
+             once) / max-over-ranks device time, inputs resident in HBM
+  e2e        the same metric through the public API with host buffers: every
+             step copies the shard's gate/up from pinned host memory and reads
+             codes/scales back (pipelined in row chunks over three streams)
+  roofline   the kernel's achieved GB/s against the measured HBM copy peak
+  cpu_baseline  the oracle port on the host cores, bounded sample (N=1 only)
+  kernels    the other BASELINE configs (C1-C4, add_inplace, RMSNorm->Q8),
+             device-timed, N=1 only
+``--impl reference`` times the CPU implementation instead (rank 0 only).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "fused-kernel HBM GB/s (% of B200 peak) and rows/s at 1/2/4/8 GPUs"
+L2_BYTES = 126 * 2**20
+C5_ROWS, C5_N = 16384, 12288
+GROUP = 64
+
+
+def c5_bytes(rows: int, n: int = C5_N) -> int:
+    """Algorithmic bytes: gate + up read once, codes + scales written once."""
+    return rows * (n * 4 * 2 + n + (n // GROUP) * 4)
+
+
+def measured_peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def ncu_traffic() -> dict:
+    """Per-launch DRAM bytes of each kernel from the committed ncu summary."""
+    p = ROOT / "profiles" / "ncu_traffic.json"
+    return json.loads(p.read_text()) if p.exists() else {}
+
+
+# ------------------------------------------------------------------ clocks
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML while running."""
+
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4,
+               "hw_power_brake_slowdown": 0x80}
+
+    def __init__(self, device_index: int, period_s: float = 0.005):
+        self.samples: list[tuple[int, int, int]] = []
+        self.period = period_s
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+            self.h = pynvml.nvmlDeviceGetHandleByUUID(uuid.encode())
+            self.nvml = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # pragma: no cover - reported in the JSON line
+            self.err = repr(e)
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        n = self.nvml
+        while True:
+            try:
+                sm = n.nvmlDeviceGetClockInfo(self.h, n.NVML_CLOCK_SM)
+                reasons = n.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                util = n.nvmlDeviceGetUtilizationRates(self.h).gpu
+                self.samples.append((sm, reasons, util))
+            except Exception:
+                pass
+            if self._stop.wait(self.period):
+                break
+
+    def __enter__(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._t:
+            self._t.join()
+
+    def summary(self) -> dict:
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": getattr(self, "err", "nvml unavailable")}
+        loaded = [s for s in self.samples if s[2] > 0] or self.samples
+        reasons = sorted({name for _, r, _ in loaded for name, bit in self.REASONS.items() if r & bit})
+        return {"sm_mhz": statistics.median(s[0] for s in loaded) if loaded else None, "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(loaded), "source": "NVML, sampled every 5 ms in the timed region"}
+
+
+# ------------------------------------------------------------ distributed
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def shard(rows: int, rank: int, world: int) -> tuple[int, int]:
+    """Contiguous row shard of rank (balanced to within one row)."""
+    return rows * rank // world, rows * (rank + 1) // world
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t)
+    return float(t.item())
+
+
+def barrier(world: int) -> None:
+    if world > 1:
+        torch.distributed.barrier()
+
+
+# ------------------------------------------------------------ timing helpers
+
+
+def time_launches(fn, steps: int, stream: torch.cuda.Stream, flush: torch.Tensor | None = None):
+    """Runs fn() `steps` times on `stream`; returns (region_ms, per-launch ms list).
+    With `flush`, a buffer larger than L2 is rewritten before every launch
+    (outside the launch's own events)."""
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for a, b in ev:
+            if flush is not None:
+                flush.add_(1)
+            a.record(stream)
+            fn()
+            b.record(stream)
+        end.record(stream)
+    stream.synchronize()
+    return start.elapsed_time(end), [a.elapsed_time(b) for a, b in ev]
+
+
+# --------------------------------------------------------------- our arm
+
+
+def run_ours(args, rank: int, world: int, local: int) -> None:
+    import v7multiplikator_b200 as v7g
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    peak, peak_kind = measured_peaks()
+    r0, r1 = shard(C5_ROWS, rank, world)
+    rows = r1 - r0
+    g = torch.empty(rows, C5_N, device=dev)
+    u = torch.empty(rows, C5_N, device=dev)
+    v7g.fill_normal(g, seed=12, mean=0.0, std=2.0, row0=r0)
+    v7g.fill_normal(u, seed=13, mean=0.0, std=2.0, row0=r0)
+    codes = torch.empty(rows, C5_N, dtype=torch.int8, device=dev)
+    scales = torch.empty(rows, C5_N // GROUP, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def step():
+        v7g.swiglu_q8_rows(codes, scales, g, u, stream=stream)
+
+    torch.cuda.synchronize()  # inputs were written on the default stream
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+    stream.synchronize()
+    barrier(world)
+
+    launches0 = v7g.launch_count()
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+        region_ms, per_launch = time_launches(step, args.steps, stream)
+        torch.cuda.synchronize()
+        barrier(world)
+    launches = v7g.launch_count() - launches0
+    t_max = max_over_ranks(region_ms, world)
+    total_bytes = c5_bytes(C5_ROWS) * args.steps
+    value = total_bytes / (t_max * 1e-3) / 1e9
+    rows_per_s = C5_ROWS * args.steps / (t_max * 1e-3)
+    launch_ms = statistics.mean(per_launch)
+    achieved = c5_bytes(rows) / (launch_ms * 1e-3) / 1e9
+    gpu_launches = int(sum_over_ranks(launches, world))
+
+    # verification gather (NCCL, outside the timed region): per-rank checksums
+    chk = torch.stack([codes.view(-1).to(torch.int64).sum(), scales.double().sum().to(torch.int64)])
+    if world > 1:
+        gathered = [torch.empty_like(chk) for _ in range(world)]
+        torch.distributed.all_gather(gathered, chk)
+        chk_all = torch.stack(gathered).cpu().tolist()
+    else:
+        chk_all = [chk.cpu().tolist()]
+
+    e2e = run_e2e(args, v7g, dev, g, u, codes, scales, rows, world)
+
+    table = None
+    cpu = None
+    if world == 1 and not args.no_extras:
+        table = kernel_table(v7g, dev, stream, peak)
+        cpu = cpu_baseline(args)
+    traffic = ncu_traffic().get("swiglu_q8_c5_per_row")
+    line = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "rows_per_s": round(rows_per_s, 1),
+        "pct_of_peak": round(100.0 * value / (world * peak), 2),
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(t_max / args.steps, 6),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic: counter-based N(0, 2) gate/up (seed 12/13), generated on device per row shard",
+        "config": {
+            "workload": "C5 SwiGLU + Q8 requantisation: gate/up [16384, 12288] fp32 -> int8 codes [16384, 12288] "
+                        "+ fp32 scales [16384, 192] (one per 64-element group)",
+            "rows": C5_ROWS, "n": C5_N, "rows_per_gpu": rows, "parallelism": f"row-shard x{world}, no collective",
+            "bytes_per_row": c5_bytes(1), "l2": "inputs 1.61 GB > 126 MB L2: no flush needed",
+        },
+        "roofline": {
+            "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs copy)",
+            "traffic": round(traffic * rows) if traffic else None, "launch_ms": round(launch_ms, 5),
+            "kernel": "k_q8_groups<true> (v7g_swiglu_q8_rows)",
+        },
+        "e2e": e2e,
+        "clocks": clk.summary(),
+        "gpu_launches": gpu_launches,
+        "checksums": chk_all,
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    if table is not None:
+        line["kernels"] = table
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+def run_e2e(args, v7g, dev, g, u, codes, scales, rows, world):
+    """Public-API end to end: pinned host gate/up in, codes/scales out, every
+    step.  Rows go in chunks over three streams so the host-to-device copy of
+    chunk i+1 overlaps the kernel and the device-to-host copy of chunk i."""
+    hg = torch.empty(rows, C5_N, dtype=torch.float32, pin_memory=True)
+    hu = torch.empty(rows, C5_N, dtype=torch.float32, pin_memory=True)
+    hg.copy_(g)
+    hu.copy_(u)
+    hc = torch.empty(rows, C5_N, dtype=torch.int8, pin_memory=True)
+    hs = torch.empty(rows, C5_N // GROUP, dtype=torch.float32, pin_memory=True)
+    streams = [torch.cuda.Stream(device=dev) for _ in range(3)]
+    nchunks = max(1, min(16, rows // 256))
+    bounds = [(rows * i // nchunks, rows * (i + 1) // nchunks) for i in range(nchunks)]
+
+    def step():
+        for i, (a, b) in enumerate(bounds):
+            s = streams[i % len(streams)]
+            with torch.cuda.stream(s):
+                g[a:b].copy_(hg[a:b], non_blocking=True)
+                u[a:b].copy_(hu[a:b], non_blocking=True)
+                v7g.swiglu_q8_rows(codes[a:b], scales[a:b], g[a:b], u[a:b], stream=s)
+                hc[a:b].copy_(codes[a:b], non_blocking=True)
+                hs[a:b].copy_(scales[a:b], non_blocking=True)
+
+    steps = max(3, min(args.steps, 20))
+    step()
+    torch.cuda.synchronize()
+    barrier(world)
+    t0 = time.perf_counter()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    cur = torch.cuda.current_stream(dev)
+    start.record(cur)
+    for _ in range(steps):
+        for s in streams:
+            s.wait_stream(cur)
+        step()
+        for s in streams:
+            cur.wait_stream(s)
+    end.record(cur)
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    wall = (time.perf_counter() - t0) * 1e3
+    t_max = max_over_ranks(ms, world)
+    value = c5_bytes(C5_ROWS) * steps / (t_max * 1e-3) / 1e9
+    return {"value": round(value, 2), "unit": "GB/s", "steps": steps,
+            "h2d_bytes_per_step": int(C5_ROWS * C5_N * 8), "d2h_bytes_per_step": int(C5_ROWS * (C5_N + C5_N // GROUP * 4)),
+            "ms_per_step": round(t_max / steps, 4), "wall_ms_per_step_rank0": round(wall / steps, 4),
+            "path": f"pinned host -> v7g_swiglu_q8_rows -> pinned host, {nchunks} row chunks on 3 streams"}
+
+
+def kernel_table(v7g, dev, stream, peak) -> dict:
+    """Device-timed GB/s of the other BASELINE configs on one GPU.  C1 and C2
+    (inputs under the L2 size) rewrite a 512 MB buffer before every launch."""
+    out = {}
+    flush = torch.zeros(128 * 2**20, device=dev)  # 512 MB > L2
+    K = 50
+
+    def rec(name, fn, nbytes, rows, flushed, note=""):
+        torch.cuda.synchronize()  # inputs were written on the default stream
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                fn()
+        stream.synchronize()
+        _, per = time_launches(fn, K, stream, flush if flushed else None)
+        ms = statistics.median(per)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[name] = {"gbs": round(gbs, 1), "frac": round(gbs / peak, 4), "us": round(ms * 1e3, 2),
+                     "rows_per_s": round(rows / (ms * 1e-3), 1), "bytes": nbytes, "l2_flushed": flushed}
+        if note:
+            out[name]["note"] = note
+
+    def fill(shape, seed, mean, std):
+        t = torch.empty(*shape, device=dev)
+        return v7g.fill_normal(t.view(-1, shape[-1]), seed=seed, mean=mean, std=std)
+
+    # C1 RMSNorm x[64, 2048]
+    x = fill((64, 2048), 1, 0.0, 1.0)
+    w = fill((1, 2048), 2, 1.0, 0.1)[0]
+    o = torch.empty_like(x)
+    rec("c1_rmsnorm_64x2048", lambda: v7g.rmsnorm_rows(o, x, w, 1e-6, stream=stream), 64 * 2048 * 8 + 2048 * 4, 64, True,
+        "launch/latency-bound: 1 MiB of traffic")
+    # C2 fused add + RMSNorm [4096, 2048]
+    r = fill((4096, 2048), 3, 0.0, 1.0)
+    d = fill((4096, 2048), 4, 0.0, 0.5)
+    o2 = torch.empty_like(r)
+    rec("c2_fused_add_rmsnorm_4096x2048", lambda: v7g.fused_add_rmsnorm_rows(o2, r, d, w, 1e-6, stream=stream),
+        4096 * 2048 * 16 + 2048 * 4, 4096, True)
+    rec("add_inplace_4096x2048", lambda: v7g.add_inplace(r, d, stream=stream), 4096 * 2048 * 12, 4096, True)
+    from v7multiplikator_b200.tables import rope_tables
+    # C3 RMSNorm + RoPE Q[8192,16,128] K[8192,8,128]
+    q = fill((8192, 16 * 128), 6, 0.0, 1.0).view(8192, 16, 128)
+    k = fill((8192, 8 * 128), 7, 0.0, 1.0).view(8192, 8, 128)
+    wq = fill((1, 128), 8, 1.0, 0.1)[0]
+    wk = fill((1, 128), 9, 1.0, 0.1)[0]
+    cos, sin = (torch.from_numpy(t).to(dev) for t in rope_tables(8192, 64, 64, 1e6))
+    rec("c3_rmsnorm_rope_8192x(16+8)x128", lambda: v7g.rmsnorm_rope_rows(q, k, wq, wk, cos, sin, 0, 1e-6, stream=stream),
+        8192 * 24 * 128 * 8 + 8192 * 64 * 8 + 2 * 128 * 4, 8192, False)
+    del q, k
+    # C4 SwiGLU [4096, 8192]
+    gg = fill((4096, 8192), 10, 0.0, 2.0)
+    uu = fill((4096, 8192), 11, 0.0, 2.0)
+    oo = torch.empty_like(gg)
+    rec("c4_swiglu_4096x8192", lambda: v7g.swiglu(oo, gg, uu, stream=stream), 4096 * 8192 * 12, 4096, False)
+    # RMSNorm -> Q8 at the C2 shape
+    codes = torch.empty(4096, 2048, dtype=torch.int8, device=dev)
+    sc = torch.empty(4096, 32, device=dev)
+    rec("rmsnorm_quantize_4096x2048", lambda: v7g.rmsnorm_quantize_rows(codes, sc, r, w, 1e-6, stream=stream),
+        4096 * (2048 * 5 + 32 * 4) + 2048 * 4, 4096, True)
+    return out
+
+
+def cpu_baseline(args) -> dict:
+    """The oracle port of the reference's AVX2 kernels on the host cores, on
+    a bounded sample of C5 rows (calibrated to ~10 s of work)."""
+    from oracle.pyoracle import Oracle
+    threads = os.cpu_count() or 1
+    orc = Oracle(nthreads=threads)
+    rng = np.random.default_rng(0)
+    cal_rows = 64
+    g = rng.normal(0, 2, (cal_rows, C5_N)).astype(np.float32)
+    u = rng.normal(0, 2, (cal_rows, C5_N)).astype(np.float32)
+    t = time.perf_counter()
+    orc.swiglu_q8(g, u)
+    dt = max(time.perf_counter() - t, 1e-4)
+    rows = int(min(C5_ROWS, max(cal_rows, cal_rows * args.cpu_seconds / dt)))
+    g = rng.normal(0, 2, (rows, C5_N)).astype(np.float32)
+    u = rng.normal(0, 2, (rows, C5_N)).astype(np.float32)
+    t = time.perf_counter()
+    orc.swiglu_q8(g, u)
+    dt = time.perf_counter() - t
+    gbs = c5_bytes(rows) / dt / 1e9
+    return {"value": round(gbs, 3), "unit": "GB/s", "rows_per_s": round(rows / dt, 1), "cores": threads, "kind": "port",
+            "sample": f"{rows} of 16384 C5 rows ({dt:.1f} s), oracle/v7_oracle.c restatement, {threads} threads",
+            "cpu_model": cpu_model()}
+
+
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+# ------------------------------------------------------------ reference arm
+
+
+def run_reference(args, rank: int, world: int) -> None:
+    """The reference path's CPU implementation (the oracle port: the reference's
+    NASM engine cannot be assembled here), all host threads, C5, each step a
+    bounded row sample.  Rank 0 only."""
+    if rank != 0:
+        return
+    from oracle.pyoracle import Oracle
+    threads = os.cpu_count() or 1
+    orc = Oracle(nthreads=threads)
+    rng = np.random.default_rng(0)
+    rows = min(C5_ROWS, args.ref_rows)
+    g = rng.normal(0, 2, (rows, C5_N)).astype(np.float32)
+    u = rng.normal(0, 2, (rows, C5_N)).astype(np.float32)
+    for _ in range(args.warmup):
+        orc.swiglu_q8(g, u)
+    times = []
+    for _ in range(args.steps):
+        t = time.perf_counter()
+        orc.swiglu_q8(g, u)
+        times.append(time.perf_counter() - t)
+    total = sum(times)
+    value = c5_bytes(rows) * args.steps / total / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
+        "rows_per_s": round(rows * args.steps / total, 1), "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(total / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic: numpy N(0, 2) gate/up, seed 0",
+        "config": {"workload": "C5 SwiGLU + Q8 requantisation, gate/up [16384, 12288] fp32 (row sample per step)",
+                   "rows": C5_ROWS, "n": C5_N, "sample_rows_per_step": rows, "parallelism": f"{threads} host threads"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": f"{rows} rows of C5 per step", "cpu_model": cpu_model()},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference engine is NASM; nasm is absent on this image, so its restatement (oracle/v7_oracle.c) "
+                "is timed",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def _profile_case(name: str, rows: int, dev):
+    """Inputs and launcher of one kernel at `rows` rows of its BASELINE shape."""
+    import v7multiplikator_b200 as v7g
+
+    def fill(shape, seed, mean, std):
+        t = torch.empty(*shape, device=dev)
+        return v7g.fill_normal(t.view(-1, shape[-1]), seed=seed, mean=mean, std=std)
+
+    if name == "swiglu_q8":
+        g, u = fill((rows, C5_N), 12, 0.0, 2.0), fill((rows, C5_N), 13, 0.0, 2.0)
+        c = torch.empty(rows, C5_N, dtype=torch.int8, device=dev)
+        s = torch.empty(rows, C5_N // GROUP, device=dev)
+        return lambda: v7g.swiglu_q8_rows(c, s, g, u), c5_bytes(rows)
+    if name == "swiglu":
+        g, u = fill((rows, 8192), 10, 0.0, 2.0), fill((rows, 8192), 11, 0.0, 2.0)
+        o = torch.empty_like(g)
+        return lambda: v7g.swiglu(o, g, u), rows * 8192 * 12
+    if name in ("rmsnorm", "fused_add_rmsnorm", "add_inplace", "rmsnorm_quantize"):
+        x, d = fill((rows, 2048), 3, 0.0, 1.0), fill((rows, 2048), 4, 0.0, 0.5)
+        w = fill((1, 2048), 5, 1.0, 0.1)[0]
+        o = torch.empty_like(x)
+        if name == "rmsnorm":
+            return lambda: v7g.rmsnorm_rows(o, x, w, 1e-6), rows * 2048 * 8
+        if name == "fused_add_rmsnorm":
+            return lambda: v7g.fused_add_rmsnorm_rows(o, x, d, w, 1e-6), rows * 2048 * 16
+        if name == "add_inplace":
+            return lambda: v7g.add_inplace(x, d), rows * 2048 * 12
+        c = torch.empty(rows, 2048, dtype=torch.int8, device=dev)
+        s = torch.empty(rows, 32, device=dev)
+        return lambda: v7g.rmsnorm_quantize_rows(c, s, x, w, 1e-6), rows * (2048 * 5 + 128)
+    if name == "rmsnorm_rope":
+        from v7multiplikator_b200.tables import rope_tables
+        q, k = fill((rows, 16 * 128), 6, 0.0, 1.0).view(rows, 16, 128), fill((rows, 8 * 128), 7, 0.0, 1.0).view(rows, 8, 128)
+        wq, wk = fill((1, 128), 8, 1.0, 0.1)[0], fill((1, 128), 9, 1.0, 0.1)[0]
+        cos, sin = (torch.from_numpy(t).to(dev) for t in rope_tables(rows, 64, 64, 1e6))
+        return lambda: v7g.rmsnorm_rope_rows(q, k, wq, wk, cos, sin, 0, 1e-6), rows * (24 * 128 * 8 + 64 * 8)
+    raise ValueError(name)
+
+
+PROFILE_CASES = ("swiglu_q8", "swiglu", "rmsnorm", "fused_add_rmsnorm", "add_inplace", "rmsnorm_quantize", "rmsnorm_rope")
+
+
+def run_profile(args) -> None:
+    """A small, fixed case for ncu: fill, `warmup` + `steps` launches of one
+    kernel, one line of device-timed GB/s (not a bench value)."""
+    dev = torch.device("cuda", 0)
+    fn, nbytes = _profile_case(args.profile, args.rows, dev)
+    torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / args.steps
+    print(json.dumps({"profile": args.profile, "rows": args.rows, "bytes_per_launch": nbytes, "us": round(ms * 1e3, 2),
+                      "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1)}))
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-extras", action="store_true", help="skip the per-config table and the CPU baseline")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample size in seconds of work")
+    ap.add_argument("--ref-rows", type=int, default=1024, help="rows of C5 per reference-arm step")
+    ap.add_argument("--profile", choices=sorted(PROFILE_CASES), help="profiling mode: launch one kernel --steps times "
+                    "on a --rows-row case and exit (for ncu captures)")
+    ap.add_argument("--rows", type=int, default=2048, help="rows of the --profile case")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    rank, world, local = dist_env()
+    if args.profile:
+        run_profile(args)
+        return
+    if world != args.gpus:
+        if world == 1 and args.gpus > 1:
+            ap.error("--gpus > 1 needs torchrun (one process per GPU)")
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    run_ours(args, rank, world, local)
+
+
+if __name__ == "__main__":
+    main()

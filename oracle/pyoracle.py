@@ -1,0 +1,145 @@
+"""numpy front end of the C oracle (oracle/v7_oracle.c) -- TEST INFRASTRUCTURE ONLY.
+
+Used as the parity checker by tests/, __graft_entry__.smoke() and the CPU
+baseline of bench.py.  ``ensure_built()`` compiles the library with the recipe
+in oracle/Makefile when it is missing.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from ctypes import POINTER, c_double, c_float, c_int, c_int64, c_void_p
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB = HERE / "_build" / "libv7_oracle.so"
+ABI_SHIM = HERE / "_build" / "libv7_oracle_abi.so"
+REF_DIR = HERE / "_ref"
+
+
+def ensure_built() -> None:
+    if not LIB.exists() or not ABI_SHIM.exists():
+        subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+
+
+def _ptr(a: np.ndarray) -> c_void_p:
+    assert a.flags["C_CONTIGUOUS"]
+    return c_void_p(a.ctypes.data)
+
+
+class Oracle:
+    """Thin typed wrapper; every method allocates and returns its outputs."""
+
+    def __init__(self, nthreads: int | None = None):
+        ensure_built()
+        self.lib = ctypes.CDLL(str(LIB))
+        self.nthreads = nthreads or max(1, os.cpu_count() or 1)
+        L = self.lib
+        sig = {
+            "orc_rmsnorm_rows": [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_float, c_int],
+            "orc_fused_add_rmsnorm_rows": [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_float, c_int],
+            "orc_rmsnorm_rope_rows": [c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int64, c_int,
+                                      c_float, c_int],
+            "orc_swiglu": [c_void_p, c_void_p, c_void_p, c_int64, c_int],
+            "orc_quantize_rows": [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int],
+            "orc_swiglu_q8_rows": [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int],
+            "orc_add_inplace": [c_void_p, c_void_p, c_int64, c_int],
+            "orc_rmsnorm_quantize_rows": [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_float, c_int],
+            "orc_rope_tables": [c_void_p, c_void_p, c_int64, c_int, c_int, c_double],
+        }
+        for name, args in sig.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = c_int
+        L.orc_sigmoid.argtypes = [c_float]
+        L.orc_sigmoid.restype = c_float
+
+    @staticmethod
+    def _ok(rc: int, what: str) -> None:
+        if rc != 0:
+            raise ValueError(f"oracle {what}: contract violation")
+
+    def rmsnorm(self, x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32)
+        rows, n = x.reshape(-1, x.shape[-1]).shape
+        o = np.empty_like(x)
+        self._ok(self.lib.orc_rmsnorm_rows(_ptr(o), _ptr(x), _ptr(np.ascontiguousarray(w, np.float32)), rows, n, eps,
+                                           self.nthreads), "rmsnorm")
+        return o
+
+    def fused_add_rmsnorm(self, r: np.ndarray, a: np.ndarray, w: np.ndarray, eps: float):
+        """Returns (out, residual after the in-place add)."""
+        r = np.array(r, np.float32, copy=True, order="C")
+        a = np.ascontiguousarray(a, np.float32)
+        rows, n = r.reshape(-1, r.shape[-1]).shape
+        o = np.empty_like(r)
+        self._ok(self.lib.orc_fused_add_rmsnorm_rows(_ptr(o), _ptr(r), _ptr(a), _ptr(np.ascontiguousarray(w, np.float32)),
+                                                     rows, n, eps, self.nthreads), "fused_add_rmsnorm")
+        return o, r
+
+    def rope(self, buf: np.ndarray, w: np.ndarray, cos: np.ndarray, sin: np.ndarray, pos0: int, eps: float,
+             rope_max_dim: int | None = None) -> np.ndarray:
+        """buf [tokens, heads, head_dim]; cos/sin flat tables with rows of
+        rope_max_dim (default: the last dimension of cos)."""
+        out = np.array(buf, np.float32, copy=True, order="C")
+        tokens, heads, hd = out.shape
+        cos = np.ascontiguousarray(cos, np.float32)
+        sin = np.ascontiguousarray(sin, np.float32)
+        rmd = rope_max_dim if rope_max_dim is not None else cos.shape[-1]
+        self._ok(self.lib.orc_rmsnorm_rope_rows(_ptr(out), tokens, heads, hd, _ptr(np.ascontiguousarray(w, np.float32)),
+                                                _ptr(cos), _ptr(sin), pos0, rmd, eps, self.nthreads), "rope")
+        return out
+
+    def sigmoid(self, g: float) -> float:
+        return float(self.lib.orc_sigmoid(g))
+
+    def swiglu(self, g: np.ndarray, u: np.ndarray) -> np.ndarray:
+        g = np.ascontiguousarray(g, np.float32)
+        u = np.ascontiguousarray(u, np.float32)
+        o = np.empty_like(g)
+        self._ok(self.lib.orc_swiglu(_ptr(o), _ptr(g), _ptr(u), g.size, self.nthreads), "swiglu")
+        return o
+
+    def quantize(self, x: np.ndarray):
+        """Per-row Q8 of x [rows, n] -> (codes int8 [rows, n], scales [rows, ceil(n/64)])."""
+        x = np.ascontiguousarray(x, np.float32)
+        x2 = x.reshape(-1, x.shape[-1])
+        rows, n = x2.shape
+        q = np.empty((rows, n), np.int8)
+        s = np.empty((rows, (n + 63) // 64), np.float32)
+        self._ok(self.lib.orc_quantize_rows(_ptr(q), _ptr(s), _ptr(x2), rows, n, self.nthreads), "quantize")
+        return q, s
+
+    def swiglu_q8(self, g: np.ndarray, u: np.ndarray):
+        g = np.ascontiguousarray(g, np.float32)
+        u = np.ascontiguousarray(u, np.float32)
+        rows, n = g.reshape(-1, g.shape[-1]).shape
+        q = np.empty((rows, n), np.int8)
+        s = np.empty((rows, n // 64), np.float32)
+        self._ok(self.lib.orc_swiglu_q8_rows(_ptr(q), _ptr(s), _ptr(g), _ptr(u), rows, n, self.nthreads), "swiglu_q8")
+        return q, s
+
+    def add_inplace(self, x: np.ndarray, y: np.ndarray) -> np.ndarray:
+        out = np.array(x, np.float32, copy=True, order="C")
+        self._ok(self.lib.orc_add_inplace(_ptr(out), _ptr(np.ascontiguousarray(y, np.float32)), out.size,
+                                          self.nthreads), "add_inplace")
+        return out
+
+    def rmsnorm_quantize(self, x: np.ndarray, w: np.ndarray, eps: float):
+        x = np.ascontiguousarray(x, np.float32)
+        rows, n = x.reshape(-1, x.shape[-1]).shape
+        q = np.empty((rows, n), np.int8)
+        s = np.empty((rows, n // 64), np.float32)
+        self._ok(self.lib.orc_rmsnorm_quantize_rows(_ptr(q), _ptr(s), _ptr(x), _ptr(np.ascontiguousarray(w, np.float32)),
+                                                    rows, n, eps, self.nthreads), "rmsnorm_quantize")
+        return q, s
+
+    def rope_tables(self, positions: int, half: int, stride: int | None = None, base: float = 1e6):
+        stride = stride or half
+        c = np.empty((positions, stride), np.float32)
+        s = np.empty((positions, stride), np.float32)
+        self._ok(self.lib.orc_rope_tables(_ptr(c), _ptr(s), positions, half, stride, base), "rope_tables")
+        return c, s

@@ -1,0 +1,56 @@
+"""The reference's own validators and loadtests, unchanged, against this
+library on a B200.
+
+oracle/ref.mk compiles tools/v_{rmsnorm,add_inplace,quantize}_validate.cpp and
+tools/b_*_loadtest.cpp from the reference's sources into oracle/_ref/ (they
+travel to the GPU box as binaries).  Each loads libv7_threading.so through the
+reference's loader (dlopen + 99 dlsym, ms_abi calls) and drives the hot-path
+exports with host pointers: the drop-in proof.  Skipped where the binaries
+were not built (no reference tree at build time).
+"""
+from __future__ import annotations
+
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+ROOT = Path(__file__).resolve().parent.parent
+REF = ROOT / "oracle" / "_ref"
+
+
+def ref_bin(name: str) -> Path:
+    p = REF / name
+    if not p.exists():
+        pytest.skip(f"{p} not built (make -C oracle ref)")
+    return p
+
+
+@pytest.fixture(scope="module")
+def db(tmp_path_factory):
+    p = tmp_path_factory.mktemp("db") / "v7g.db"
+    p.write_bytes(b"not a v7 microdb: the kernels need no key from it\n")
+    return p
+
+
+@pytest.mark.parametrize("validator,expect", [("v_rmsnorm_validate", 94), ("v_add_inplace_validate", 14),
+                                               ("v_quantize_validate", 126)])
+def test_reference_validator(cuda, native_lib_path, db, validator, expect):
+    r = subprocess.run([str(ref_bin(validator)), str(native_lib_path), "--db", str(db)], capture_output=True, text=True,
+                       timeout=600)
+    tail = r.stdout[-2000:]
+    assert r.returncode == 0, tail
+    m = re.search(r"(\d+) passed, (\d+) failed", r.stdout)
+    assert m and int(m.group(1)) == expect and int(m.group(2)) == 0, tail
+
+
+@pytest.mark.parametrize("args", [["b_rmsnorm_loadtest", "2048"], ["b_fused_add_rmsnorm_loadtest", "2048"],
+                                  ["b_add_inplace_loadtest", "2048"], ["b_rmsnorm_rope_loadtest", "16", "128", "7", "128"]])
+def test_reference_loadtest(cuda, native_lib_path, db, args):
+    exe = ref_bin(args[0])
+    r = subprocess.run([str(exe), str(native_lib_path), *args[1:], "--db", str(db), "--iterations", "200"],
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    assert "Pass:" in r.stdout and "us / call" in r.stdout, r.stdout

@@ -1,0 +1,569 @@
+// abi.cpp -- the reference's export surface (include/v7_threading.h) on top of
+// the batched device kernels.
+//
+// The reference's loader (src/v7_lib.h:585-739) resolves 99 names and calls
+// them with the Microsoft x64 convention.  The hot-path entries here take one
+// vector (or one token) per call, like the reference, and accept host or
+// device memory for every pointer independently:
+//   - a device (or managed) pointer is handed to the kernel as is;
+//   - a host pointer is staged through a per-device workspace: inputs copied
+//     in, outputs copied back before the call returns.
+// Each call runs on a library-owned stream and returns with its results in
+// place (the reference's calls are synchronous).  A contract violation or a
+// CUDA failure marks the engine dead with a reason (v7_engine_is_dead /
+// v7_get_death_reason, src/v7_lib.h:179-184) and leaves the outputs unwritten,
+// where the reference would FATAL (engine_landing.inc:150) or silently
+// mis-size (rmsnorm_kernel.inc:15-19).
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "../../include/v7_threading.h"
+#include "../../include/v7g.h"
+
+extern "C" float *v7g_rms_eps_slot(void);
+
+unsigned long long v7g_zero_block[16];
+int enable_token_dump = 0;
+int enable_dump = 0;
+// The reference sets this from its CPUID probe; this library needs no CPU
+// feature, so it is 1.  A CUDA device is checked on the first kernel call.
+int cpu_features_ok = 1;
+
+namespace {
+
+std::mutex g_mutex; // serialises the reference-ABI entries (shared workspace)
+int g_dead = 0;
+char g_reason[512] = "";
+
+void die(const char *fmt, ...)
+{
+	va_list ap;
+	va_start(ap, fmt);
+	vsnprintf(g_reason, sizeof(g_reason), fmt, ap);
+	va_end(ap);
+	g_dead = 1;
+}
+
+// ---- per-device stream and staging workspace ------------------------------
+struct DeviceCtx {
+	cudaStream_t stream = nullptr;
+	char *work = nullptr;
+	size_t work_bytes = 0;
+};
+constexpr int kMaxDevices = 64;
+DeviceCtx g_ctx[kMaxDevices];
+
+int ensure_ctx(int dev, size_t bytes, DeviceCtx **out)
+{
+	if (dev < 0 || dev >= kMaxDevices)
+		return -1;
+	DeviceCtx &c = g_ctx[dev];
+	if (!c.stream && cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking) != cudaSuccess)
+		return -1;
+	if (bytes > c.work_bytes) {
+		if (c.work)
+			cudaFree(c.work);
+		c.work = nullptr;
+		c.work_bytes = 0;
+		size_t want = bytes < (1u << 20) ? (1u << 20) : bytes + bytes / 4;
+		if (cudaMalloc(&c.work, want) != cudaSuccess) {
+			cudaGetLastError();
+			return -1;
+		}
+		c.work_bytes = want;
+	}
+	*out = &c;
+	return 0;
+}
+
+// Classifies a pointer: 1 = device/managed memory (sets *dev), 0 = host.
+int pointer_device(const void *p, int *dev)
+{
+	cudaPointerAttributes a;
+	if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+		cudaGetLastError(); // plain host memory on old runtimes reports an error
+		return 0;
+	}
+	if (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) {
+		*dev = a.device;
+		return 1;
+	}
+	return 0;
+}
+
+// Maps every argument of one call to device memory.
+class Stager {
+  public:
+	struct Arg {
+		void *user;
+		size_t bytes;
+		bool in, out, host;
+		size_t offset; // into the workspace, for host arguments
+		int alias;     // index of an earlier identical host argument, or -1
+	};
+
+	int add(void *p, size_t bytes, bool in, bool out)
+	{
+		Arg a{p, bytes, in, out, true, 0, -1};
+		int dev = -1;
+		if (p && pointer_device(p, &dev)) {
+			a.host = false;
+			if (device_ < 0)
+				device_ = dev;
+			else if (device_ != dev)
+				mixed_ = true;
+		}
+		if (a.host)
+			for (size_t i = 0; i < args_.size(); ++i)
+				if (args_[i].host && args_[i].user == p && args_[i].bytes == bytes) {
+					a.alias = (int)i;
+					args_[i].in = args_[i].in || in;
+					args_[i].out = args_[i].out || out;
+				}
+		args_.push_back(a);
+		return (int)args_.size() - 1;
+	}
+
+	// Selects the device, reserves the workspace and uploads host inputs.
+	bool begin(const char *what)
+	{
+		what_ = what;
+		if (mixed_) {
+			die("%s: pointers on different CUDA devices", what);
+			return false;
+		}
+		if (device_ < 0 && cudaGetDevice(&device_) != cudaSuccess) {
+			cudaGetLastError();
+			die("%s: no CUDA device", what);
+			return false;
+		}
+		if (cudaSetDevice(device_) != cudaSuccess) {
+			cudaGetLastError();
+			die("%s: cannot select CUDA device %d", what, device_);
+			return false;
+		}
+		size_t total = 0;
+		for (Arg &a : args_)
+			if (a.host && a.alias < 0) {
+				a.offset = total;
+				total += (a.bytes + 255) & ~(size_t)255;
+			}
+		if (ensure_ctx(device_, total, &ctx_) != 0) {
+			die("%s: cannot allocate a %zu-byte staging workspace on device %d", what, total, device_);
+			return false;
+		}
+		for (Arg &a : args_)
+			if (a.host && a.alias < 0 && a.in && a.bytes)
+				if (cudaMemcpyAsync(ctx_->work + a.offset, a.user, a.bytes, cudaMemcpyHostToDevice, ctx_->stream) != cudaSuccess)
+					return fail("host-to-device copy");
+		return true;
+	}
+
+	void *dev(int i) const
+	{
+		const Arg &a = args_[i];
+		if (!a.host)
+			return a.user;
+		const Arg &b = a.alias >= 0 ? args_[a.alias] : a;
+		return ctx_->work + b.offset;
+	}
+
+	cudaStream_t stream() const { return ctx_->stream; }
+
+	// Checks the kernel status, copies host outputs back and waits.
+	bool end(int rc)
+	{
+		if (rc != V7G_OK) {
+			cudaStreamSynchronize(ctx_->stream);
+			die("%s: %s", what_, v7g_last_error());
+			return false;
+		}
+		for (const Arg &a : args_)
+			if (a.host && a.alias < 0 && a.out && a.bytes)
+				if (cudaMemcpyAsync(a.user, ctx_->work + a.offset, a.bytes, cudaMemcpyDeviceToHost, ctx_->stream) != cudaSuccess)
+					return fail("device-to-host copy");
+		if (cudaStreamSynchronize(ctx_->stream) != cudaSuccess)
+			return fail("stream synchronisation");
+		return true;
+	}
+
+  private:
+	bool fail(const char *step)
+	{
+		cudaError_t e = cudaGetLastError();
+		die("%s: %s failed: %s", what_, step, cudaGetErrorString(e));
+		return false;
+	}
+
+	std::vector<Arg> args_;
+	int device_ = -1;
+	bool mixed_ = false;
+	DeviceCtx *ctx_ = nullptr;
+	const char *what_ = "";
+};
+
+// ---- key store (the reference's MicroDB surface, reduced to a map) ---------
+std::unordered_map<std::string, std::vector<unsigned char>> g_store;
+int g_readonly = 0;
+const char *kEpsKey = "__sys_rms_eps";
+const char kDbMagic[8] = {'V', '7', 'G', 'D', 'B', '0', '0', '1'};
+
+int store_add(const char *key, const void *data, unsigned long long len)
+{
+	if (!key || (!data && len))
+		return 0;
+	if (strcmp(key, kEpsKey) == 0) {
+		if (len != sizeof(float))
+			return 0;
+		memcpy(v7g_rms_eps_slot(), data, sizeof(float));
+		return 1;
+	}
+	if (g_readonly)
+		return 0;
+	const unsigned char *d = static_cast<const unsigned char *>(data);
+	g_store[key].assign(d, d + len);
+	return 1;
+}
+
+void *store_find(const char *key, unsigned long long *out_len)
+{
+	if (!key)
+		return nullptr;
+	if (strcmp(key, kEpsKey) == 0) {
+		if (out_len)
+			*out_len = sizeof(float);
+		return v7g_rms_eps_slot();
+	}
+	auto it = g_store.find(key);
+	if (it == g_store.end())
+		return nullptr;
+	if (out_len)
+		*out_len = it->second.size();
+	return it->second.empty() ? (void *)v7g_zero_block : it->second.data();
+}
+
+int store_save(const char *path)
+{
+	if (!path)
+		return 0;
+	FILE *f = fopen(path, "wb");
+	if (!f)
+		return 0;
+	bool ok = fwrite(kDbMagic, 1, 8, f) == 8;
+	float eps = *v7g_rms_eps_slot();
+	auto put = [&](const std::string &k, const void *d, unsigned long long n) {
+		unsigned int kl = (unsigned int)k.size();
+		ok = ok && fwrite(&kl, 4, 1, f) == 1 && fwrite(k.data(), 1, kl, f) == kl && fwrite(&n, 8, 1, f) == 1 && (n == 0 || fwrite(d, 1, n, f) == n);
+	};
+	put(kEpsKey, &eps, sizeof(float));
+	for (const auto &kv : g_store)
+		put(kv.first, kv.second.data(), kv.second.size());
+	ok = (fclose(f) == 0) && ok;
+	return ok ? 1 : 0;
+}
+
+// Returns 1 on success, 0 when the file is missing, -1 when it is not a
+// store written by store_save.
+int store_load(const char *path)
+{
+	FILE *f = path ? fopen(path, "rb") : nullptr;
+	if (!f)
+		return 0;
+	char magic[8];
+	if (fread(magic, 1, 8, f) != 8 || memcmp(magic, kDbMagic, 8) != 0) {
+		fclose(f);
+		return -1;
+	}
+	std::unordered_map<std::string, std::vector<unsigned char>> loaded;
+	float eps = *v7g_rms_eps_slot();
+	bool ok = true;
+	for (;;) {
+		unsigned int kl;
+		if (fread(&kl, 4, 1, f) != 1)
+			break;
+		std::string k(kl, '\0');
+		unsigned long long n;
+		if (kl > (1u << 20) || fread(&k[0], 1, kl, f) != kl || fread(&n, 8, 1, f) != 1 || n > (1ull << 40)) {
+			ok = false;
+			break;
+		}
+		std::vector<unsigned char> d(n);
+		if (n && fread(d.data(), 1, n, f) != n) {
+			ok = false;
+			break;
+		}
+		if (k == kEpsKey && n == sizeof(float))
+			memcpy(&eps, d.data(), sizeof(float));
+		else
+			loaded[k] = std::move(d);
+	}
+	fclose(f);
+	if (!ok)
+		return -1;
+	g_store.swap(loaded);
+	*v7g_rms_eps_slot() = eps;
+	return 1;
+}
+
+} // namespace
+
+extern "C" {
+
+// ---- hot path --------------------------------------------------------------
+
+V7_ABI void v7s_rmsnorm(float *o, float *x, float *weight, int size)
+{
+	std::lock_guard<std::mutex> lock(g_mutex);
+	if (size <= 0 || size % 32 != 0) {
+		die("v7s_rmsnorm: size %d breaks the contract size > 0, size %% 32 == 0", size);
+		return;
+	}
+	const size_t b = (size_t)size * sizeof(float);
+	Stager s;
+	int io = s.add(o, b, false, true), ix = s.add(x, b, true, false), iw = s.add(weight, b, true, false);
+	if (!s.begin("v7s_rmsnorm"))
+		return;
+	s.end(v7g_rmsnorm_rows((float *)s.dev(io), (const float *)s.dev(ix), (const float *)s.dev(iw), 1, size, *v7g_rms_eps_slot(), s.stream()));
+}
+
+V7_ABI void v7s_add_inplace(float *x, float *y, int n)
+{
+	std::lock_guard<std::mutex> lock(g_mutex);
+	if (n <= 0 || n % 32 != 0) {
+		die("v7s_add_inplace: n %d breaks the contract n > 0, n %% 32 == 0", n);
+		return;
+	}
+	const size_t b = (size_t)n * sizeof(float);
+	Stager s;
+	int ix = s.add(x, b, true, true), iy = s.add(y, b, true, false);
+	if (!s.begin("v7s_add_inplace"))
+		return;
+	s.end(v7g_add_inplace((float *)s.dev(ix), (const float *)s.dev(iy), n, s.stream()));
+}
+
+V7_ABI void v7s_fused_add_rmsnorm(float *o, float *residual, float *add, float *weight, int dim)
+{
+	std::lock_guard<std::mutex> lock(g_mutex);
+	if (dim < 0 || dim % 8 != 0) {
+		die("v7s_fused_add_rmsnorm: dim %d breaks the contract dim %% 8 == 0", dim);
+		return;
+	}
+	if (dim == 0)
+		return;
+	const size_t b = (size_t)dim * sizeof(float);
+	Stager s;
+	int io = s.add(o, b, false, true), ir = s.add(residual, b, true, true), ia = s.add(add, b, true, false), iw = s.add(weight, b, true, false);
+	if (!s.begin("v7s_fused_add_rmsnorm"))
+		return;
+	s.end(v7g_fused_add_rmsnorm_rows((float *)s.dev(io), (float *)s.dev(ir), (const float *)s.dev(ia), (const float *)s.dev(iw), 1, dim, *v7g_rms_eps_slot(), s.stream()));
+}
+
+V7_ABI void v7s_rmsnorm_rope_heads(float *buf, int n_heads, int head_dim, float *norm_weight, float *cos_table, float *sin_table, int pos, int rope_max_dim)
+{
+	std::lock_guard<std::mutex> lock(g_mutex);
+	if (n_heads < 0 || head_dim < 32 || head_dim > 1024 || head_dim % 32 != 0 || pos < 0 || rope_max_dim < 0) {
+		die("v7s_rmsnorm_rope_heads: n_heads %d, head_dim %d, pos %d, rope_max_dim %d break the contract (head_dim %% 32 == 0, 32 <= head_dim <= 1024)", n_heads, head_dim, pos, rope_max_dim);
+		return;
+	}
+	if (n_heads == 0)
+		return;
+	const size_t hb = (size_t)head_dim * sizeof(float);
+	const size_t half_b = (size_t)(head_dim / 2) * sizeof(float);
+	Stager s;
+	int ib = s.add(buf, hb * (size_t)n_heads, true, true), iw = s.add(norm_weight, hb, true, false);
+	// The reference pre-offsets the tables to row pos (rmsnorm_rope_dispatch.inc:28-33)
+	// and reads head_dim/2 entries of it; only that row is staged.
+	int ic = -1, is = -1;
+	if (pos != 0) {
+		ic = s.add(cos_table + (size_t)pos * rope_max_dim, half_b, true, false);
+		is = s.add(sin_table + (size_t)pos * rope_max_dim, half_b, true, false);
+	}
+	if (!s.begin("v7s_rmsnorm_rope_heads"))
+		return;
+	// One token at position pos: the staged row is the table (row stride 0).
+	const float *c = ic >= 0 ? (const float *)s.dev(ic) : nullptr;
+	const float *sn = is >= 0 ? (const float *)s.dev(is) : nullptr;
+	s.end(v7g_rmsnorm_rope_rows((float *)s.dev(ib), nullptr, 1, n_heads, 0, head_dim, (const float *)s.dev(iw), nullptr, c, sn, pos, 0, *v7g_rms_eps_slot(), s.stream()));
+}
+
+V7_ABI void v7d_quantize(char *out_q, float *in_x, float *out_s, int n)
+{
+	std::lock_guard<std::mutex> lock(g_mutex);
+	if (n < 0) {
+		die("v7d_quantize: n %d < 0", n);
+		return;
+	}
+	if (n == 0)
+		return;
+	const size_t groups = ((size_t)n + 63) / 64;
+	Stager s;
+	int iq = s.add(out_q, (size_t)n, false, true), ix = s.add(in_x, (size_t)n * sizeof(float), true, false), is = s.add(out_s, groups * sizeof(float), false, true);
+	if (!s.begin("v7d_quantize"))
+		return;
+	s.end(v7g_quantize_rows((int8_t *)s.dev(iq), (float *)s.dev(is), (const float *)s.dev(ix), 1, n, s.stream()));
+}
+
+V7_ABI void v7s_rmsnorm_quantize(char *out_q, float *in_x, float *out_s, int n, float *weight)
+{
+	std::lock_guard<std::mutex> lock(g_mutex);
+	if (n <= 0 || n % 64 != 0) {
+		die("v7s_rmsnorm_quantize: n %d breaks the contract n > 0, n %% 64 == 0", n);
+		return;
+	}
+	const size_t b = (size_t)n * sizeof(float);
+	Stager s;
+	int iq = s.add(out_q, (size_t)n, false, true), ix = s.add(in_x, b, true, false), is = s.add(out_s, (size_t)(n / 64) * sizeof(float), false, true), iw = s.add(weight, b, true, false);
+	if (!s.begin("v7s_rmsnorm_quantize"))
+		return;
+	s.end(v7g_rmsnorm_quantize_rows((int8_t *)s.dev(iq), (float *)s.dev(is), (const float *)s.dev(ix), (const float *)s.dev(iw), 1, n, *v7g_rms_eps_slot(), s.stream()));
+}
+
+// ---- runtime surface ---------------------------------------------------------
+
+V7_ABI int v7_init(const char *db_path)
+{
+	std::lock_guard<std::mutex> lock(g_mutex);
+	g_dead = 0;
+	g_reason[0] = 0;
+	if (!db_path) {
+		g_store.clear();
+		return 1;
+	}
+	int rc = store_load(db_path);
+	if (rc == 0) {
+		die("v7_init: cannot open %s", db_path);
+		return 0;
+	}
+	if (rc < 0)
+		g_store.clear(); // a foreign database: the kernels need none of its keys
+	return 1;
+}
+
+V7_ABI int v7_db_load(const char *path)
+{
+	std::lock_guard<std::mutex> lock(g_mutex);
+	return store_load(path) == 1 ? 1 : 0;
+}
+V7_ABI int v7_db_save(const char *path)
+{
+	std::lock_guard<std::mutex> lock(g_mutex);
+	return store_save(path);
+}
+V7_ABI int db_load(const char *filename) { return v7_db_load(filename); }
+V7_ABI int db_save(const char *filename) { return v7_db_save(filename); }
+V7_ABI int ht_add(const char *key, void *data, unsigned long long data_len, unsigned int persist)
+{
+	std::lock_guard<std::mutex> lock(g_mutex);
+	return store_add(key, data, data_len);
+}
+V7_ABI void *ht_find(const char *key, unsigned long long *out_len)
+{
+	std::lock_guard<std::mutex> lock(g_mutex);
+	return store_find(key, out_len);
+}
+V7_ABI int v7_db_add(const char *key, const void *data, int len, unsigned int persist)
+{
+	if (len < 0)
+		return 0;
+	return ht_add(key, const_cast<void *>(data), (unsigned long long)len, persist);
+}
+V7_ABI void *v7_db_find(const char *key, unsigned long long *out_len) { return ht_find(key, out_len); }
+V7_ABI void ht_init(void)
+{
+	std::lock_guard<std::mutex> lock(g_mutex);
+	g_store.clear();
+}
+V7_ABI void ht_destroy(void) { ht_init(); }
+V7_ABI void db_set_readonly(int flag) { g_readonly = flag != 0; }
+
+V7_ABI int v7_engine_is_dead(void) { return g_dead; }
+V7_ABI const char *v7_get_death_reason(void) { return g_reason; }
+V7_ABI const char *v7_get_version(void) { return v7g_version(); }
+V7_ABI int v7_get_console_width(void) { return 80; }
+V7_ABI void v7_do_fatal(const char *message)
+{
+	std::lock_guard<std::mutex> lock(g_mutex);
+	die("%s", message ? message : "v7_do_fatal");
+}
+
+// The reference builds internal RoPE tables here for its fused QKV matmul,
+// which this library does not provide; the kernels here take caller tables.
+V7_ABI void v7s_rope_init(int head_dim, float rope_base) {}
+V7_ABI void v7s_set_fused_rope(int pos, int head_dim) {}
+// Worker spin policy of the CPU pool: nothing spins on the GPU path.
+V7_ABI void v7s_set_spin(int flag) {}
+V7_ABI void v7s_enable_thinking(int on) {}
+V7_ABI unsigned long long get_config_was_fixed(void) { return 0; }
+
+// Parallel workers: the streaming multiprocessors of the current device.
+V7_ABI int v7s_get_num_workers(void)
+{
+	int dev = 0, sms = 0;
+	if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+		cudaGetLastError();
+		return 0;
+	}
+	return sms;
+}
+
+// Releases the per-device streams and staging workspaces.
+V7_ABI void v7s_shutdown(void)
+{
+	std::lock_guard<std::mutex> lock(g_mutex);
+	int cur = -1;
+	cudaGetDevice(&cur);
+	for (int d = 0; d < kMaxDevices; ++d) {
+		DeviceCtx &c = g_ctx[d];
+		if (!c.stream && !c.work)
+			continue;
+		cudaSetDevice(d);
+		if (c.stream)
+			cudaStreamSynchronize(c.stream);
+		if (c.work)
+			cudaFree(c.work);
+		if (c.stream)
+			cudaStreamDestroy(c.stream);
+		c = DeviceCtx();
+	}
+	if (cur >= 0)
+		cudaSetDevice(cur);
+	cudaGetLastError();
+}
+V7_ABI void v7_shutdown(void) { v7s_shutdown(); }
+
+// Console formatting belongs to the reference's runtime, not to this library.
+V7_ABI int v7sprintf(char *buffer, int buf_size, const char *format, ...)
+{
+	if (buffer && buf_size > 0)
+		buffer[0] = 0;
+	std::lock_guard<std::mutex> lock(g_mutex);
+	die("v7sprintf: not provided by v7g");
+	return 0;
+}
+
+// ---- everything outside the kernel path ------------------------------------
+
+#define V7G_DEFINE_VOID(name, params)                   \
+	V7_ABI void name params                             \
+	{                                                   \
+		std::lock_guard<std::mutex> lock(g_mutex);      \
+		die(#name ": not provided by v7g");             \
+	}
+#define V7G_DEFINE_RET(type, name, params, value)       \
+	V7_ABI type name params                             \
+	{                                                   \
+		std::lock_guard<std::mutex> lock(g_mutex);      \
+		die(#name ": not provided by v7g");             \
+		return (type)(value);                           \
+	}
+V7G_STUBS_VOID(V7G_DEFINE_VOID)
+V7G_STUBS_RET(V7G_DEFINE_RET)
+
+} // extern "C"

@@ -1,0 +1,191 @@
+// swiglu.cu -- elementwise SwiGLU, SwiGLU -> Q8 and Q8 quantisation.
+//
+// All three stream activations once through registers (HBM-bound, no tensor
+// cores: a handful of FLOPs per 8-12 bytes).  The Q8 kernels treat a tensor
+// whose rows are a multiple of 64 long as a flat sequence of 64-element
+// groups -- codes [rows, n] and scales [rows, n/64] are then simply group g at
+// byte 64g and scale slot g -- and give each group to a half-warp: lane L of
+// the half holds elements 4L..4L+3 as one float4 (16-byte loads, one 4-byte
+// code store per lane).  Rows of other lengths (and unaligned pointers) go
+// through a general kernel, one warp per group, that also implements the
+// reference's trailing-group rule.
+#include "internal.h"
+#include "q8.cuh"
+
+namespace v7g {
+namespace {
+
+constexpr int kBlock = 256;
+
+__device__ __forceinline__ float4 swiglu4(float4 g, float4 u)
+{
+	return make_float4(v7_swiglu(g.x, u.x), v7_swiglu(g.y, u.y), v7_swiglu(g.z, u.z), v7_swiglu(g.w, u.w));
+}
+
+// --- A5  elementwise SwiGLU ---------------------------------------------
+// VEC: float4 body over count/4 vectors, the (< 4) trailing elements by the
+// first threads of block 0.
+template <bool VEC>
+__global__ void __launch_bounds__(kBlock) k_swiglu(float *out, const float *gate, const float *up, int64_t count)
+{
+	const int64_t tid = (int64_t)blockIdx.x * kBlock + threadIdx.x;
+	const int64_t nthreads = (int64_t)gridDim.x * kBlock;
+	if (VEC) {
+		const int64_t n4 = count >> 2;
+		const float4 *g4 = reinterpret_cast<const float4 *>(gate);
+		const float4 *u4 = reinterpret_cast<const float4 *>(up);
+		float4 *o4 = reinterpret_cast<float4 *>(out);
+		for (int64_t i = tid; i < n4; i += nthreads)
+			st_stream4(o4 + i, swiglu4(ld_stream4(g4 + i), ld_stream4(u4 + i)));
+		const int64_t t = (n4 << 2) + tid;
+		if (tid < (count & 3))
+			out[t] = v7_swiglu(gate[t], up[t]);
+	} else {
+		for (int64_t i = tid; i < count; i += nthreads)
+			out[i] = v7_swiglu(gate[i], up[i]);
+	}
+}
+
+// --- A6 / A8  Q8 over flat 64-element groups (n % 64 == 0, 16-byte aligned) ---
+// One pair of groups per warp iteration; SWIGLU computes h = swiglu(a, b) in
+// registers first (A8), otherwise h = a (A6).
+template <bool SWIGLU>
+__global__ void __launch_bounds__(kBlock) k_q8_groups(uint32_t *codes, float *scales, const float4 *a, const float4 *b, int64_t ngroups)
+{
+	const int lane = threadIdx.x & 31;
+	const int half = lane >> 4;
+	const int hl = lane & 15;
+	const int64_t nwarps = ((int64_t)gridDim.x * kBlock) >> 5;
+	for (int64_t pair = ((int64_t)blockIdx.x * kBlock + threadIdx.x) >> 5; 2 * pair < ngroups; pair += nwarps) {
+		const int64_t g = 2 * pair + half;
+		const bool valid = g < ngroups;
+		const int64_t i4 = g * 16 + hl;
+		float4 h = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+		if (valid) {
+			if (SWIGLU)
+				h = swiglu4(ld_stream4(a + i4), ld_stream4(b + i4));
+			else
+				h = ld_stream4(a + i4);
+		}
+		float scale, recip;
+		q8_scale(group_absmax_f4(h, lane), scale, recip);
+		if (valid) {
+			__stcs(codes + i4, q8_codes4(h, recip));
+			if (hl == 0)
+				__stcs(scales + g, scale);
+		}
+	}
+}
+
+// --- general Q8: any row length, any alignment -----------------------------
+// One warp per group (row r, group j); lane l holds elements 64j + l and
+// 64j + 32 + l of the row.  A full group follows the vector path's MAXPS tree;
+// a trailing group of fewer than 64 elements follows the scalar tail path
+// (quantize_kernel.inc:119-152).
+template <bool SWIGLU>
+__global__ void __launch_bounds__(kBlock) k_q8_general(int8_t *codes, float *scales, const float *a, const float *b, int64_t rows, int n)
+{
+	using M = F<true>;
+	const int lane = threadIdx.x & 31;
+	const int64_t nwarps = ((int64_t)gridDim.x * kBlock) >> 5;
+	const int groups_per_row = (n + kQ8Group - 1) / kQ8Group;
+	const int64_t total = rows * groups_per_row;
+	for (int64_t gi = ((int64_t)blockIdx.x * kBlock + threadIdx.x) >> 5; gi < total; gi += nwarps) {
+		const int64_t row = gi / groups_per_row;
+		const int j = (int)(gi - row * groups_per_row);
+		const int r = min(kQ8Group, n - kQ8Group * j);
+		const int64_t base = row * n + (int64_t)kQ8Group * j;
+		const bool v0 = lane < r, v1 = lane + 32 < r;
+		float h0 = 0.0f, h1 = 0.0f;
+		if (v0)
+			h0 = SWIGLU ? v7_swiglu(a[base + lane], b[base + lane]) : a[base + lane];
+		if (v1)
+			h1 = SWIGLU ? v7_swiglu(a[base + 32 + lane], b[base + 32 + lane]) : a[base + 32 + lane];
+		float scale, recip;
+		if (r == kQ8Group) {
+			q8_scale(group_absmax_w2(h0, h1, lane), scale, recip);
+			codes[base + lane] = (int8_t)(q8_code_bits(M::mul(h0, recip)) & 0xffu);
+			codes[base + 32 + lane] = (int8_t)(q8_code_bits(M::mul(h1, recip)) & 0xffu);
+		} else {
+			q8_scale(tail_absmax_w2(h0, v0, h1, v1), scale, recip);
+			if (v0)
+				codes[base + lane] = (int8_t)(q8_tail_code_bits(M::mul(h0, recip)) & 0xffu);
+			if (v1)
+				codes[base + 32 + lane] = (int8_t)(q8_tail_code_bits(M::mul(h1, recip)) & 0xffu);
+		}
+		if (lane == 0)
+			scales[gi] = scale;
+	}
+}
+
+template <typename Kernel, typename... Args>
+int launch_persistent(Kernel kernel, const char *what, int64_t work_blocks, void *stream, Args... args)
+{
+	DeviceInfo dev;
+	int rc = current_device(&dev);
+	if (rc != V7G_OK)
+		return rc;
+	const int grid = resident_grid((const void *)kernel, kBlock, 0, work_blocks, dev);
+	kernel<<<grid, kBlock, 0, (cudaStream_t)stream>>>(args...);
+	return check_launch(what);
+}
+
+int q8_rows(const char *what, int8_t *codes, float *scales, const float *a, const float *b, int64_t rows, int n, void *stream, bool swiglu)
+{
+	if (rows < 0 || n <= 0)
+		return set_error(V7G_ERR_ARG, "%s: rows = %lld, n = %d: need rows >= 0 and n > 0", what, (long long)rows, n);
+	if (rows == 0)
+		return clear_error();
+	if (!codes || !scales || !a || (swiglu && !b))
+		return set_error(V7G_ERR_ARG, "%s: NULL pointer", what);
+	const bool flat = n % kQ8Group == 0 && aligned16(codes) && aligned16(a) && (!swiglu || aligned16(b));
+	if (flat) {
+		const int64_t ngroups = rows * (n / kQ8Group);
+		const int64_t warps = (ngroups + 1) / 2;
+		const int64_t blocks = (warps + kBlock / 32 - 1) / (kBlock / 32);
+		if (swiglu)
+			return launch_persistent(k_q8_groups<true>, what, blocks, stream, reinterpret_cast<uint32_t *>(codes), scales, reinterpret_cast<const float4 *>(a), reinterpret_cast<const float4 *>(b), ngroups);
+		return launch_persistent(k_q8_groups<false>, what, blocks, stream, reinterpret_cast<uint32_t *>(codes), scales, reinterpret_cast<const float4 *>(a), reinterpret_cast<const float4 *>(b), ngroups);
+	}
+	const int64_t total = rows * ((n + kQ8Group - 1) / kQ8Group);
+	const int64_t blocks = (total + kBlock / 32 - 1) / (kBlock / 32);
+	if (swiglu)
+		return launch_persistent(k_q8_general<true>, what, blocks, stream, codes, scales, a, b, rows, n);
+	return launch_persistent(k_q8_general<false>, what, blocks, stream, codes, scales, a, b, rows, n);
+}
+
+} // namespace
+} // namespace v7g
+
+using namespace v7g;
+
+extern "C" {
+
+int v7g_swiglu(float *out, const float *gate, const float *up, int64_t count, void *stream)
+{
+	if (count < 0)
+		return set_error(V7G_ERR_ARG, "v7g_swiglu: count = %lld < 0", (long long)count);
+	if (count == 0)
+		return clear_error();
+	if (!out || !gate || !up)
+		return set_error(V7G_ERR_ARG, "v7g_swiglu: NULL pointer");
+	if (aligned16(out) && aligned16(gate) && aligned16(up)) {
+		const int64_t blocks = ((count >> 2) + kBlock - 1) / kBlock;
+		return launch_persistent(k_swiglu<true>, "v7g_swiglu", blocks < 1 ? 1 : blocks, stream, out, gate, up, count);
+	}
+	return launch_persistent(k_swiglu<false>, "v7g_swiglu", (count + kBlock - 1) / kBlock, stream, out, gate, up, count);
+}
+
+int v7g_swiglu_q8_rows(int8_t *codes, float *scales, const float *gate, const float *up, int64_t rows, int n, void *stream)
+{
+	if (n <= 0 || n % kQ8Group != 0)
+		return set_error(V7G_ERR_ARG, "v7g_swiglu_q8_rows: n = %d must be a positive multiple of 64", n);
+	return q8_rows("v7g_swiglu_q8_rows", codes, scales, gate, up, rows, n, stream, true);
+}
+
+int v7g_quantize_rows(int8_t *codes, float *scales, const float *x, int64_t rows, int n, void *stream)
+{
+	return q8_rows("v7g_quantize_rows", codes, scales, x, nullptr, rows, n, stream, false);
+}
+
+} // extern "C"
