@@ -137,20 +137,29 @@ def shard(rows: int, rank: int, world: int) -> tuple[int, int]:
     return rows * rank // world, rows * (rank + 1) // world
 
 
-def max_over_ranks(x: float, world: int) -> float:
+def max_over_ranks(x: float, world: int, device: str = "cuda") -> float:
     if world == 1:
         return x
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    t = torch.tensor([x], dtype=torch.float64, device=device)
     torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     return float(t.item())
 
 
-def sum_over_ranks(x: float, world: int) -> float:
+def sum_over_ranks(x: float, world: int, device: str = "cuda") -> float:
     if world == 1:
         return x
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    t = torch.tensor([x], dtype=torch.float64, device=device)
     torch.distributed.all_reduce(t)
     return float(t.item())
+
+
+def gather_checksums(chk: torch.Tensor, world: int) -> list:
+    """Per-rank output checksums to every rank (verification only, after timing)."""
+    if world == 1:
+        return [chk.cpu().tolist()]
+    gathered = [torch.empty_like(chk) for _ in range(world)]
+    torch.distributed.all_gather(gathered, chk)
+    return torch.stack(gathered).cpu().tolist()
 
 
 def barrier(world: int) -> None:
@@ -158,20 +167,29 @@ def barrier(world: int) -> None:
         torch.distributed.barrier()
 
 
+def output_checksum(codes: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    """[sum of codes, sum of scale bit patterns] as int64: equal for equal outputs."""
+    return torch.stack([codes.reshape(-1).to(torch.int64).sum(),
+                        scales.contiguous().view(torch.int32).reshape(-1).to(torch.int64).sum()])
+
+
 # ------------------------------------------------------------ timing helpers
 
 
-def time_launches(fn, steps: int, stream: torch.cuda.Stream, flush: torch.Tensor | None = None):
+def time_launches(fn, steps: int, stream: torch.cuda.Stream, flush: tuple | None = None):
     """Runs fn() `steps` times on `stream`; returns (region_ms, per-launch ms list).
-    With `flush`, a buffer larger than L2 is rewritten before every launch
-    (outside the launch's own events)."""
+    With `flush` = (buffer_a, buffer_b), both larger than L2, buffer_a is
+    rewritten and buffer_b read before every launch (outside the launch's own
+    events): the write evicts the kernel's data, the read leaves L2 holding
+    clean lines, so no write-back of the flush lands inside the timed launch."""
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
         start.record(stream)
         for a, b in ev:
             if flush is not None:
-                flush.add_(1)
+                flush[0].add_(1)
+                torch.amax(flush[1], dim=0, out=flush[2])
             a.record(stream)
             fn()
             b.record(stream)
@@ -230,13 +248,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     gpu_launches = int(sum_over_ranks(launches, world))
 
     # verification gather (NCCL, outside the timed region): per-rank checksums
-    chk = torch.stack([codes.view(-1).to(torch.int64).sum(), scales.double().sum().to(torch.int64)])
-    if world > 1:
-        gathered = [torch.empty_like(chk) for _ in range(world)]
-        torch.distributed.all_gather(gathered, chk)
-        chk_all = torch.stack(gathered).cpu().tolist()
-    else:
-        chk_all = [chk.cpu().tolist()]
+    chk_all = gather_checksums(output_checksum(codes, scales), world)
 
     e2e = run_e2e(args, v7g, dev, g, u, codes, scales, rows, world)
 
@@ -340,10 +352,13 @@ def run_e2e(args, v7g, dev, g, u, codes, scales, rows, world):
 
 
 def kernel_table(v7g, dev, stream, peak) -> dict:
-    """Device-timed GB/s of the other BASELINE configs on one GPU.  C1 and C2
-    (inputs under the L2 size) rewrite a 512 MB buffer before every launch."""
+    """Device-timed GB/s of the other BASELINE configs on one GPU, median of 50
+    launches.  Configs whose inputs fit in L2 (C1, C2 and the add / RMSNorm->Q8
+    rows at the C2 shape) flush L2 before every launch."""
     out = {}
-    flush = torch.zeros(128 * 2**20, device=dev)  # 512 MB > L2
+    # 512 MB written + 512 MB read (each > 4x L2) before every flushed launch
+    flush = (torch.zeros(128 * 2**20, device=dev), torch.zeros(1024, 128 * 1024, device=dev),
+             torch.empty(128 * 1024, device=dev))
     K = 50
 
     def rec(name, fn, nbytes, rows, flushed, note=""):

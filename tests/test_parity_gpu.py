@@ -46,6 +46,17 @@ def normal(rng, shape, mean=0.0, std=1.0):
     return rng.normal(mean, std, shape).astype(F)
 
 
+# ------------------------------------------------- the fast arithmetic itself
+
+
+def test_selftest_arith_exhaustive(cuda):
+    """The Markstein reciprocal / divide and the packed SiLU and Q8 code paths
+    equal the IEEE instructions on every input they can receive (2^23
+    mantissas x every exponent, all 2^32 patterns for the SiLU and codes)."""
+    import v7multiplikator_b200 as v7g
+    assert v7g.selftest_arith() == [0, 0, 0, 0, 0]
+
+
 # --------------------------------------------------------------- RMSNorm rows
 
 
@@ -334,6 +345,14 @@ def test_rmsnorm_quantize_rows(cuda, oracle, rows, n):
     s2 = torch.empty_like(scales)
     v7g.quantize_rows(c2, s2, xb)
     np.testing.assert_array_equal(host(c2), host(codes))
+
+
+def test_rmsnorm_quantize_rejects_unaligned_codes(cuda):
+    import v7multiplikator_b200 as v7g
+    x = torch.zeros(2, 64, device=cuda)
+    buf = torch.zeros(2 * 64 + 4, dtype=torch.int8, device=cuda)
+    with pytest.raises(v7g.V7GError, match="aligned"):
+        v7g.rmsnorm_quantize_rows(buf[4:].view(2, 64), torch.empty(2, 1, device=cuda), x, torch.ones(64, device=cuda), 1e-6)
 
 
 # -------------------------------------------------------------- add_inplace

@@ -28,6 +28,7 @@ from .ops import (  # noqa: F401
     rmsnorm_quantize_rows,
     rmsnorm_rope_rows,
     rmsnorm_rows,
+    selftest_arith,
     set_rms_eps,
     swiglu,
     swiglu_q8_rows,

@@ -32,9 +32,9 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xptxas", "-warn-spills"] + ARCH
 CXX_FLAGS = ["-O2", "-std=c++17", "-fPIC", "-Wall", "-Wno-unused-parameter", f"-I{CUDA_HOME / 'include'}"]
 
-KERNEL_SOURCES = ["runtime.cu", "norm.cu", "rope.cu", "swiglu.cu", "add.cu"]
+KERNEL_SOURCES = ["runtime.cu", "norm.cu", "rope.cu", "swiglu.cu", "add.cu", "selftest.cu"]
 HOST_SOURCES = ["abi.cpp"]
-HEADERS = ["fp.cuh", "reduce.cuh", "q8.cuh", "internal.h"]
+HEADERS = ["fp.cuh", "arith.cuh", "reduce.cuh", "q8.cuh", "internal.h"]
 
 
 def exported_names() -> list[str]:

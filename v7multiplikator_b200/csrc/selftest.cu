@@ -1,0 +1,83 @@
+// selftest.cu -- exhaustive device check of the fast arithmetic in arith.cuh
+// and q8.cuh against the plain IEEE instructions it replaces.
+//
+//   test 0  rcp_nr(d) == rcp.rn.ftz(d) for every normal d in [2^-126, 2^126)
+//   test 1  div127(a) == div.rn.ftz(a, 127) for every normal a in [2^-120, 2^128)
+//   test 2  v7_sigmoid_x2 == v7_sigmoid for all 2^32 bit patterns of g
+//   test 3  q8_codes4_x2 code == q8_code_bits code for all 2^32 bit patterns
+//           of p = h * recip (recip = 1, so p = h)
+//   test 4  q8_scale_fast == q8_scale (scale and reciprocal) for every normal
+//           absmax in [2^-127, 2^128) plus inf and NaN
+// The counts of mismatches are the kernel's output (all zero when the fast
+// forms are exact over their whole input range).
+#include "internal.h"
+#include "q8.cuh"
+
+namespace v7g {
+namespace {
+
+constexpr int kBlock = 256;
+
+__device__ __forceinline__ float from_exp_mant(int e, uint32_t m) { return __uint_as_float(((uint32_t)(e + 127) << 23) | m); }
+
+__global__ void __launch_bounds__(kBlock) k_selftest(unsigned long long *counts)
+{
+	const uint64_t stride = (uint64_t)gridDim.x * kBlock;
+	const uint64_t tid = (uint64_t)blockIdx.x * kBlock + threadIdx.x;
+	unsigned long long bad[5] = {0, 0, 0, 0, 0};
+	// test 0: exponents -126 .. 125
+	for (uint64_t i = tid; i < (252ull << 23); i += stride) {
+		const float d = from_exp_mant((int)(i >> 23) - 126, (uint32_t)(i & 0x7fffff));
+		bad[0] += __float_as_uint(rcp_nr(d)) != __float_as_uint(F<true>::rcp(d));
+	}
+	// test 1: exponents -120 .. 127
+	for (uint64_t i = tid; i < (248ull << 23); i += stride) {
+		const float a = from_exp_mant((int)(i >> 23) - 120, (uint32_t)(i & 0x7fffff));
+		bad[1] += __float_as_uint(div127(a)) != __float_as_uint(F<true>::div(a, 127.0f));
+	}
+	// tests 2 and 3: every 32-bit pattern, two per thread step
+	for (uint64_t i = tid; i < (1ull << 31); i += stride) {
+		const float g0 = __uint_as_float((uint32_t)(2 * i)), g1 = __uint_as_float((uint32_t)(2 * i + 1));
+		float s0, s1;
+		unpack2(v7_sigmoid_x2(g0, g1), s0, s1);
+		bad[2] += (__float_as_uint(s0) != __float_as_uint(v7_sigmoid(g0))) + (__float_as_uint(s1) != __float_as_uint(v7_sigmoid(g1)));
+		const uint32_t packed = q8_codes4_x2(make_float4(g0, g1, g0, g1), 1.0f);
+		const uint32_t want = pack4_low_bytes(q8_code_bits(g0), q8_code_bits(g1), q8_code_bits(g0), q8_code_bits(g1));
+		bad[3] += packed != want;
+	}
+	// test 4: exponents -127 (subnormal range read as zero under FTZ) .. 127, then inf, NaN
+	for (uint64_t i = tid; i < (255ull << 23) + 2; i += stride) {
+		float w;
+		if (i < (255ull << 23))
+			w = i < (1ull << 23) ? __uint_as_float((uint32_t)i) : from_exp_mant((int)(i >> 23) - 127, (uint32_t)(i & 0x7fffff));
+		else
+			w = i == (255ull << 23) ? __int_as_float(0x7f800000) : __int_as_float(0x7fc00000);
+		float s_fast, r_fast, s_ref, r_ref;
+		q8_scale_fast(w, s_fast, r_fast);
+		q8_scale(w, s_ref, r_ref);
+		const bool same_s = __float_as_uint(s_fast) == __float_as_uint(s_ref) || (s_fast != s_fast && s_ref != s_ref);
+		const bool same_r = __float_as_uint(r_fast) == __float_as_uint(r_ref) || (r_fast != r_fast && r_ref != r_ref);
+		bad[4] += !(same_s && same_r);
+	}
+	for (int t = 0; t < 5; ++t)
+		if (bad[t])
+			atomicAdd(counts + t, bad[t]);
+}
+
+} // namespace
+} // namespace v7g
+
+using namespace v7g;
+
+extern "C" int v7g_selftest_arith(unsigned long long *dev_counts, void *stream)
+{
+	if (!dev_counts)
+		return set_error(V7G_ERR_ARG, "v7g_selftest_arith: NULL counts");
+	DeviceInfo dev;
+	int rc = current_device(&dev);
+	if (rc != V7G_OK)
+		return rc;
+	const int grid = resident_grid((const void *)k_selftest, kBlock, 0, 1 << 20, dev);
+	k_selftest<<<grid, kBlock, 0, (cudaStream_t)stream>>>(dev_counts);
+	return check_launch("v7g_selftest_arith");
+}

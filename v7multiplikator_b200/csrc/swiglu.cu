@@ -16,11 +16,8 @@ namespace v7g {
 namespace {
 
 constexpr int kBlock = 256;
-
-__device__ __forceinline__ float4 swiglu4(float4 g, float4 u)
-{
-	return make_float4(v7_swiglu(g.x, u.x), v7_swiglu(g.y, u.y), v7_swiglu(g.z, u.z), v7_swiglu(g.w, u.w));
-}
+// group pairs per warp iteration of the flat Q8 kernel
+constexpr int kQ8Unroll = 2;
 
 // --- A5  elementwise SwiGLU ---------------------------------------------
 // VEC: float4 body over count/4 vectors, the (< 4) trailing elements by the
@@ -36,7 +33,7 @@ __global__ void __launch_bounds__(kBlock) k_swiglu(float *out, const float *gate
 		const float4 *u4 = reinterpret_cast<const float4 *>(up);
 		float4 *o4 = reinterpret_cast<float4 *>(out);
 		for (int64_t i = tid; i < n4; i += nthreads)
-			st_stream4(o4 + i, swiglu4(ld_stream4(g4 + i), ld_stream4(u4 + i)));
+			st_stream4(o4 + i, v7_swiglu4(ld_stream4(g4 + i), ld_stream4(u4 + i)));
 		const int64_t t = (n4 << 2) + tid;
 		if (tid < (count & 3))
 			out[t] = v7_swiglu(gate[t], up[t]);
@@ -47,32 +44,39 @@ __global__ void __launch_bounds__(kBlock) k_swiglu(float *out, const float *gate
 }
 
 // --- A6 / A8  Q8 over flat 64-element groups (n % 64 == 0, 16-byte aligned) ---
-// One pair of groups per warp iteration; SWIGLU computes h = swiglu(a, b) in
-// registers first (A8), otherwise h = a (A6).
-template <bool SWIGLU>
+// A warp iteration covers 2*U consecutive groups: half-warp h takes groups
+// base + 2u + h, u < U, all loads issued before any arithmetic.  SWIGLU
+// computes h = swiglu(a, b) in registers first (A8), otherwise h = a (A6).
+template <bool SWIGLU, int U>
 __global__ void __launch_bounds__(kBlock) k_q8_groups(uint32_t *codes, float *scales, const float4 *a, const float4 *b, int64_t ngroups)
 {
 	const int lane = threadIdx.x & 31;
 	const int half = lane >> 4;
 	const int hl = lane & 15;
 	const int64_t nwarps = ((int64_t)gridDim.x * kBlock) >> 5;
-	for (int64_t pair = ((int64_t)blockIdx.x * kBlock + threadIdx.x) >> 5; 2 * pair < ngroups; pair += nwarps) {
-		const int64_t g = 2 * pair + half;
-		const bool valid = g < ngroups;
-		const int64_t i4 = g * 16 + hl;
-		float4 h = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-		if (valid) {
-			if (SWIGLU)
-				h = swiglu4(ld_stream4(a + i4), ld_stream4(b + i4));
-			else
-				h = ld_stream4(a + i4);
+	for (int64_t it = ((int64_t)blockIdx.x * kBlock + threadIdx.x) >> 5; 2 * U * it < ngroups; it += nwarps) {
+		float4 x[U], y[U];
+		int64_t g[U];
+#pragma unroll
+		for (int u = 0; u < U; ++u) {
+			g[u] = 2 * U * it + 2 * u + half;
+			x[u] = y[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+			if (g[u] < ngroups) {
+				x[u] = ld_stream4(a + g[u] * 16 + hl);
+				if (SWIGLU)
+					y[u] = ld_stream4(b + g[u] * 16 + hl);
+			}
 		}
-		float scale, recip;
-		q8_scale(group_absmax_f4(h, lane), scale, recip);
-		if (valid) {
-			__stcs(codes + i4, q8_codes4(h, recip));
-			if (hl == 0)
-				__stcs(scales + g, scale);
+#pragma unroll
+		for (int u = 0; u < U; ++u) {
+			const float4 h = SWIGLU ? v7_swiglu4(x[u], y[u]) : x[u];
+			float scale, recip;
+			q8_scale_fast(group_absmax_f4(h, lane), scale, recip);
+			if (g[u] < ngroups) {
+				__stcs(codes + g[u] * 16 + hl, q8_codes4_x2(h, recip));
+				if (hl == 0)
+					__stcs(scales + g[u], scale);
+			}
 		}
 	}
 }
@@ -140,12 +144,15 @@ int q8_rows(const char *what, int8_t *codes, float *scales, const float *a, cons
 		return set_error(V7G_ERR_ARG, "%s: NULL pointer", what);
 	const bool flat = n % kQ8Group == 0 && aligned16(codes) && aligned16(a) && (!swiglu || aligned16(b));
 	if (flat) {
+		constexpr int U = kQ8Unroll;
 		const int64_t ngroups = rows * (n / kQ8Group);
-		const int64_t warps = (ngroups + 1) / 2;
+		const int64_t warps = (ngroups + 2 * U - 1) / (2 * U);
 		const int64_t blocks = (warps + kBlock / 32 - 1) / (kBlock / 32);
+		uint32_t *c4 = reinterpret_cast<uint32_t *>(codes);
+		const float4 *a4 = reinterpret_cast<const float4 *>(a), *b4 = reinterpret_cast<const float4 *>(b);
 		if (swiglu)
-			return launch_persistent(k_q8_groups<true>, what, blocks, stream, reinterpret_cast<uint32_t *>(codes), scales, reinterpret_cast<const float4 *>(a), reinterpret_cast<const float4 *>(b), ngroups);
-		return launch_persistent(k_q8_groups<false>, what, blocks, stream, reinterpret_cast<uint32_t *>(codes), scales, reinterpret_cast<const float4 *>(a), reinterpret_cast<const float4 *>(b), ngroups);
+			return launch_persistent(k_q8_groups<true, U>, what, blocks, stream, c4, scales, a4, b4, ngroups);
+		return launch_persistent(k_q8_groups<false, U>, what, blocks, stream, c4, scales, a4, b4, ngroups);
 	}
 	const int64_t total = rows * ((n + kQ8Group - 1) / kQ8Group);
 	const int64_t blocks = (total + kBlock / 32 - 1) / (kBlock / 32);

@@ -54,6 +54,7 @@ _SIGNATURES = {
     "v7g_add_inplace": [c_void_p, c_void_p, c_int64, c_void_p],
     "v7g_rmsnorm_quantize_rows": [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_float, c_void_p],
     "v7g_fill_normal": [c_void_p, c_int64, c_int64, c_int64, c_uint64, c_float, c_float, c_void_p],
+    "v7g_selftest_arith": [c_void_p, c_void_p],
 }
 
 _lib: Optional[ctypes.CDLL] = None
@@ -293,6 +294,15 @@ def v7d_quantize(out_q: torch.Tensor, in_x: torch.Tensor, out_s: torch.Tensor) -
 def v7s_rmsnorm_quantize(out_q: torch.Tensor, in_x: torch.Tensor, out_s: torch.Tensor, weight: torch.Tensor) -> None:
     """src/v7_lib.h:124 -- one vector (contract n % 64 == 0)."""
     rmsnorm_quantize_rows(out_q.view(1, -1), out_s.view(1, -1), in_x.view(1, -1), weight, get_rms_eps())
+
+
+def selftest_arith(device: Optional[torch.device] = None) -> list[int]:
+    """Runs the library's exhaustive device check of its fast arithmetic and
+    returns the mismatch count of each of its five tests (all 0 when exact)."""
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    counts = torch.zeros(5, dtype=torch.int64, device=device)
+    _check(lib().v7g_selftest_arith(counts.data_ptr(), _stream(counts, None)))
+    return [int(c) for c in counts.cpu().tolist()]
 
 
 def launch_count() -> int:
