@@ -32,9 +32,13 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xptxas", "-warn-spills"] + ARCH
 CXX_FLAGS = ["-O2", "-std=c++17", "-fPIC", "-Wall", "-Wno-unused-parameter", f"-I{CUDA_HOME / 'include'}"]
 
-KERNEL_SOURCES = ["runtime.cu", "norm.cu", "rope.cu", "swiglu.cu", "add.cu", "selftest.cu"]
+KERNEL_SOURCES = ["runtime.cu", "norm.cu", "norm_q8.cu", "rope.cu", "swiglu.cu", "add.cu", "selftest.cu"]
+# Units whose kernels the reference runs with MXCSR FTZ+DAZ and that use the
+# packed-pair intrinsics, whose denormal mode follows -ftz (csrc/arith.cuh).
+# Explicit-PTX arithmetic elsewhere carries its own .ftz or not.
+FTZ_SOURCES = {"norm_q8.cu", "swiglu.cu", "selftest.cu"}
 HOST_SOURCES = ["abi.cpp"]
-HEADERS = ["fp.cuh", "arith.cuh", "reduce.cuh", "q8.cuh", "internal.h"]
+HEADERS = ["fp.cuh", "arith.cuh", "reduce.cuh", "q8.cuh", "q8_fast.cuh", "internal.h"]
 
 
 def exported_names() -> list[str]:
@@ -78,7 +82,8 @@ def build(force: bool = False) -> Path:
     for src in KERNEL_SOURCES:
         obj = BUILD / (src + ".o")
         if force or _stale(obj, [CSRC / src] + headers):
-            _run([NVCC, *NVCC_FLAGS, "-c", str(CSRC / src), "-o", str(obj)])
+            ftz = ["-ftz=true", "-DV7G_FTZ_TU"] if src in FTZ_SOURCES else ["-ftz=false"]
+            _run([NVCC, *NVCC_FLAGS, *ftz, "-c", str(CSRC / src), "-o", str(obj)])
         objs.append(obj)
     for src in HOST_SOURCES:
         obj = BUILD / (src + ".o")

@@ -8,7 +8,6 @@
 //   code  = CVTPS2DQ(x * recip) -> saturating packs -> max(code, -127)
 // all under FTZ+DAZ.
 #pragma once
-#include "arith.cuh"
 #include "fp.cuh"
 #include "reduce.cuh"
 
@@ -144,82 +143,6 @@ __device__ __forceinline__ float v7_swiglu(float g, float u)
 	return M::mul(M::mul(v7_sigmoid(g), g), u);
 }
 
-
-// ---- packed / fast forms of the above, bit-identical by construction and
-// ---- checked exhaustively by v7g_selftest_arith -------------------------
-
-// v7_sigmoid of two elements with pair arithmetic and the Markstein
-// reciprocal.  Same operations in the same order; the reciprocal argument d
-// lies in [1, 2^117), where rcp_nr is exact.
-__device__ __forceinline__ f32x2 v7_sigmoid_x2(float g0, float g1)
-{
-	const float c5 = __uint_as_float(0x3AADD303u), c4 = __uint_as_float(0x3C1E7411u), c3 = __uint_as_float(0x3D635B9Bu),
-	            c2 = __uint_as_float(0x3E75FCE0u), c1 = __uint_as_float(0x3F317215u);
-	const float t0 = fminf(fmaxf(-g0, -80.0f), 80.0f);
-	const float t1 = fminf(fmaxf(-g1, -80.0f), 80.0f);
-	const f32x2 fx = mul2(pack2(t0, t1), splat2(1.4426950408889634f));
-	const f32x2 big = add2(fx, splat2(kRoundMagic));
-	const f32x2 f = sub2(fx, sub2(big, splat2(kRoundMagic)));
-	float b0, b1;
-	unpack2(big, b0, b1);
-	// (i + 127) << 23 with i = bits(big) - bits(magic): the magic's low 9 bits
-	// are zero, so this is (bits(big) << 23) + (127 << 23) modulo 2^32
-	const float s0 = __uint_as_float((__float_as_uint(b0) << 23) + 0x3F800000u);
-	const float s1 = __uint_as_float((__float_as_uint(b1) << 23) + 0x3F800000u);
-	f32x2 p = fma2(splat2(c5), f, splat2(c4));
-	p = fma2(p, f, splat2(c3));
-	p = fma2(p, f, splat2(c2));
-	p = fma2(p, f, splat2(c1));
-	p = fma2(p, f, splat2(1.0f));
-	const f32x2 e = mul2(pack2(s0, s1), p);
-	const f32x2 d = add2(e, splat2(1.0f));
-	const f32x2 nd = sub2(splat2(-1.0f), e); // -(1 + e): round-to-nearest is sign-symmetric
-	return rcp_nr2(d, nd);
-}
-
-// (sig * g) * u for two elements.
-__device__ __forceinline__ f32x2 v7_swiglu_x2(float g0, float g1, float u0, float u1)
-{
-	return mul2(mul2(v7_sigmoid_x2(g0, g1), pack2(g0, g1)), pack2(u0, u1));
-}
-
-__device__ __forceinline__ float4 v7_swiglu4(float4 g, float4 u)
-{
-	float4 h;
-	unpack2(v7_swiglu_x2(g.x, g.y, u.x, u.y), h.x, h.y);
-	unpack2(v7_swiglu_x2(g.z, g.w, u.z, u.w), h.z, h.w);
-	return h;
-}
-
-// q8_scale with the cheap exact divide and reciprocal; non-finite maxima
-// (an inf or a NaN that survived the tree) take the IEEE instructions.
-__device__ __forceinline__ void q8_scale_fast(float wmax, float &scale, float &recip)
-{
-	wmax = x86_max(wmax, kQ8WmaxFloor);
-	if (wmax <= 3.402823466e38f) {
-		scale = div127(wmax);
-		recip = rcp_nr(scale);
-	} else {
-		q8_scale(wmax, scale, recip);
-	}
-}
-
-// q8_codes4 with pair arithmetic.
-__device__ __forceinline__ uint32_t q8_codes4_x2(float4 h, float recip)
-{
-	float p0, p1, p2, p3;
-	unpack2(mul2(pack2(h.x, h.y), splat2(recip)), p0, p1);
-	unpack2(mul2(pack2(h.z, h.w), splat2(recip)), p2, p3);
-	const f32x2 m = splat2(kRoundMagic);
-	float b0, b1, b2, b3;
-	unpack2(add2(pack2(fminf(fmaxf(p0, -127.0f), 127.0f), fminf(fmaxf(p1, -127.0f), 127.0f)), m), b0, b1);
-	unpack2(add2(pack2(fminf(fmaxf(p2, -127.0f), 127.0f), fminf(fmaxf(p3, -127.0f), 127.0f)), m), b2, b3);
-	const uint32_t q0 = fabsf(p0) < 2147483648.0f ? __float_as_uint(b0) : 0x81u;
-	const uint32_t q1 = fabsf(p1) < 2147483648.0f ? __float_as_uint(b1) : 0x81u;
-	const uint32_t q2 = fabsf(p2) < 2147483648.0f ? __float_as_uint(b2) : 0x81u;
-	const uint32_t q3 = fabsf(p3) < 2147483648.0f ? __float_as_uint(b3) : 0x81u;
-	return pack4_low_bytes(q0, q1, q2, q3);
-}
 
 } // namespace v7g
 

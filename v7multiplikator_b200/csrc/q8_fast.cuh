@@ -1,0 +1,79 @@
+// q8_fast.cuh -- packed / cheaper forms of the SiLU and Q8 steps in q8.cuh.
+// Same operations in the same order on the same values, so the results are
+// bit-identical; v7g_selftest_arith checks each against its q8.cuh original
+// over every input it can receive.  FTZ compilation units only (arith.cuh).
+#pragma once
+#include "arith.cuh"
+#include "q8.cuh"
+
+namespace v7g {
+
+// v7_sigmoid of two elements: pair arithmetic, Markstein reciprocal.  The
+// reciprocal argument d = 1 + 2^i * P(f) lies in [1, 2^117).
+__device__ __forceinline__ float2 v7_sigmoid_x2(float g0, float g1)
+{
+	const float c5 = __uint_as_float(0x3AADD303u), c4 = __uint_as_float(0x3C1E7411u), c3 = __uint_as_float(0x3D635B9Bu),
+	            c2 = __uint_as_float(0x3E75FCE0u), c1 = __uint_as_float(0x3F317215u);
+	const float2 t = make_float2(fminf(fmaxf(-g0, -80.0f), 80.0f), fminf(fmaxf(-g1, -80.0f), 80.0f));
+	const float2 fx = mul2(t, splat2(1.4426950408889634f));
+	const float2 big = add2(fx, splat2(kRoundMagic)); // rounds fx to an integer
+	// f = fx - (big - magic), written as fx + (big - magic) * -1 (both exact):
+	// this is the form the exhaustive checks pass in the compiled kernels; the
+	// packed subtraction fx - (big - magic) produced different results on
+	// about a quarter of all inputs on sm_100a with CUDA 12.9
+	const float2 f = add2(fx, mul2(add2(big, splat2(-kRoundMagic)), splat2(-1.0f)));
+	// 2^i with i = bits(big) - bits(magic): the magic's low 9 bits are zero,
+	// so (i + 127) << 23 is (bits(big) << 23) + (127 << 23) modulo 2^32
+	const float2 two = make_float2(__uint_as_float((__float_as_uint(big.x) << 23) + 0x3F800000u),
+	                               __uint_as_float((__float_as_uint(big.y) << 23) + 0x3F800000u));
+	float2 p = fma2(splat2(c5), f, splat2(c4));
+	p = fma2(p, f, splat2(c3));
+	p = fma2(p, f, splat2(c2));
+	p = fma2(p, f, splat2(c1));
+	p = fma2(p, f, splat2(1.0f));
+	const float2 e = mul2(two, p);
+	return rcp_nr2(add2(e, splat2(1.0f)));
+}
+
+// (sig * g) * u for two elements.
+__device__ __forceinline__ float2 v7_swiglu_x2(float g0, float g1, float u0, float u1)
+{
+	return mul2(mul2(v7_sigmoid_x2(g0, g1), make_float2(g0, g1)), make_float2(u0, u1));
+}
+
+__device__ __forceinline__ float4 v7_swiglu4(float4 g, float4 u)
+{
+	const float2 a = v7_swiglu_x2(g.x, g.y, u.x, u.y);
+	const float2 b = v7_swiglu_x2(g.z, g.w, u.z, u.w);
+	return make_float4(a.x, a.y, b.x, b.y);
+}
+
+// q8_scale with the Markstein reciprocal for a finite maximum; an inf or a
+// NaN that survived the tree takes the IEEE instructions.
+__device__ __forceinline__ void q8_scale_fast(float wmax, float &scale, float &recip)
+{
+	wmax = x86_max(wmax, kQ8WmaxFloor);
+	if (wmax <= 3.402823466e38f) {
+		scale = F<true>::div(wmax, 127.0f);
+		recip = rcp_nr(scale); // scale in [FLT_MIN, FLT_MAX/127]: reciprocal normal
+	} else {
+		q8_scale(wmax, scale, recip);
+	}
+}
+
+// q8_codes4 with pair arithmetic.
+__device__ __forceinline__ uint32_t q8_codes4_x2(float4 h, float recip)
+{
+	const float2 p01 = mul2(make_float2(h.x, h.y), splat2(recip));
+	const float2 p23 = mul2(make_float2(h.z, h.w), splat2(recip));
+	const float2 m = splat2(kRoundMagic);
+	const float2 b01 = add2(make_float2(fminf(fmaxf(p01.x, -127.0f), 127.0f), fminf(fmaxf(p01.y, -127.0f), 127.0f)), m);
+	const float2 b23 = add2(make_float2(fminf(fmaxf(p23.x, -127.0f), 127.0f), fminf(fmaxf(p23.y, -127.0f), 127.0f)), m);
+	const uint32_t q0 = fabsf(p01.x) < 2147483648.0f ? __float_as_uint(b01.x) : 0x81u;
+	const uint32_t q1 = fabsf(p01.y) < 2147483648.0f ? __float_as_uint(b01.y) : 0x81u;
+	const uint32_t q2 = fabsf(p23.x) < 2147483648.0f ? __float_as_uint(b23.x) : 0x81u;
+	const uint32_t q3 = fabsf(p23.y) < 2147483648.0f ? __float_as_uint(b23.y) : 0x81u;
+	return pack4_low_bytes(q0, q1, q2, q3);
+}
+
+} // namespace v7g

@@ -2,7 +2,8 @@
 // and q8.cuh against the plain IEEE instructions it replaces.
 //
 //   test 0  rcp_nr(d) == rcp.rn.ftz(d) for every normal d in [2^-126, 2^126)
-//   test 1  div127(a) == div.rn.ftz(a, 127) for every normal a in [2^-120, 2^128)
+//   test 1  rcp_nr2 == rcp.rn.ftz on both halves, same range (the halves
+//           paired with different mantissas and exponents)
 //   test 2  v7_sigmoid_x2 == v7_sigmoid for all 2^32 bit patterns of g
 //   test 3  q8_codes4_x2 code == q8_code_bits code for all 2^32 bit patterns
 //           of p = h * recip (recip = 1, so p = h)
@@ -11,7 +12,7 @@
 // The counts of mismatches are the kernel's output (all zero when the fast
 // forms are exact over their whole input range).
 #include "internal.h"
-#include "q8.cuh"
+#include "q8_fast.cuh"
 
 namespace v7g {
 namespace {
@@ -30,17 +31,19 @@ __global__ void __launch_bounds__(kBlock) k_selftest(unsigned long long *counts)
 		const float d = from_exp_mant((int)(i >> 23) - 126, (uint32_t)(i & 0x7fffff));
 		bad[0] += __float_as_uint(rcp_nr(d)) != __float_as_uint(F<true>::rcp(d));
 	}
-	// test 1: exponents -120 .. 127
-	for (uint64_t i = tid; i < (248ull << 23); i += stride) {
-		const float a = from_exp_mant((int)(i >> 23) - 120, (uint32_t)(i & 0x7fffff));
-		bad[1] += __float_as_uint(div127(a)) != __float_as_uint(F<true>::div(a, 127.0f));
+	// test 1: same range, the high half walking the space in reverse
+	for (uint64_t i = tid; i < (252ull << 23); i += stride) {
+		const uint64_t j = (252ull << 23) - 1 - i;
+		const float d0 = from_exp_mant((int)(i >> 23) - 126, (uint32_t)(i & 0x7fffff));
+		const float d1 = from_exp_mant((int)(j >> 23) - 126, (uint32_t)((j * 2654435761ull) & 0x7fffff));
+		const float2 y = rcp_nr2(make_float2(d0, d1));
+		bad[1] += (__float_as_uint(y.x) != __float_as_uint(F<true>::rcp(d0))) + (__float_as_uint(y.y) != __float_as_uint(F<true>::rcp(d1)));
 	}
 	// tests 2 and 3: every 32-bit pattern, two per thread step
 	for (uint64_t i = tid; i < (1ull << 31); i += stride) {
 		const float g0 = __uint_as_float((uint32_t)(2 * i)), g1 = __uint_as_float((uint32_t)(2 * i + 1));
-		float s0, s1;
-		unpack2(v7_sigmoid_x2(g0, g1), s0, s1);
-		bad[2] += (__float_as_uint(s0) != __float_as_uint(v7_sigmoid(g0))) + (__float_as_uint(s1) != __float_as_uint(v7_sigmoid(g1)));
+		const float2 s = v7_sigmoid_x2(g0, g1);
+		bad[2] += (__float_as_uint(s.x) != __float_as_uint(v7_sigmoid(g0))) + (__float_as_uint(s.y) != __float_as_uint(v7_sigmoid(g1)));
 		const uint32_t packed = q8_codes4_x2(make_float4(g0, g1, g0, g1), 1.0f);
 		const uint32_t want = pack4_low_bytes(q8_code_bits(g0), q8_code_bits(g1), q8_code_bits(g0), q8_code_bits(g1));
 		bad[3] += packed != want;

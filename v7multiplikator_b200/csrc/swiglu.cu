@@ -10,7 +10,7 @@
 // through a general kernel, one warp per group, that also implements the
 // reference's trailing-group rule.
 #include "internal.h"
-#include "q8.cuh"
+#include "q8_fast.cuh"
 
 namespace v7g {
 namespace {
