@@ -185,6 +185,9 @@ def time_launches(fn, steps: int, stream: torch.cuda.Stream, flush: tuple | None
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
+        # head start: keep the GPU busy (a bounded ~2 ms sleep) while the host
+        # enqueues every launch, so no launch waits on the host's submission
+        torch.cuda._sleep(4_000_000)
         start.record(stream)
         for a, b in ev:
             if flush is not None:

@@ -56,14 +56,19 @@ __global__ void __launch_bounds__(kBlock) k_fill_normal(float *dst, int64_t rows
 	}
 }
 
+// `oversubscribe` x the blocks that fit resident at once (at most
+// work_blocks): a few waves of CTAs stream measurably faster on B200 than
+// exactly one resident wave.
 template <typename Kernel, typename... Args>
-int launch_persistent(Kernel kernel, const char *what, int64_t work_blocks, void *stream, Args... args)
+int launch_persistent(Kernel kernel, const char *what, int64_t work_blocks, int oversubscribe, void *stream, Args... args)
 {
 	DeviceInfo dev;
 	int rc = current_device(&dev);
 	if (rc != V7G_OK)
 		return rc;
-	const int grid = resident_grid((const void *)kernel, kBlock, 0, work_blocks < 1 ? 1 : work_blocks, dev);
+	work_blocks = work_blocks < 1 ? 1 : work_blocks;
+	const int resident = resident_grid((const void *)kernel, kBlock, 0, work_blocks, dev);
+	const int grid = (int)(work_blocks < (int64_t)resident * oversubscribe ? work_blocks : (int64_t)resident * oversubscribe);
 	kernel<<<grid, kBlock, 0, (cudaStream_t)stream>>>(args...);
 	return check_launch(what);
 }
@@ -84,8 +89,8 @@ int v7g_add_inplace(float *x, const float *y, int64_t count, void *stream)
 	if (!x || !y)
 		return set_error(V7G_ERR_ARG, "v7g_add_inplace: NULL pointer");
 	if (aligned16(x) && aligned16(y))
-		return launch_persistent(k_add_inplace<true>, "v7g_add_inplace", ((count >> 2) + kBlock - 1) / kBlock, stream, x, y, count);
-	return launch_persistent(k_add_inplace<false>, "v7g_add_inplace", (count + kBlock - 1) / kBlock, stream, x, y, count);
+		return launch_persistent(k_add_inplace<true>, "v7g_add_inplace", ((count >> 2) + kBlock - 1) / kBlock, 4, stream, x, y, count);
+	return launch_persistent(k_add_inplace<false>, "v7g_add_inplace", (count + kBlock - 1) / kBlock, 1, stream, x, y, count);
 }
 
 int v7g_fill_normal(float *dst, int64_t rows, int64_t n, int64_t row0, uint64_t seed, float mean, float std, void *stream)
@@ -96,7 +101,7 @@ int v7g_fill_normal(float *dst, int64_t rows, int64_t n, int64_t row0, uint64_t 
 		return clear_error();
 	if (!dst)
 		return set_error(V7G_ERR_ARG, "v7g_fill_normal: NULL pointer");
-	return launch_persistent(k_fill_normal, "v7g_fill_normal", (rows * n + kBlock - 1) / kBlock, stream, dst, rows, n, row0, seed, mean, std);
+	return launch_persistent(k_fill_normal, "v7g_fill_normal", (rows * n + kBlock - 1) / kBlock, 1, stream, dst, rows, n, row0, seed, mean, std);
 }
 
 } // extern "C"

@@ -42,13 +42,7 @@ __device__ __forceinline__ float rcp_seed(float d)
 }
 
 // 1/d correctly rounded, for finite normal d whose reciprocal is normal.
-__device__ __forceinline__ float rcp_nr(float d)
-{
-	using M = F<true>;
-	const float y = rcp_seed(d);
-	const float r = M::fma(-d, y, 1.0f);
-	return M::fma(y, r, y);
-}
+__device__ __forceinline__ float rcp_nr(float d) { return rcp_nr_ftz(d); }
 
 // The pair form: both corrections in packed instructions.
 __device__ __forceinline__ float2 rcp_nr2(float2 d)

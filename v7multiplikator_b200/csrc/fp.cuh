@@ -71,6 +71,19 @@ struct F<true> {
 };
 #undef V7G_FP_BODY
 
+// Correctly rounded 1/d under FTZ for normal d with a normal reciprocal: the
+// hardware reciprocal seed (rcp.approx, at most 1 ulp off) and one
+// Newton-Raphson correction in Markstein's form (P. Markstein, IBM J. Res.
+// Dev. 34(1), 1990).  Checked against rcp.rn.ftz for every such d by
+// v7g_selftest_arith.
+__device__ __forceinline__ float rcp_nr_ftz(float d)
+{
+	float y;
+	asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(d));
+	const float r = F<true>::fma(-d, y, 1.0f);
+	return F<true>::fma(y, r, y);
+}
+
 // x86 MAXPS/MAXSS: the second operand is returned when either input is NaN
 // (or both are zero).  MINPS/MINSS likewise.
 __device__ __forceinline__ float x86_max(float a, float b) { return a > b ? a : b; }

@@ -16,7 +16,23 @@ namespace v7g {
 namespace {
 
 constexpr int kBlock = 256;
+// heads per warp work item
 constexpr int kChunk = 4;
+
+// 1/sqrt(ss / D + eps) in v7's order (COMPUTE_RMS_SCALE, v7_macros.inc:348-354)
+// with cheaper exact steps: for a power-of-two D, ss / D is the exact product
+// ss * (1/D) (FTZ flushes a subnormal quotient either way), and the final
+// reciprocal takes the Markstein form (exact for normal arguments with normal
+// reciprocals; zero, subnormal, inf and NaN take rcp.rn).
+template <int D>
+__device__ __forceinline__ float head_rms_scale(float ss, float eps)
+{
+	using M = F<true>;
+	constexpr bool pow2 = (D & (D - 1)) == 0;
+	const float mean = pow2 ? M::mul(ss, 1.0f / (float)D) : M::div(ss, (float)D);
+	const float r = M::sqrt(M::add(mean, eps));
+	return (r >= 1.17549435e-38f && r < 8.50705917e37f) ? rcp_nr_ftz(r) : M::rcp(r);
+}
 
 struct RopeArgs {
 	float *q;
@@ -32,7 +48,7 @@ struct RopeArgs {
 	float eps;
 };
 
-template <int V>
+template <int V, int CH = kChunk>
 __global__ void __launch_bounds__(kBlock) k_rope_rows(RopeArgs p)
 {
 	using M = F<true>;
@@ -40,8 +56,8 @@ __global__ void __launch_bounds__(kBlock) k_rope_rows(RopeArgs p)
 	constexpr int P = V / 2;
 	const int lane = threadIdx.x & 31;
 	const int64_t nwarps = ((int64_t)gridDim.x * kBlock) >> 5;
-	const int cq = (p.hq + kChunk - 1) / kChunk;
-	const int ck = (p.hk + kChunk - 1) / kChunk;
+	const int cq = (p.hq + CH - 1) / CH;
+	const int ck = (p.hk + CH - 1) / CH;
 	const int per_token = cq + ck;
 	const int64_t total = p.tokens * per_token;
 	float gq[V], gk[V];
@@ -50,14 +66,13 @@ __global__ void __launch_bounds__(kBlock) k_rope_rows(RopeArgs p)
 		gq[k] = p.hq ? __ldg(p.wq + lane + 32 * k) : 0.0f;
 		gk[k] = p.hk ? __ldg(p.wk + lane + 32 * k) : 0.0f;
 	}
-	const float nf = (float)D;
 	for (int64_t item = ((int64_t)blockIdx.x * kBlock + threadIdx.x) >> 5; item < total; item += nwarps) {
 		const int64_t t = item / per_token;
 		const int s = (int)(item - t * per_token);
 		const bool isq = s < cq;
 		const int heads = isq ? p.hq : p.hk;
-		const int h0 = (isq ? s : s - cq) * kChunk;
-		const int nh = min(kChunk, heads - h0);
+		const int h0 = (isq ? s : s - cq) * CH;
+		const int nh = min(CH, heads - h0);
 		float *base = (isq ? p.q : p.k) + (t * heads + h0) * (int64_t)D + lane;
 		const int64_t pos = p.pos0 + t;
 		float c[P], sn[P];
@@ -70,22 +85,22 @@ __global__ void __launch_bounds__(kBlock) k_rope_rows(RopeArgs p)
 				sn[j] = __ldg(sr + 32 * j);
 			}
 		}
-		float x[kChunk][V];
+		float x[CH][V];
 #pragma unroll
-		for (int h = 0; h < kChunk; ++h)
+		for (int h = 0; h < CH; ++h)
 			if (h < nh) {
 #pragma unroll
 				for (int k = 0; k < V; ++k)
 					x[h][k] = ld_stream(base + h * D + 32 * k);
 			}
 #pragma unroll
-		for (int h = 0; h < kChunk; ++h)
+		for (int h = 0; h < CH; ++h)
 			if (h < nh) {
 				float acc = 0.0f;
 #pragma unroll
 				for (int k = 0; k < V; ++k)
 					acc = M::fma(x[h][k], x[h][k], acc);
-				const float scale = rms_scale<true>(reduce_chains_4x8<true>(acc), nf, p.eps);
+				const float scale = head_rms_scale<D>(reduce_chains_4x8<true>(acc), p.eps);
 				float *hb = base + h * D;
 				if (pos == 0) {
 #pragma unroll
@@ -148,6 +163,8 @@ __global__ void __launch_bounds__(kBlock) k_rope_rows_general(RopeArgs p, int D)
 	}
 }
 
+// Up to 4 x the blocks resident at once (at most work_blocks): a few waves of
+// CTAs stream faster on B200 than exactly one resident wave.
 template <typename Kernel, typename... Args>
 int launch_persistent(Kernel kernel, const char *what, int64_t work_blocks, void *stream, Args... args)
 {
@@ -155,7 +172,8 @@ int launch_persistent(Kernel kernel, const char *what, int64_t work_blocks, void
 	int rc = current_device(&dev);
 	if (rc != V7G_OK)
 		return rc;
-	const int grid = resident_grid((const void *)kernel, kBlock, 0, work_blocks, dev);
+	const int resident = resident_grid((const void *)kernel, kBlock, 0, work_blocks, dev);
+	const int grid = (int)(work_blocks < 4ll * resident ? work_blocks : 4ll * resident);
 	kernel<<<grid, kBlock, 0, (cudaStream_t)stream>>>(args...);
 	return check_launch(what);
 }
