@@ -97,6 +97,10 @@ V7_ABI void *ht_find(const char *key, unsigned long long *out_len);             
 V7_ABI int db_save(const char *filename);                /* :134 */
 V7_ABI int db_load(const char *filename);                /* :135 */
 V7_ABI void db_set_readonly(int flag);                   /* :138 */
+
+/* Exported but not provided: marks the engine dead ("v7sprintf: not provided
+   by v7g") and returns 0.  Declared here rather than in v7_threading_stubs.h
+   because it is variadic. */
 V7_ABI int v7sprintf(char *buffer, int buf_size, const char *format, ...); /* :318 */
 
 /* Exported data words (src/v7_lib.h:306-314). */
