@@ -17,7 +17,8 @@ Reported (one JSON line from rank 0):
              codes/scales back (pipelined in row chunks over three streams)
   roofline   the kernel's achieved GB/s against the measured HBM copy peak
   cpu_baseline  the oracle port on the host cores, bounded sample (N=1 only)
-  kernels    the other BASELINE configs (C1-C4, add_inplace, RMSNorm->Q8),
+  kernels    the other BASELINE configs (C1-C4) and the next rows (add_inplace,
+             RMSNorm->Q8, RoPE without the norm, the RoPE table build),
              device-timed, N=1 only
 ``--impl reference`` times the CPU implementation instead (rank 0 only).
 """
@@ -395,16 +396,26 @@ def kernel_table(v7g, dev, stream, peak) -> dict:
     rec("c2_fused_add_rmsnorm_4096x2048", lambda: v7g.fused_add_rmsnorm_rows(o2, r, d, w, 1e-6, stream=stream),
         4096 * 2048 * 16 + 2048 * 4, 4096, True)
     rec("add_inplace_4096x2048", lambda: v7g.add_inplace(r, d, stream=stream), 4096 * 2048 * 12, 4096, True)
-    from v7multiplikator_b200.tables import rope_tables
     # C3 RMSNorm + RoPE Q[8192,16,128] K[8192,8,128]
     q = fill((8192, 16 * 128), 6, 0.0, 1.0).view(8192, 16, 128)
     k = fill((8192, 8 * 128), 7, 0.0, 1.0).view(8192, 8, 128)
     wq = fill((1, 128), 8, 1.0, 0.1)[0]
     wk = fill((1, 128), 9, 1.0, 0.1)[0]
-    cos, sin = (torch.from_numpy(t).to(dev) for t in rope_tables(8192, 64, 64, 1e6))
+    cos, sin = v7g.rope_tables(8192, 64, 1e6, device=dev)
     rec("c3_rmsnorm_rope_8192x(16+8)x128", lambda: v7g.rmsnorm_rope_rows(q, k, wq, wk, cos, sin, 0, 1e-6, stream=stream),
         8192 * 24 * 128 * 8 + 8192 * 64 * 8 + 2 * 128 * 4, 8192, False)
+    # RoPE without the norm at the C3 geometry
+    rec("rope_only_8192x(16+8)x128", lambda: v7g.rope_only_rows(q, k, cos, sin, 0, stream=stream),
+        8192 * 24 * 128 * 8 + 8192 * 64 * 8, 8192, False)
     del q, k
+    # the reference's internal tables: 131072 positions x 64 pairs, cos + sin written
+    tc = torch.empty(131072, 64, device=dev)
+    ts = torch.empty_like(tc)
+    freqs = np.ascontiguousarray(v7g.rope_freqs(64, 1e6))
+    rec("rope_tables_131072x64", lambda: v7g.ops._check(v7g.lib().v7g_rope_tables(
+        tc.data_ptr(), ts.data_ptr(), 0, 131072, 64, 64, freqs.ctypes.data, stream.cuda_stream)),
+        131072 * 64 * 8, 131072, False, "double-precision sincos per entry: FP64-bound, not HBM-bound")
+    del tc, ts
     # C4 SwiGLU [4096, 8192]
     gg = fill((4096, 8192), 10, 0.0, 2.0)
     uu = fill((4096, 8192), 11, 0.0, 2.0)
@@ -524,16 +535,24 @@ def _profile_case(name: str, rows: int, dev):
         c = torch.empty(rows, 2048, dtype=torch.int8, device=dev)
         s = torch.empty(rows, 32, device=dev)
         return lambda: v7g.rmsnorm_quantize_rows(c, s, x, w, 1e-6), rows * (2048 * 5 + 128)
-    if name == "rmsnorm_rope":
-        from v7multiplikator_b200.tables import rope_tables
+    if name in ("rmsnorm_rope", "rope_only"):
         q, k = fill((rows, 16 * 128), 6, 0.0, 1.0).view(rows, 16, 128), fill((rows, 8 * 128), 7, 0.0, 1.0).view(rows, 8, 128)
         wq, wk = fill((1, 128), 8, 1.0, 0.1)[0], fill((1, 128), 9, 1.0, 0.1)[0]
-        cos, sin = (torch.from_numpy(t).to(dev) for t in rope_tables(rows, 64, 64, 1e6))
+        cos, sin = v7g.rope_tables(rows, 64, 1e6, device=dev)
+        if name == "rope_only":
+            return lambda: v7g.rope_only_rows(q, k, cos, sin, 0), rows * (24 * 128 * 8 + 64 * 8)
         return lambda: v7g.rmsnorm_rope_rows(q, k, wq, wk, cos, sin, 0, 1e-6), rows * (24 * 128 * 8 + 64 * 8)
+    if name == "rope_tables":
+        tc = torch.empty(rows, 64, device=dev)
+        ts = torch.empty_like(tc)
+        freqs = np.ascontiguousarray(v7g.rope_freqs(64, 1e6))
+        return (lambda: v7g.ops._check(v7g.lib().v7g_rope_tables(tc.data_ptr(), ts.data_ptr(), 0, rows, 64, 64,
+                                                                 freqs.ctypes.data, None))), rows * 64 * 8
     raise ValueError(name)
 
 
-PROFILE_CASES = ("swiglu_q8", "swiglu", "rmsnorm", "fused_add_rmsnorm", "add_inplace", "rmsnorm_quantize", "rmsnorm_rope")
+PROFILE_CASES = ("swiglu_q8", "swiglu", "rmsnorm", "fused_add_rmsnorm", "add_inplace", "rmsnorm_quantize", "rmsnorm_rope",
+                 "rope_only", "rope_tables")
 
 
 def run_profile(args) -> None:

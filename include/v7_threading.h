@@ -70,6 +70,33 @@ V7_ABI void v7d_quantize(char *out_q, float *in_x, float *out_s, int n);
    n % 64 == 0. */
 V7_ABI void v7s_rmsnorm_quantize(char *out_q, float *in_x, float *out_s, int n, float *weight);
 
+/* ---- engine-internal kernels ------------------------------------------- */
+/* The reference links these statically into its forward pass; they are not
+   among the names v7_load resolves.  Exported here under the same names and
+   conventions so that an engine-side caller can bind them. */
+
+/* rope_only_dispatch.inc:10-47 (called at forward_q8.inc:44).  RoPE without
+   the norm on one token's n_heads heads, in place; cos/sin row
+   pos * rope_max_dim; position 0 is the identity; head_dim % 32 == 0. */
+V7_ABI void v7s_rope_only_heads(float *buf, int n_heads, int head_dim, float *cos_table, float *sin_table, int pos, int rope_max_dim);
+
+/* Descriptor of v7s_qk_fork_heads (qk_fork_kernel.inc:10-27), 48 bytes. */
+typedef struct v7_qk_fork_args {
+	float *buf;    /* first head */
+	float *weight; /* per-layer norm gamma [head_dim] */
+	float *cos;    /* cos table, already offset to the position's row */
+	float *sin;    /* sin table, already offset to the position's row */
+	int head_dim;
+	int heads;
+	int pos;
+	int unused;
+} v7_qk_fork_args;
+
+/* qk_fork_kernel.inc:40-62: the RMSNorm + RoPE of v7s_rmsnorm_rope_heads over
+   args->heads heads, every input taken from the descriptor (reentrant in the
+   reference). */
+V7_ABI void v7s_qk_fork_heads(const v7_qk_fork_args *args);
+
 /* ---- runtime surface, implemented on the host ------------------------- */
 
 V7_ABI int v7_init(const char *db_path);                 /* src/v7_lib.h:167 */
@@ -82,8 +109,15 @@ V7_ABI int v7_get_console_width(void);                   /* :189 */
 V7_ABI int v7_db_add(const char *key, const void *data, int len, unsigned int persist); /* :238 */
 V7_ABI void *v7_db_find(const char *key, unsigned long long *out_len);                 /* :239 */
 V7_ABI void v7_shutdown(void);                           /* :250 */
-V7_ABI void v7s_rope_init(int head_dim, float rope_base);/* :275 */
-V7_ABI void v7s_set_fused_rope(int pos, int head_dim);   /* :276 */
+/* :275; fused_dispatch.inc:58-76.  Builds the library's RoPE tables
+   [131072, head_dim/2] on the current device (v7g_get_rope_tables) from the
+   keys __sys_rope_base (float) and __sys_rope_type (int; 1 = llama3, which
+   also reads __sys_rope_factor, __sys_rope_high_freq_factor,
+   __sys_rope_low_freq_factor, __sys_rope_orig_max_pos).  A missing key marks
+   the engine dead, as the reference FATALs.  rope_base is not read (the
+   reference takes the base from the key store too). */
+V7_ABI void v7s_rope_init(int head_dim, float rope_base);
+V7_ABI void v7s_set_fused_rope(int pos, int head_dim);   /* :276; records the position */
 V7_ABI void v7s_set_spin(int flag);                      /* :278 */
 V7_ABI void v7s_enable_thinking(int on);                 /* :279 */
 V7_ABI void v7s_shutdown(void);                          /* :280 */

@@ -85,6 +85,46 @@ int v7g_add_inplace(float *x, const float *y, int64_t count, void *stream);
    Contract: n > 0, n % 64 == 0. */
 int v7g_rmsnorm_quantize_rows(int8_t *codes, float *scales, const float *x, const float *w, int64_t rows, int n, float eps, void *stream);
 
+/* RoPE without the norm over GQA Q/K, in place (v7s_rope_only_heads,
+   rope_only_kernel.inc:11-53, rope_only_dispatch.inc:10-47; the path of
+   models without a QK norm, forward_q8.inc:40-44).  Same layout and table
+   addressing as v7g_rmsnorm_rope_rows; position 0 leaves its heads untouched.
+   Contract: head_dim % 32 == 0, 32 <= head_dim <= 1024. */
+int v7g_rope_only_rows(float *q, float *k, int64_t tokens, int n_q_heads, int n_kv_heads, int head_dim, const float *cos_table, const float *sin_table, int64_t pos0, int rope_max_dim, void *stream);
+
+/* RoPE frequencies freqs[j], j < half (host function, host memory, no
+   device): base^(-j/half) as the reference's table builder computes it on
+   the x87 unit and stores it as a double (fused_f32_kernel.inc:117-147), or
+   with llama3 scaling when scaling == 1 (:149-256; factor, high/low frequency
+   factors and original context length as in the keys __sys_rope_factor,
+   __sys_rope_high_freq_factor, __sys_rope_low_freq_factor,
+   __sys_rope_orig_max_pos).  Contract: 0 < half <= 256. */
+int v7g_rope_freqs(double *freqs, int half, float base, int scaling, float factor, float high_freq_factor, float low_freq_factor, int orig_max_pos);
+
+/* RoPE tables on the device: rows pos0 .. pos0+positions-1 of cos / sin,
+   row stride `stride` floats, entry j < half = cos / sin(freqs[j] * pos) with
+   the angle at x87 extended precision (fused_f32_kernel.inc:257-302),
+   columns half.. zero.  freqs: HOST array of `half` doubles (v7g_rope_freqs).
+   Agrees with the reference's fsincos tables to within one fp32 ulp (equal
+   on all but about one entry in ten million).
+   Contract: 0 < half <= 256, stride >= half, pos0 + positions <= 2^31. */
+int v7g_rope_tables(float *cos_table, float *sin_table, int64_t pos0, int64_t positions, int half, int stride, const double *freqs, void *stream);
+
+/* Positions of the tables v7s_rope_init builds (ROPE_INTERNAL_MAX_SEQ_LEN,
+   fused_f32_kernel.inc:9). */
+#define V7G_ROPE_TABLE_POSITIONS 131072
+
+/* Builds the library's RoPE tables [V7G_ROPE_TABLE_POSITIONS, head_dim/2] on
+   the current device from explicit parameters (v7s_rope_init reads the same
+   ones from the key store): v7g_rope_freqs on the host, then v7g_rope_tables.
+   Synchronous.  Contract: head_dim even, head_dim/2 <= 256. */
+int v7g_rope_init(int head_dim, float base, int scaling, float factor, float high_freq_factor, float low_freq_factor, int orig_max_pos);
+
+/* The device tables the last v7s_rope_init / v7g_rope_init built on the current device:
+   [V7G_ROPE_TABLE_POSITIONS, *half] fp32 each, row stride *half, owned by the
+   library (freed by v7s_shutdown).  V7G_ERR_ARG when none was built. */
+int v7g_get_rope_tables(const float **cos_table, const float **sin_table, int *half);
+
 /* ---- runtime ---------------------------------------------------------- */
 
 /* RMS epsilon used by the reference-ABI entries (v7s_rmsnorm & co.), which
@@ -100,8 +140,8 @@ const char *v7g_last_error(void);
 uint64_t v7g_launch_count(void);
 
 /* Exhaustive device self-check of the library's fast arithmetic (the
-   Markstein-corrected reciprocal and divide, the packed-pair SiLU and Q8 code
-   paths) against the plain IEEE instructions, over every input each can
+   Markstein-corrected reciprocal, the fast Q8 scale, the packed-pair SiLU and
+   Q8 code paths) against the plain IEEE instructions, over every input each can
    receive.  dev_counts: 5 zeroed device counters, incremented by the number of
    mismatches of each test (all must stay 0).  Asynchronous on `stream`. */
 int v7g_selftest_arith(unsigned long long *dev_counts, void *stream);

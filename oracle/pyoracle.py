@@ -48,7 +48,9 @@ class Oracle:
             "orc_swiglu_q8_rows": [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int],
             "orc_add_inplace": [c_void_p, c_void_p, c_int64, c_int],
             "orc_rmsnorm_quantize_rows": [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_float, c_int],
-            "orc_rope_tables": [c_void_p, c_void_p, c_int64, c_int, c_int, c_double],
+            "orc_rope_only_rows": [c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p, c_int64, c_int, c_int],
+            "orc_rope_freqs": [c_void_p, c_int, c_float, c_int, c_float, c_float, c_float, c_int],
+            "orc_rope_tables": [c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_void_p, c_int],
         }
         for name, args in sig.items():
             fn = getattr(L, name)
@@ -137,9 +139,37 @@ class Oracle:
                                                     rows, n, eps, self.nthreads), "rmsnorm_quantize")
         return q, s
 
-    def rope_tables(self, positions: int, half: int, stride: int | None = None, base: float = 1e6):
+    def rope_only(self, buf: np.ndarray, cos: np.ndarray, sin: np.ndarray, pos0: int,
+                  rope_max_dim: int | None = None) -> np.ndarray:
+        """RoPE without the norm; buf [tokens, heads, head_dim]."""
+        out = np.array(buf, np.float32, copy=True, order="C")
+        tokens, heads, hd = out.shape
+        cos = np.ascontiguousarray(cos, np.float32)
+        sin = np.ascontiguousarray(sin, np.float32)
+        rmd = rope_max_dim if rope_max_dim is not None else cos.shape[-1]
+        self._ok(self.lib.orc_rope_only_rows(_ptr(out), tokens, heads, hd, _ptr(cos), _ptr(sin), pos0, rmd,
+                                             self.nthreads), "rope_only")
+        return out
+
+    def rope_freqs(self, half: int, base: float = 1e6, scaling: dict | None = None) -> np.ndarray:
+        """freqs[j] (float64) as the reference's table builder stores them;
+        scaling = None or {"factor", "high_freq_factor", "low_freq_factor",
+        "orig_max_pos"} for llama3 scaling."""
+        f = np.empty(half, np.float64)
+        sc = scaling or {}
+        self._ok(self.lib.orc_rope_freqs(_ptr(f), half, base, 1 if scaling else 0, sc.get("factor", 0.0),
+                                         sc.get("high_freq_factor", 0.0), sc.get("low_freq_factor", 0.0),
+                                         int(sc.get("orig_max_pos", 0))), "rope_freqs")
+        return f
+
+    def rope_tables(self, positions: int, half: int, stride: int | None = None, base: float = 1e6,
+                    pos0: int = 0, scaling: dict | None = None):
+        """cos, sin [positions, stride] fp32 for positions pos0.. (x87, as the
+        reference builds them)."""
         stride = stride or half
+        freqs = self.rope_freqs(half, base, scaling)
         c = np.empty((positions, stride), np.float32)
         s = np.empty((positions, stride), np.float32)
-        self._ok(self.lib.orc_rope_tables(_ptr(c), _ptr(s), positions, half, stride, base), "rope_tables")
+        self._ok(self.lib.orc_rope_tables(_ptr(c), _ptr(s), pos0, positions, half, stride, _ptr(freqs),
+                                          self.nthreads), "rope_tables")
         return c, s

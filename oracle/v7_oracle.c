@@ -263,6 +263,25 @@ static void rmsnorm_rope_head(float *x, int head_dim, const float *w, const floa
 	}
 }
 
+/* RoPE without the norm, one head in place (rope_only_kernel.inc:13-50):
+   position 0 is the identity and writes nothing; otherwise each pair (j,
+   j + half) becomes (lo*cos - hi*sin, lo*sin + hi*cos) with the product by
+   cos / sin of lo rounded and the hi term fused (vfnmadd231ps /
+   vfmadd231ps). */
+static void rope_only_head(float *x, int head_dim, const float *cs, const float *sn, int64_t pos)
+{
+	if (pos == 0)
+		return;
+	int half = head_dim / 2;
+	for (int j = 0; j < half; ++j) {
+		float lo = x[j], hi = x[j + half];
+		float lc = lo * cs[j];
+		float ls = lo * sn[j];
+		x[j] = fmaf(-hi, sn[j], lc);
+		x[j + half] = fmaf(hi, cs[j], ls);
+	}
+}
+
 static void rmsnorm_quantize_row(int8_t *q, float *s, const float *x, const float *w, int n, float eps)
 {
 	float scale = rms_scale(sumsq_blocks(x, n), (float)n, eps);
@@ -276,6 +295,136 @@ static void rmsnorm_quantize_row(int8_t *q, float *s, const float *x, const floa
 		}
 		quantize_group64(q + g * ORC_Q8_GS, s + g, norm);
 	}
+}
+
+/* ------------------------------------------------------------------------ */
+/* RoPE tables: the x87 extended-precision producer                         */
+/* ------------------------------------------------------------------------ */
+
+/* The reference builds its tables with x87 instructions at extended
+   precision, round to nearest, all exceptions masked (control word 0x037F,
+   fused_f32_kernel.inc:22,117-118), keeping some intermediates in 80-bit
+   registers and storing others as doubles.  long double on x86-64 is that
+   80-bit format and its arithmetic compiles to the same x87 operations; the
+   instructions C has no operator for are issued directly. */
+#define X87_CW_EXTENDED_NEAREST 0x037F
+
+static unsigned short x87_set_cw(unsigned short cw)
+{
+	unsigned short old;
+	__asm__ __volatile__("fnstcw %0" : "=m"(old));
+	__asm__ __volatile__("fldcw %0" : : "m"(cw));
+	return old;
+}
+
+/* y * log2(x) */
+static long double x87_fyl2x(long double x, long double y)
+{
+	long double r;
+	__asm__("fyl2x" : "=t"(r) : "0"(x), "u"(y) : "st(1)");
+	return r;
+}
+
+static long double x87_frndint(long double x)
+{
+	long double r;
+	__asm__("frndint" : "=t"(r) : "0"(x));
+	return r;
+}
+
+/* 2^x - 1 for |x| <= 1 */
+static long double x87_f2xm1(long double x)
+{
+	long double r;
+	__asm__("f2xm1" : "=t"(r) : "0"(x));
+	return r;
+}
+
+/* x * 2^trunc(n) */
+static long double x87_fscale(long double x, long double n)
+{
+	long double r;
+	__asm__("fscale" : "=t"(r) : "0"(x), "u"(n));
+	return r;
+}
+
+static void x87_fsincos(long double a, long double *c, long double *s)
+{
+	long double cr, sr;
+	__asm__("fsincos" : "=t"(cr), "=u"(sr) : "0"(a));
+	*c = cr;
+	*s = sr;
+}
+
+/* base^(-j/half) at extended precision: -j/half, times log2(base) by fyl2x,
+   split into integer and fraction, 2^fraction by f2xm1 + 1, scaled by the
+   integer power (RBIT_CALC_INV_FREQ, fused_f32_kernel.inc:120-137). */
+static long double inv_freq_x87(float base, int j, int half)
+{
+	long double e = (long double)j / (long double)half;
+	long double y = x87_fyl2x((long double)base, -e);
+	long double ip = x87_frndint(y);
+	long double p = x87_f2xm1(y - ip) + 1.0L;
+	return x87_fscale(p, ip);
+}
+
+/* 2*pi as the double the reference stores (fused_f32_kernel.inc:65-66) */
+static const double kTwoPi = 6.28318530717958647692;
+
+/* llama3 frequency scaling for one j (fused_f32_kernel.inc:186-256): the
+   values the reference keeps in double slots are rounded to double at the
+   same points, the rest stays at extended precision. */
+static double llama3_freq_x87(float base, int j, int half, double factor, double high, double low, double old_ctx, double low_wl, double high_wl)
+{
+	long double inv80 = inv_freq_x87(base, j, half);
+	double inv = (double)inv80;
+	double wavelen = (double)((long double)kTwoPi / inv80);
+	double ifl = low_wl < wavelen ? (double)((long double)inv / (long double)factor) : inv;
+	long double num = (long double)old_ctx / (long double)wavelen - (long double)low;
+	long double den = (long double)high - (long double)low;
+	double smooth = (double)(num / den);
+	long double t1 = (1.0L - (long double)smooth) * ((long double)ifl / (long double)factor);
+	long double t2 = (long double)smooth * (long double)ifl;
+	double smoothed = (double)(t1 + t2);
+	int medium = (high_wl < wavelen && low_wl >= wavelen) || high_wl == wavelen;
+	return medium ? smoothed : ifl;
+}
+
+int orc_rope_freqs(double *freqs, int half, float base, int scaling, float factor, float high_freq_factor, float low_freq_factor, int orig_max_pos)
+{
+	if (!freqs || half <= 0 || half > ORC_ROPE_MAX_HALF || (scaling != 0 && scaling != 1))
+		return -1;
+	unsigned short saved = x87_set_cw(X87_CW_EXTENDED_NEAREST);
+	if (scaling == 0) {
+		for (int j = 0; j < half; ++j)
+			freqs[j] = (double)inv_freq_x87(base, j, half);
+	} else {
+		double f = factor, hi = high_freq_factor, lo = low_freq_factor, old = (double)orig_max_pos;
+		double low_wl = (double)((long double)old / (long double)lo);
+		double high_wl = (double)((long double)old / (long double)hi);
+		for (int j = 0; j < half; ++j)
+			freqs[j] = llama3_freq_x87(base, j, half, f, hi, lo, old, low_wl, high_wl);
+	}
+	x87_set_cw(saved);
+	return 0;
+}
+
+/* One table row: angle = freq_j * pos at extended precision, fsincos, each
+   stored as fp32 (fused_f32_kernel.inc:262-283).  Columns half..stride-1 are
+   zero. */
+static void rope_table_row(float *cs, float *sn, int64_t pos, int half, int stride, const double *freqs)
+{
+	unsigned short saved = x87_set_cw(X87_CW_EXTENDED_NEAREST);
+	double pd = (double)pos;
+	for (int j = 0; j < half; ++j) {
+		long double c, s;
+		x87_fsincos((long double)freqs[j] * (long double)pd, &c, &s);
+		cs[j] = (float)c;
+		sn[j] = (float)s;
+	}
+	for (int j = half; j < stride; ++j)
+		cs[j] = sn[j] = 0.0f;
+	x87_set_cw(saved);
 }
 
 /* ------------------------------------------------------------------------ */
@@ -300,9 +449,10 @@ typedef struct job {
 	int n, heads, rope_max_dim;
 	int64_t pos0;
 	float eps;
+	const double *freqs;
 } job;
 
-enum { K_RMSNORM, K_ADD_RMSNORM, K_ROPE, K_SWIGLU, K_QUANT, K_SWIGLU_Q8, K_ADD, K_RMSNORM_Q8 };
+enum { K_RMSNORM, K_ADD_RMSNORM, K_ROPE, K_SWIGLU, K_QUANT, K_SWIGLU_Q8, K_ADD, K_RMSNORM_Q8, K_ROPE_ONLY, K_ROPE_TABLE };
 
 static void run_job(job *j)
 {
@@ -328,6 +478,18 @@ static void run_job(job *j)
 				rmsnorm_rope_head(tok + (int64_t)h * j->n, j->n, j->fw, cs, sn, pos, j->eps);
 			break;
 		}
+		case K_ROPE_ONLY: {
+			int64_t pos = j->pos0 + r;
+			float *tok = j->fr + r * (int64_t)j->heads * j->n;
+			const float *cs = j->fc + pos * j->rope_max_dim;
+			const float *sn = j->fs + pos * j->rope_max_dim;
+			for (int h = 0; h < j->heads; ++h)
+				rope_only_head(tok + (int64_t)h * j->n, j->n, cs, sn, pos);
+			break;
+		}
+		case K_ROPE_TABLE: /* rows are positions; n = half, rope_max_dim = row stride */
+			rope_table_row(j->fo + r * j->rope_max_dim, j->fr + r * j->rope_max_dim, j->pos0 + r, j->n, j->rope_max_dim, j->freqs);
+			break;
 		case K_SWIGLU: /* rows here are chunks of 4096 elements */
 		{
 			int64_t b = r * 4096, e = b + 4096 < j->n64 ? b + 4096 : j->n64;
@@ -546,21 +708,35 @@ int orc_rmsnorm_quantize_rows(int8_t *q, float *s, const float *x, const float *
 	return run_rows(&j, rows, nthreads);
 }
 
-int orc_rope_tables(float *cos_table, float *sin_table, int64_t positions, int half, int stride, double base)
+int orc_rope_tables(float *cos_table, float *sin_table, int64_t pos0, int64_t positions, int half, int stride, const double *freqs, int nthreads)
 {
-	if (half <= 0 || stride < half || positions < 0 || !(base > 0.0))
+	if (half <= 0 || stride < half || positions < 0 || pos0 < 0 || pos0 + positions > ((int64_t)1 << 31) || !freqs)
 		return -1;
-	for (int64_t p = 0; p < positions; ++p)
-		for (int j = 0; j < stride; ++j) {
-			if (j < half) {
-				double freq = pow(base, -(double)j / (double)half);
-				double ang = (double)p * freq;
-				cos_table[p * stride + j] = (float)cos(ang);
-				sin_table[p * stride + j] = (float)sin(ang);
-			} else {
-				cos_table[p * stride + j] = 0.0f;
-				sin_table[p * stride + j] = 0.0f;
-			}
-		}
-	return 0;
+	job j = { 0 };
+	j.kind = K_ROPE_TABLE;
+	j.ftz = 0;
+	j.fo = cos_table;
+	j.fr = sin_table;
+	j.pos0 = pos0;
+	j.n = half;
+	j.rope_max_dim = stride;
+	j.freqs = freqs;
+	return run_rows(&j, positions, nthreads);
+}
+
+int orc_rope_only_rows(float *buf, int64_t tokens, int n_heads, int head_dim, const float *cos_table, const float *sin_table, int64_t pos0, int rope_max_dim, int nthreads)
+{
+	if (head_dim <= 0 || head_dim % 32 != 0 || n_heads < 0 || tokens < 0 || pos0 < 0 || rope_max_dim < head_dim / 2)
+		return -1;
+	job j = { 0 };
+	j.kind = K_ROPE_ONLY;
+	j.ftz = 1;
+	j.fr = buf;
+	j.fc = cos_table;
+	j.fs = sin_table;
+	j.n = head_dim;
+	j.heads = n_heads;
+	j.pos0 = pos0;
+	j.rope_max_dim = rope_max_dim;
+	return run_rows(&j, tokens, nthreads);
 }

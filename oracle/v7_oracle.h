@@ -83,11 +83,27 @@ int orc_add_inplace(float *x, const float *y, int64_t n, int nthreads);
    Contract n % 64 == 0. */
 int orc_rmsnorm_quantize_rows(int8_t *q, float *s, const float *x, const float *w, int64_t rows, int n, float eps, int nthreads);
 
-/* RoPE tables [positions, half] (row stride `stride`) for NeoX half-split
-   rotation: angle = p * base^(-j/half), computed in double and rounded to
-   fp32 (restates the table producer of fused_f32_kernel.inc:120-147,257-302
-   without llama3 scaling). */
-int orc_rope_tables(float *cos_table, float *sin_table, int64_t positions, int half, int stride, double base);
+/* Next row 2: RoPE without the norm (v7s_rope_only_heads,
+   rope_only_kernel.inc:11-53, rope_only_dispatch.inc:10-47) over `tokens`
+   tokens of one tensor [tokens, n_heads, head_dim], in place.  Position 0
+   is the identity.  Contract head_dim % 32 == 0.  FTZ+DAZ. */
+int orc_rope_only_rows(float *buf, int64_t tokens, int n_heads, int head_dim, const float *cos_table, const float *sin_table, int64_t pos0, int rope_max_dim, int nthreads);
+
+/* largest half the reference's frequency buffer holds (256 doubles,
+   fused_f32_kernel.inc:138-139) */
+#define ORC_ROPE_MAX_HALF 256
+
+/* A4 frequencies freqs[j], j < half, as the reference's table builder
+   computes and stores them (doubles): base^(-j/half) by the x87 chain of
+   fused_f32_kernel.inc:120-137 (scaling 0), or with llama3 scaling
+   (scaling 1, :149-256; factor, high/low frequency factors and the original
+   context length as the __sys_rope_* keys hold them). */
+int orc_rope_freqs(double *freqs, int half, float base, int scaling, float factor, float high_freq_factor, float low_freq_factor, int orig_max_pos);
+
+/* A4 tables: rows pos0 .. pos0+positions-1 of cos / sin (row stride `stride`,
+   columns half.. zero): angle = freqs[j] * pos at x87 extended precision,
+   fsincos, stored as fp32 (fused_f32_kernel.inc:257-302). */
+int orc_rope_tables(float *cos_table, float *sin_table, int64_t pos0, int64_t positions, int half, int stride, const double *freqs, int nthreads);
 
 #ifdef __cplusplus
 }

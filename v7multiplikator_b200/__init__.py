@@ -28,6 +28,10 @@ from .ops import (  # noqa: F401
     rmsnorm_quantize_rows,
     rmsnorm_rope_rows,
     rmsnorm_rows,
+    rope_freqs,
+    rope_init,
+    rope_only_rows,
+    rope_tables,
     selftest_arith,
     set_rms_eps,
     swiglu,
@@ -38,6 +42,7 @@ from .ops import (  # noqa: F401
     v7s_rmsnorm,
     v7s_rmsnorm_quantize,
     v7s_rmsnorm_rope_heads,
+    v7s_rope_only_heads,
     version,
 )
 

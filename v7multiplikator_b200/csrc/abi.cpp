@@ -26,6 +26,7 @@
 
 #include "../../include/v7_threading.h"
 #include "../../include/v7g.h"
+#include "internal.h"
 
 extern "C" float *v7g_rms_eps_slot(void);
 
@@ -56,7 +57,13 @@ struct DeviceCtx {
 	cudaStream_t stream = nullptr;
 	char *work = nullptr;
 	size_t work_bytes = 0;
+	// RoPE tables built by v7s_rope_init: [V7G_ROPE_TABLE_POSITIONS, rope_half]
+	float *rope_cos = nullptr;
+	float *rope_sin = nullptr;
+	int rope_half = 0;
 };
+int g_fused_pos = 0;      // v7s_set_fused_rope
+int g_fused_head_dim = 0; // v7s_set_fused_rope / v7s_rope_init
 constexpr int kMaxDevices = 64;
 DeviceCtx g_ctx[kMaxDevices];
 
@@ -393,6 +400,55 @@ V7_ABI void v7s_rmsnorm_rope_heads(float *buf, int n_heads, int head_dim, float 
 	s.end(v7g_rmsnorm_rope_rows((float *)s.dev(ib), nullptr, 1, n_heads, 0, head_dim, (const float *)s.dev(iw), nullptr, c, sn, pos, 0, *v7g_rms_eps_slot(), s.stream()));
 }
 
+V7_ABI void v7s_rope_only_heads(float *buf, int n_heads, int head_dim, float *cos_table, float *sin_table, int pos, int rope_max_dim)
+{
+	std::lock_guard<std::mutex> lock(g_mutex);
+	if (n_heads < 0 || head_dim < 32 || head_dim > 1024 || head_dim % 32 != 0 || pos < 0 || rope_max_dim < 0) {
+		die("v7s_rope_only_heads: n_heads %d, head_dim %d, pos %d, rope_max_dim %d break the contract (head_dim %% 32 == 0, 32 <= head_dim <= 1024)", n_heads, head_dim, pos, rope_max_dim);
+		return;
+	}
+	if (n_heads == 0 || pos == 0) // position 0 is the identity (rope_only_kernel.inc:13-14)
+		return;
+	const size_t half_b = (size_t)(head_dim / 2) * sizeof(float);
+	Stager s;
+	int ib = s.add(buf, (size_t)head_dim * sizeof(float) * (size_t)n_heads, true, true);
+	int ic = s.add(cos_table + (size_t)pos * rope_max_dim, half_b, true, false);
+	int is = s.add(sin_table + (size_t)pos * rope_max_dim, half_b, true, false);
+	if (!s.begin("v7s_rope_only_heads"))
+		return;
+	s.end(v7g_rope_only_rows((float *)s.dev(ib), nullptr, 1, n_heads, 0, head_dim, (const float *)s.dev(ic), (const float *)s.dev(is), pos, 0, s.stream()));
+}
+
+V7_ABI void v7s_qk_fork_heads(const v7_qk_fork_args *a)
+{
+	std::lock_guard<std::mutex> lock(g_mutex);
+	if (!a) {
+		die("v7s_qk_fork_heads: NULL descriptor");
+		return;
+	}
+	const int head_dim = a->head_dim, heads = a->heads, pos = a->pos;
+	if (heads < 0 || head_dim < 32 || head_dim > 1024 || head_dim % 32 != 0 || pos < 0) {
+		die("v7s_qk_fork_heads: heads %d, head_dim %d, pos %d break the contract (head_dim %% 32 == 0, 32 <= head_dim <= 1024)", heads, head_dim, pos);
+		return;
+	}
+	if (heads == 0)
+		return;
+	const size_t hb = (size_t)head_dim * sizeof(float);
+	const size_t half_b = hb / 2;
+	Stager s;
+	int ib = s.add(a->buf, hb * (size_t)heads, true, true), iw = s.add(a->weight, hb, true, false);
+	int ic = -1, is = -1;
+	if (pos != 0) { // the descriptor's tables are already offset to the position's row
+		ic = s.add(a->cos, half_b, true, false);
+		is = s.add(a->sin, half_b, true, false);
+	}
+	if (!s.begin("v7s_qk_fork_heads"))
+		return;
+	const float *c = ic >= 0 ? (const float *)s.dev(ic) : nullptr;
+	const float *sn = is >= 0 ? (const float *)s.dev(is) : nullptr;
+	s.end(v7g_rmsnorm_rope_rows((float *)s.dev(ib), nullptr, 1, heads, 0, head_dim, (const float *)s.dev(iw), nullptr, c, sn, pos, 0, *v7g_rms_eps_slot(), s.stream()));
+}
+
 V7_ABI void v7d_quantize(char *out_q, float *in_x, float *out_s, int n)
 {
 	std::lock_guard<std::mutex> lock(g_mutex);
@@ -493,10 +549,113 @@ V7_ABI void v7_do_fatal(const char *message)
 	die("%s", message ? message : "v7_do_fatal");
 }
 
-// The reference builds internal RoPE tables here for its fused QKV matmul,
-// which this library does not provide; the kernels here take caller tables.
-V7_ABI void v7s_rope_init(int head_dim, float rope_base) {}
-V7_ABI void v7s_set_fused_rope(int pos, int head_dim) {}
+namespace {
+// ht_find_or_fatal of the reference (a missing key is fatal): the value of a
+// 4-byte key, or false with the engine marked dead.
+bool find_key4(const char *key, void *out)
+{
+	unsigned long long len = 0;
+	void *p = store_find(key, &len);
+	if (!p || len < 4) {
+		die("v7s_rope_init: key %s not found", key);
+		return false;
+	}
+	memcpy(out, p, 4);
+	return true;
+}
+} // namespace
+
+// Frequencies on the host (x87, as the reference), the [131072, half] tables
+// on the current device, kept for v7g_get_rope_tables and the engine's calls.
+// Caller holds g_mutex.  Returns a v7g status with the error recorded.
+int rope_init_locked(int head_dim, float base, int scaling, float factor, float high, float low, int orig)
+{
+	using v7g::set_error;
+	if (head_dim <= 0 || head_dim % 2 != 0 || head_dim / 2 > 256)
+		return set_error(V7G_ERR_ARG, "rope init: head_dim %d must be even and at most 512", head_dim);
+	const int half = head_dim / 2;
+	double freqs[256];
+	int rc = v7g_rope_freqs(freqs, half, base, scaling, factor, high, low, orig);
+	if (rc != V7G_OK)
+		return rc;
+	int dev = -1;
+	DeviceCtx *c = nullptr;
+	if (cudaGetDevice(&dev) != cudaSuccess || ensure_ctx(dev, 0, &c) != 0) {
+		cudaGetLastError();
+		return set_error(V7G_ERR_NO_DEVICE, "rope init: no CUDA device");
+	}
+	if (c->rope_half != half || !c->rope_cos) {
+		cudaFree(c->rope_cos);
+		cudaFree(c->rope_sin);
+		c->rope_cos = c->rope_sin = nullptr;
+		c->rope_half = 0;
+		const size_t bytes = (size_t)V7G_ROPE_TABLE_POSITIONS * half * sizeof(float);
+		if (cudaMalloc(&c->rope_cos, bytes) != cudaSuccess || cudaMalloc(&c->rope_sin, bytes) != cudaSuccess) {
+			cudaGetLastError();
+			cudaFree(c->rope_cos);
+			c->rope_cos = nullptr;
+			return set_error(V7G_ERR_CUDA, "rope init: cannot allocate the RoPE tables on device %d", dev);
+		}
+	}
+	c->rope_half = 0; // unusable until the build below has finished
+	rc = v7g_rope_tables(c->rope_cos, c->rope_sin, 0, V7G_ROPE_TABLE_POSITIONS, half, half, freqs, c->stream);
+	if (rc != V7G_OK)
+		return rc;
+	cudaError_t e = cudaStreamSynchronize(c->stream);
+	if (e != cudaSuccess) {
+		cudaGetLastError();
+		return set_error(V7G_ERR_CUDA, "rope init: table build failed: %s", cudaGetErrorString(e));
+	}
+	c->rope_half = half;
+	return v7g::clear_error();
+}
+
+V7_ABI void v7s_rope_init(int head_dim, float rope_base)
+{
+	std::lock_guard<std::mutex> lock(g_mutex);
+	g_fused_head_dim = head_dim;
+	float base, factor = 0, high = 0, low = 0;
+	int type, orig = 0;
+	if (!find_key4("__sys_rope_base", &base) || !find_key4("__sys_rope_type", &type))
+		return;
+	if (type == 1 && (!find_key4("__sys_rope_factor", &factor) || !find_key4("__sys_rope_high_freq_factor", &high) ||
+	                  !find_key4("__sys_rope_low_freq_factor", &low) || !find_key4("__sys_rope_orig_max_pos", &orig)))
+		return;
+	if (rope_init_locked(head_dim, base, type == 1 ? 1 : 0, factor, high, low, orig) != V7G_OK)
+		die("v7s_rope_init: %s", v7g_last_error());
+}
+
+int v7g_rope_init(int head_dim, float base, int scaling, float factor, float high_freq_factor, float low_freq_factor, int orig_max_pos)
+{
+	std::lock_guard<std::mutex> lock(g_mutex);
+	return rope_init_locked(head_dim, base, scaling, factor, high_freq_factor, low_freq_factor, orig_max_pos);
+}
+
+// The position and head size of the reference's fused QKV matmul (which
+// this library does not provide) are recorded, nothing more.
+V7_ABI void v7s_set_fused_rope(int pos, int head_dim)
+{
+	std::lock_guard<std::mutex> lock(g_mutex);
+	g_fused_pos = pos;
+	g_fused_head_dim = head_dim;
+}
+
+int v7g_get_rope_tables(const float **cos_table, const float **sin_table, int *half)
+{
+	std::lock_guard<std::mutex> lock(g_mutex);
+	int dev = -1;
+	if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices || g_ctx[dev].rope_half == 0) {
+		cudaGetLastError();
+		return v7g::set_error(V7G_ERR_ARG, "v7g_get_rope_tables: v7s_rope_init has built no tables on this device");
+	}
+	if (cos_table)
+		*cos_table = g_ctx[dev].rope_cos;
+	if (sin_table)
+		*sin_table = g_ctx[dev].rope_sin;
+	if (half)
+		*half = g_ctx[dev].rope_half;
+	return v7g::clear_error();
+}
 // Worker spin policy of the CPU pool: nothing spins on the GPU path.
 V7_ABI void v7s_set_spin(int flag) {}
 V7_ABI void v7s_enable_thinking(int on) {}
@@ -521,13 +680,15 @@ V7_ABI void v7s_shutdown(void)
 	cudaGetDevice(&cur);
 	for (int d = 0; d < kMaxDevices; ++d) {
 		DeviceCtx &c = g_ctx[d];
-		if (!c.stream && !c.work)
+		if (!c.stream && !c.work && !c.rope_cos)
 			continue;
 		cudaSetDevice(d);
 		if (c.stream)
 			cudaStreamSynchronize(c.stream);
 		if (c.work)
 			cudaFree(c.work);
+		cudaFree(c.rope_cos);
+		cudaFree(c.rope_sin);
 		if (c.stream)
 			cudaStreamDestroy(c.stream);
 		c = DeviceCtx();

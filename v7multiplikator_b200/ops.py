@@ -12,7 +12,7 @@ Two families mirror the reference's operator interface:
   of v7's per-vector kernels, one launch for all rows;
 * per-vector ops named after the reference exports (``v7s_rmsnorm``,
   ``v7s_add_inplace``, ``v7s_fused_add_rmsnorm``, ``v7s_rmsnorm_rope_heads``,
-  ``v7d_quantize``, ``v7s_rmsnorm_quantize``) with the reference's argument
+  ``v7s_rope_only_heads``, ``v7d_quantize``, ``v7s_rmsnorm_quantize``) with the reference's argument
   meaning (src/v7_lib.h:123-124, :270-273): one vector or one token per call,
   RMS epsilon taken from the library global (``set_rms_eps``), like the
   reference's BSS ``g_rms_eps``.
@@ -55,7 +55,16 @@ _SIGNATURES = {
     "v7g_rmsnorm_quantize_rows": [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_float, c_void_p],
     "v7g_fill_normal": [c_void_p, c_int64, c_int64, c_int64, c_uint64, c_float, c_float, c_void_p],
     "v7g_selftest_arith": [c_void_p, c_void_p],
+    "v7g_rope_only_rows": [c_void_p, c_void_p, c_int64, c_int, c_int, c_int, c_void_p, c_void_p, c_int64, c_int,
+                           c_void_p],
+    "v7g_rope_freqs": [c_void_p, c_int, c_float, c_int, c_float, c_float, c_float, c_int],
+    "v7g_rope_tables": [c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_void_p, c_void_p],
+    "v7g_rope_init": [c_int, c_float, c_int, c_float, c_float, c_float, c_int],
+    "v7g_get_rope_tables": [c_void_p, c_void_p, c_void_p],
 }
+
+# Positions of the tables rope_init builds (V7G_ROPE_TABLE_POSITIONS).
+ROPE_TABLE_POSITIONS = 131072
 
 _lib: Optional[ctypes.CDLL] = None
 
@@ -153,9 +162,24 @@ def rmsnorm_rope_rows(q: Optional[torch.Tensor], k: Optional[torch.Tensor], wq: 
     may be None); token t is at position pos0 + t and uses row pos0 + t of the
     [positions, rope_max_dim] cos/sin tables (v7s_rmsnorm_rope_heads on Q then K
     per token, rmsnorm_rope_dispatch.inc:11-52)."""
+    shape = _qk_shape(q, k, cos_table, sin_table, pos0)
+    if shape is None:
+        return
+    ref, tokens, head_dim = shape
+    d = ref.device
+    _check(lib().v7g_rmsnorm_rope_rows(
+        _want(q, "q", torch.float32, d), _want(k, "k", torch.float32, d), tokens,
+        q.shape[1] if q is not None else 0, k.shape[1] if k is not None else 0, head_dim,
+        _want(wq, "wq", torch.float32, d), _want(wk, "wk", torch.float32, d),
+        _want(cos_table, "cos_table", torch.float32, d), _want(sin_table, "sin_table", torch.float32, d),
+        pos0, cos_table.shape[1], eps, _stream(ref, stream)))
+
+
+def _qk_shape(q: Optional[torch.Tensor], k: Optional[torch.Tensor], cos_table: torch.Tensor,
+              sin_table: torch.Tensor, pos0: int):
     ref = q if q is not None else k
     if ref is None:
-        return
+        return None
     if ref.dim() != 3:
         raise ValueError("q/k must be [tokens, heads, head_dim]")
     tokens, _, head_dim = ref.shape
@@ -168,13 +192,82 @@ def rmsnorm_rope_rows(q: Optional[torch.Tensor], k: Optional[torch.Tensor], wq: 
         raise ValueError("cos/sin tables have fewer rows than pos0 + tokens")
     if cos_table.shape[1] < head_dim // 2:
         raise ValueError("cos/sin table rows must hold at least head_dim/2 entries")
+    return ref, tokens, head_dim
+
+
+def rope_only_rows(q: Optional[torch.Tensor], k: Optional[torch.Tensor], cos_table: torch.Tensor,
+                   sin_table: torch.Tensor, pos0: int, stream: Optional[torch.cuda.Stream] = None) -> None:
+    """NeoX RoPE without the norm, in place (v7s_rope_only_heads on Q then K per
+    token, rope_only_kernel.inc:11-53).  Same layout and tables as
+    rmsnorm_rope_rows; tokens at position 0 are left untouched."""
+    shape = _qk_shape(q, k, cos_table, sin_table, pos0)
+    if shape is None:
+        return
+    ref, tokens, head_dim = shape
     d = ref.device
-    _check(lib().v7g_rmsnorm_rope_rows(
+    _check(lib().v7g_rope_only_rows(
         _want(q, "q", torch.float32, d), _want(k, "k", torch.float32, d), tokens,
         q.shape[1] if q is not None else 0, k.shape[1] if k is not None else 0, head_dim,
-        _want(wq, "wq", torch.float32, d), _want(wk, "wk", torch.float32, d),
         _want(cos_table, "cos_table", torch.float32, d), _want(sin_table, "sin_table", torch.float32, d),
-        pos0, cos_table.shape[1], eps, _stream(ref, stream)))
+        pos0, cos_table.shape[1], _stream(ref, stream)))
+
+
+def _scaling_args(scaling: Optional[dict]):
+    if not scaling:
+        return 0, 0.0, 0.0, 0.0, 0
+    return (1, float(scaling["factor"]), float(scaling["high_freq_factor"]), float(scaling["low_freq_factor"]),
+            int(scaling["orig_max_pos"]))
+
+
+def rope_freqs(half: int, base: float, scaling: Optional[dict] = None):
+    """freqs[j] = base^(-j/half) (float64, host) as the reference's x87 table
+    builder computes them (fused_f32_kernel.inc:117-147); scaling = None or a
+    llama3 dict {"factor", "high_freq_factor", "low_freq_factor",
+    "orig_max_pos"} (:149-256)."""
+    import numpy as np
+    f = np.empty(half, np.float64)
+    _check(lib().v7g_rope_freqs(f.ctypes.data, half, base, *_scaling_args(scaling)))
+    return f
+
+
+def rope_tables(positions: int, half: int, base: float, stride: Optional[int] = None, pos0: int = 0,
+                scaling: Optional[dict] = None, device: Optional[torch.device] = None,
+                stream: Optional[torch.cuda.Stream] = None):
+    """cos, sin [positions, stride] fp32 on the device for positions
+    pos0..pos0+positions-1: the reference's x87 tables, computed by the
+    library's table kernel (columns half.. zero)."""
+    import numpy as np
+    stride = stride or half
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    freqs = np.ascontiguousarray(rope_freqs(half, base, scaling))
+    cos = torch.empty(positions, stride, dtype=torch.float32, device=device)
+    sin = torch.empty_like(cos)
+    _check(lib().v7g_rope_tables(_want(cos, "cos", torch.float32, device), _want(sin, "sin", torch.float32, device),
+                                 pos0, positions, half, stride, freqs.ctypes.data, _stream(cos, stream)))
+    return cos, sin
+
+
+class _DeviceView:
+    """A __cuda_array_interface__ view of library-owned device memory."""
+
+    def __init__(self, ptr: int, shape: tuple, typestr: str):
+        self.__cuda_array_interface__ = {"data": (ptr, False), "shape": shape, "typestr": typestr, "version": 3,
+                                         "strides": None}
+
+
+def rope_init(head_dim: int, base: float, scaling: Optional[dict] = None):
+    """Builds the library's own RoPE tables [ROPE_TABLE_POSITIONS, head_dim/2]
+    on the current device (what v7s_rope_init does from the key store) and
+    returns (cos, sin) tensors viewing them; the library owns the memory
+    until v7s_shutdown or the next rope_init with another head size."""
+    L = lib()
+    _check(L.v7g_rope_init(head_dim, base, *_scaling_args(scaling)))
+    c, s, h = c_void_p(), c_void_p(), c_int()
+    _check(L.v7g_get_rope_tables(ctypes.byref(c), ctypes.byref(s), ctypes.byref(h)))
+    shape = (ROPE_TABLE_POSITIONS, h.value)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    return (torch.as_tensor(_DeviceView(c.value, shape, "<f4"), device=dev),
+            torch.as_tensor(_DeviceView(s.value, shape, "<f4"), device=dev))
 
 
 def swiglu(out: torch.Tensor, gate: torch.Tensor, up: torch.Tensor,
@@ -284,6 +377,17 @@ def v7s_rmsnorm_rope_heads(buf: torch.Tensor, n_heads: int, head_dim: int, norm_
         _want(buf, "buf", torch.float32, d), 0, 1, n_heads, 0, head_dim, _want(norm_weight, "norm_weight", torch.float32, d),
         0, _want(ct, "cos_table", torch.float32, d), _want(st, "sin_table", torch.float32, d), pos, rope_max_dim,
         get_rms_eps(), _stream(buf, None)))
+
+
+def v7s_rope_only_heads(buf: torch.Tensor, n_heads: int, head_dim: int, cos_table: torch.Tensor,
+                        sin_table: torch.Tensor, pos: int, rope_max_dim: int) -> None:
+    """rope_only_dispatch.inc:10-47 -- one token's n_heads heads at position pos."""
+    ct = cos_table.view(-1, rope_max_dim)
+    st = sin_table.view(-1, rope_max_dim)
+    d = buf.device
+    _check(lib().v7g_rope_only_rows(
+        _want(buf, "buf", torch.float32, d), 0, 1, n_heads, 0, head_dim, _want(ct, "cos_table", torch.float32, d),
+        _want(st, "sin_table", torch.float32, d), pos, rope_max_dim, _stream(buf, None)))
 
 
 def v7d_quantize(out_q: torch.Tensor, in_x: torch.Tensor, out_s: torch.Tensor) -> None:
