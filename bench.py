@@ -18,8 +18,8 @@ Reported (one JSON line from rank 0):
   roofline   the kernel's achieved GB/s against the measured HBM copy peak
   cpu_baseline  the oracle port on the host cores, bounded sample (N=1 only)
   kernels    the other BASELINE configs (C1-C4) and the next rows (add_inplace,
-             RMSNorm->Q8, RoPE without the norm, the RoPE table build),
-             device-timed, N=1 only
+             RMSNorm->Q8, RoPE without the norm, the RoPE table build, the
+             Q8-weight GEMVs), device-timed, N=1 only
 ``--impl reference`` times the CPU implementation instead (rank 0 only).
 """
 from __future__ import annotations
@@ -357,8 +357,8 @@ def run_e2e(args, v7g, dev, g, u, codes, scales, rows, world):
 
 def kernel_table(v7g, dev, stream, peak) -> dict:
     """Device-timed GB/s of the other BASELINE configs on one GPU, median of 50
-    launches.  Configs whose inputs fit in L2 (C1, C2 and the add / RMSNorm->Q8
-    rows at the C2 shape) flush L2 before every launch."""
+    launches.  Configs whose inputs fit in L2 (C1, C2, C3 and the add,
+    RMSNorm->Q8 and RoPE-only rows) flush L2 before every launch."""
     out = {}
     # 512 MB written + 512 MB read (each > 4x L2) before every flushed launch
     flush = (torch.zeros(128 * 2**20, device=dev), torch.zeros(1024, 128 * 1024, device=dev),
@@ -402,11 +402,12 @@ def kernel_table(v7g, dev, stream, peak) -> dict:
     wq = fill((1, 128), 8, 1.0, 0.1)[0]
     wk = fill((1, 128), 9, 1.0, 0.1)[0]
     cos, sin = v7g.rope_tables(8192, 64, 1e6, device=dev)
+    # Q + K are 100.7 MB, under the 126 MB L2: flushed
     rec("c3_rmsnorm_rope_8192x(16+8)x128", lambda: v7g.rmsnorm_rope_rows(q, k, wq, wk, cos, sin, 0, 1e-6, stream=stream),
-        8192 * 24 * 128 * 8 + 8192 * 64 * 8 + 2 * 128 * 4, 8192, False)
+        8192 * 24 * 128 * 8 + 8192 * 64 * 8 + 2 * 128 * 4, 8192, True)
     # RoPE without the norm at the C3 geometry
     rec("rope_only_8192x(16+8)x128", lambda: v7g.rope_only_rows(q, k, cos, sin, 0, stream=stream),
-        8192 * 24 * 128 * 8 + 8192 * 64 * 8, 8192, False)
+        8192 * 24 * 128 * 8 + 8192 * 64 * 8, 8192, True)
     del q, k
     # the reference's internal tables: 131072 positions x 64 pairs, cos + sin written
     tc = torch.empty(131072, 64, device=dev)
@@ -421,12 +422,49 @@ def kernel_table(v7g, dev, stream, peak) -> dict:
     uu = fill((4096, 8192), 11, 0.0, 2.0)
     oo = torch.empty_like(gg)
     rec("c4_swiglu_4096x8192", lambda: v7g.swiglu(oo, gg, uu, stream=stream), 4096 * 8192 * 12, 4096, False)
+    # Q8-weight GEMVs (decode, batch 1) at model shapes; weights under L2 size: flushed
+    for n, d in ((2048, 8192), (4096, 12288)):
+        xq, xs, gq, gs, uq, us = gemv_inputs(dev, n, d)
+        y = torch.empty(1, d, device=dev)
+        rec(f"swiglu_q8_gemv_{n}x{d}", lambda: v7g.swiglu_q8_gemv(y, xq, xs, gq, gs, uq, us, stream=stream),
+            2 * d * (n + n // 16) + n + n // 16 + 4 * d, d, True)
+        if n == 2048:
+            xf = fill((1, n), 14, 0.0, 1.0)
+            rec(f"swiglu_f32q8_gemv_{n}x{d}", lambda: v7g.swiglu_f32q8_gemv(y, xf, gq, gs, uq, us, stream=stream),
+                2 * d * (n + n // 16) + 4 * n + 4 * d, d, True)
+        del gq, gs, uq, us
+    xq, xs, wq, ws, _, _ = gemv_inputs(dev, 8192, 2048, both=False)
+    y = torch.empty(1, 2048, device=dev)
+    rec("q8_gemv_8192x2048", lambda: v7g.q8_gemv(y, xq, xs, wq, ws, stream=stream),
+        2048 * (8192 + 8192 // 16) + 8192 + 8192 // 16 + 4 * 2048, 2048, True)
+    xf = fill((1, 8192), 15, 0.0, 1.0)
+    rec("q8_fused_gemv_8192x2048", lambda: v7g.q8_fused_gemv(y, xf, wq, ws, stream=stream),
+        2048 * (8192 + 8192 // 16) + 4 * 8192 + 4 * 2048, 2048, True)
+    del wq, ws
     # RMSNorm -> Q8 at the C2 shape
     codes = torch.empty(4096, 2048, dtype=torch.int8, device=dev)
     sc = torch.empty(4096, 32, device=dev)
     rec("rmsnorm_quantize_4096x2048", lambda: v7g.rmsnorm_quantize_rows(codes, sc, r, w, 1e-6, stream=stream),
         4096 * (2048 * 5 + 32 * 4) + 2048 * 4, 4096, True)
     return out
+
+
+def gemv_inputs(dev, n: int, d: int, both: bool = True):
+    """Random Q8 activation and weights for a GEMV: codes uniform in
+    [-127, 127], scales uniform in [0.001, 0.02)."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(n * 31 + d)
+
+    def codes(*shape):
+        return torch.randint(-127, 128, shape, generator=g, device=dev, dtype=torch.int8)
+
+    def scales(*shape):
+        return torch.rand(*shape, generator=g, device=dev) * 0.019 + 0.001
+
+    xq, xs = codes(1, n), scales(1, n // 64)
+    gq, gs = codes(d, n), scales(d, n // 64)
+    uq, us = (codes(d, n), scales(d, n // 64)) if both else (None, None)
+    return xq, xs, gq, gs, uq, us
 
 
 def cpu_baseline(args) -> dict:
@@ -542,6 +580,16 @@ def _profile_case(name: str, rows: int, dev):
         if name == "rope_only":
             return lambda: v7g.rope_only_rows(q, k, cos, sin, 0), rows * (24 * 128 * 8 + 64 * 8)
         return lambda: v7g.rmsnorm_rope_rows(q, k, wq, wk, cos, sin, 0, 1e-6), rows * (24 * 128 * 8 + 64 * 8)
+    if name in ("swiglu_q8_gemv", "swiglu_f32q8_gemv", "q8_gemv"):
+        n = 4096 if name != "swiglu_f32q8_gemv" else 2048
+        xq, xs, gq, gs, uq, us = gemv_inputs(dev, n, rows)
+        y = torch.empty(1, rows, device=dev)
+        if name == "q8_gemv":
+            return lambda: v7g.q8_gemv(y, xq, xs, gq, gs), rows * (n + n // 16)
+        if name == "swiglu_q8_gemv":
+            return lambda: v7g.swiglu_q8_gemv(y, xq, xs, gq, gs, uq, us), 2 * rows * (n + n // 16)
+        xf = fill((1, n), 14, 0.0, 1.0)
+        return lambda: v7g.swiglu_f32q8_gemv(y, xf, gq, gs, uq, us), 2 * rows * (n + n // 16)
     if name == "rope_tables":
         tc = torch.empty(rows, 64, device=dev)
         ts = torch.empty_like(tc)
@@ -552,7 +600,7 @@ def _profile_case(name: str, rows: int, dev):
 
 
 PROFILE_CASES = ("swiglu_q8", "swiglu", "rmsnorm", "fused_add_rmsnorm", "add_inplace", "rmsnorm_quantize", "rmsnorm_rope",
-                 "rope_only", "rope_tables")
+                 "rope_only", "rope_tables", "swiglu_q8_gemv", "swiglu_f32q8_gemv", "q8_gemv")
 
 
 def run_profile(args) -> None:

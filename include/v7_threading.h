@@ -70,6 +70,18 @@ V7_ABI void v7d_quantize(char *out_q, float *in_x, float *out_s, int n);
    n % 64 == 0. */
 V7_ABI void v7s_rmsnorm_quantize(char *out_q, float *in_x, float *out_s, int n, float *weight);
 
+/* src/v7_lib.h:113; q8_kernel.inc:84-207, matmul_dispatch.inc.  xout[i] =
+   dot(x, row i of w) for i < d: Q8 activation (x->q [n], x->s [n/64]) times Q8
+   weights (w->q [d, n], w->s [d, n/64]); n % 64 == 0. */
+V7_ABI void v7d_q8(float *xout, v7_q8_tensor *x, v7_q8_tensor *w, int n, int d);
+/* src/v7_lib.h:116; swiglu_kernel.inc, fused_dispatch.inc:27-57.  xout[i] =
+   swiglu(dot(x, gate row i), dot(x, up row i)), fp32 activation x->data [n];
+   n % 64 == 0.  Arithmetic of the reference's dual-row path. */
+V7_ABI void v7d_swiglu(float *xout, v7_f32_tensor *x, v7_q8_tensor *gate_w, int n, int d, v7_q8_tensor *up_w);
+/* src/v7_lib.h:117; swiglu_q8_kernel.inc:16-286.  As v7d_swiglu with a Q8
+   activation; n % 64 == 0. */
+V7_ABI void v7d_swiglu_q8(float *xout, v7_q8_tensor *x, v7_q8_tensor *gate_w, int n, int d, v7_q8_tensor *up_w);
+
 /* ---- engine-internal kernels ------------------------------------------- */
 /* The reference links these statically into its forward pass; they are not
    among the names v7_load resolves.  Exported here under the same names and

@@ -1,9 +1,9 @@
-/* v7_threading_stubs.h -- the 64 reference exports outside the kernel path.
+/* v7_threading_stubs.h -- the 61 reference exports outside the kernel path.
  *
  * v7_load (src/v7_lib.h:585-739) refuses a library that lacks any of its 99
  * names, so these are exported too.  They belong to subsystems this library
  * does not provide (model forward passes, chat/generate, sampler, tokenizer,
- * matmul and attention kernels, vision, SectorLogo, KV-cache files,
+ * the fp32-activation matmuls and attention kernels, vision, SectorLogo, KV-cache files,
  * MicroDB compression, the cycle tuner).  Each one marks the engine dead with
  * the reason "<name>: not provided by v7g" (v7_engine_is_dead() = 1, the
  * reference's FATAL contract, src/v7_lib.h:179-184) and returns the value
@@ -26,11 +26,8 @@ extern "C" {
 extern unsigned long long v7g_zero_block[16];
 
 #define V7G_STUBS_VOID(X) \
-	X(v7d_q8, (float *xout, v7_q8_tensor *x, v7_q8_tensor *w, int n, int d))                                        /* :113 */ \
 	X(v7d_f32, (float *xout, v7_f32_tensor *x, v7_q8_tensor *w, int n, int d))                                      /* :114 */ \
 	X(v7d_fused_f32, (float *xout, v7_f32_tensor *x, v7_q8_tensor *w, int n, int d, float *norm_weights, int is_q)) /* :115 */ \
-	X(v7d_swiglu, (float *xout, v7_f32_tensor *x, v7_q8_tensor *gate_w, int n, int d, v7_q8_tensor *up_w))          /* :116 */ \
-	X(v7d_swiglu_q8, (float *xout, v7_q8_tensor *x, v7_q8_tensor *gate_w, int n, int d, v7_q8_tensor *up_w))        /* :117 */ \
 	X(v7d_attention, (struct v7_run_state *s, struct v7_config *p, int pos, unsigned long long loff, int kv_dim, int kv_mul)) /* :119 */ \
 	X(v7d_attention_prefill, (struct v7_run_state *s, struct v7_config *p, float *q_storage, float *att_out_storage, int start_pos, int n_tokens, unsigned long long loff, int kv_dim, int kv_mul)) /* :121 */ \
 	X(v7d_memcpy, (void *dst, void *src, int byte_count))                                                         /* :125 */ \

@@ -125,6 +125,33 @@ int v7g_rope_init(int head_dim, float base, int scaling, float factor, float hig
    library (freed by v7s_shutdown).  V7G_ERR_ARG when none was built. */
 int v7g_get_rope_tables(const float **cos_table, const float **sin_table, int *half);
 
+/* ---- Q8-weight matrix-vector products ----------------------------------
+   Weights: codes [d, n] int8 row-major (4-byte aligned) + scales [d, n/64]
+   fp32, one per 64-element group of a row (src/q8_batch4.h:15-19).  batch
+   activation vectors of n; out [batch, d] fp32.  Contract: n > 0,
+   n % 64 == 0, n <= 65536, batch <= 65535.  Weight bytes in [-127, 127] (the
+   exporter's contract); a -128 weight is multiplied as the reference's
+   vpsignb forms it.  Every output equals the reference's bit for bit. */
+
+/* v7d_q8 (src/v7_lib.h:113, q8_kernel.inc:84-207): out[b, i] = dot(x_b, w_i),
+   x Q8: codes [batch, n] (16-byte aligned) + scales [batch, n/64]. */
+int v7g_q8_gemv(float *out, const int8_t *xq, const float *xs, const int8_t *wq, const float *ws, int64_t batch, int n, int d, void *stream);
+
+/* v7d_q8_fused (fused_dispatch.inc:82-114): each fp32 activation x [batch, n]
+   quantised with v7d_quantize's rules, then v7d_q8 -- in one kernel. */
+int v7g_q8_fused_gemv(float *out, const float *x, const int8_t *wq, const float *ws, int64_t batch, int n, int d, void *stream);
+
+/* v7d_swiglu_q8 (src/v7_lib.h:117, swiglu_q8_kernel.inc:16-286):
+   out[b, i] = swiglu(dot(x_b, gate_i), dot(x_b, up_i)), Q8 activation. */
+int v7g_swiglu_q8_gemv(float *out, const int8_t *xq, const float *xs, const int8_t *gate_q, const float *gate_s, const int8_t *up_q, const float *up_s, int64_t batch, int n, int d, void *stream);
+
+/* v7d_swiglu (src/v7_lib.h:116, swiglu_kernel.inc): fp32 activation x
+   [batch, n] times Q8 gate/up, SwiGLU epilogue, with the arithmetic of the
+   reference's dual-row path (every row of an even-sized work chunk; the
+   reference's single-row path for the last row of an odd-sized chunk groups
+   the sums differently and can differ in the last bits). */
+int v7g_swiglu_f32q8_gemv(float *out, const float *x, const int8_t *gate_q, const float *gate_s, const int8_t *up_q, const float *up_s, int64_t batch, int n, int d, void *stream);
+
 /* ---- runtime ---------------------------------------------------------- */
 
 /* RMS epsilon used by the reference-ABI entries (v7s_rmsnorm & co.), which

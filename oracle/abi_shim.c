@@ -2,7 +2,7 @@
  *
  * TEST INFRASTRUCTURE ONLY.  Builds libv7_oracle_abi.so, which exports the 99
  * names the reference's loader resolves (src/v7_lib.h:585-739) with the ms_abi
- * convention, the six hot-path kernels computed by the oracle on host memory.
+ * convention, the hot-path kernels computed by the oracle on host memory.
  * Its one purpose: run the reference's own validators (tools/v_rmsnorm_validate,
  * v_add_inplace_validate, v_quantize_validate, built from the reference's
  * sources into oracle/_ref/) against the oracle, which pins the restatement to
@@ -63,6 +63,22 @@ V7_ABI void v7s_rmsnorm_quantize(char *out_q, float *in_x, float *out_s, int n, 
 {
 	if (orc_rmsnorm_quantize_rows((int8_t *)out_q, out_s, in_x, weight, 1, n, g_eps, 1) != 0)
 		die("v7s_rmsnorm_quantize: n % 64 != 0");
+}
+
+V7_ABI void v7d_q8(float *xout, v7_q8_tensor *x, v7_q8_tensor *w, int n, int d)
+{
+	if (orc_q8_gemv(xout, (const int8_t *)x->q, x->s, (const int8_t *)w->q, w->s, 1, n, d, 16) != 0)
+		die("v7d_q8: n % 64 != 0");
+}
+V7_ABI void v7d_swiglu(float *xout, v7_f32_tensor *x, v7_q8_tensor *gate_w, int n, int d, v7_q8_tensor *up_w)
+{
+	if (orc_swiglu_f32q8_gemv(xout, x->data, (const int8_t *)gate_w->q, gate_w->s, (const int8_t *)up_w->q, up_w->s, 1, n, d, 0, 16) != 0)
+		die("v7d_swiglu: n % 64 != 0");
+}
+V7_ABI void v7d_swiglu_q8(float *xout, v7_q8_tensor *x, v7_q8_tensor *gate_w, int n, int d, v7_q8_tensor *up_w)
+{
+	if (orc_swiglu_q8_gemv(xout, (const int8_t *)x->q, x->s, (const int8_t *)gate_w->q, gate_w->s, (const int8_t *)up_w->q, up_w->s, 1, n, d, 16) != 0)
+		die("v7d_swiglu_q8: n % 64 != 0");
 }
 
 V7_ABI int v7_init(const char *db_path) { return 1; }

@@ -51,6 +51,12 @@ class Oracle:
             "orc_rope_only_rows": [c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p, c_int64, c_int, c_int],
             "orc_rope_freqs": [c_void_p, c_int, c_float, c_int, c_float, c_float, c_float, c_int],
             "orc_rope_tables": [c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_void_p, c_int],
+            "orc_q8_gemv": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_int],
+            "orc_q8_fused_gemv": [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_int],
+            "orc_swiglu_q8_gemv": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int,
+                                   c_int, c_int],
+            "orc_swiglu_f32q8_gemv": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int,
+                                      c_int, c_int],
         }
         for name, args in sig.items():
             fn = getattr(L, name)
@@ -173,3 +179,47 @@ class Oracle:
         self._ok(self.lib.orc_rope_tables(_ptr(c), _ptr(s), pos0, positions, half, stride, _ptr(freqs),
                                           self.nthreads), "rope_tables")
         return c, s
+
+    # ---- Q8-weight GEMVs: activations [batch, n], weights [d, n] + [d, n/64]
+
+    @staticmethod
+    def _c(a, dt):
+        return np.ascontiguousarray(a, dt)
+
+    def q8_gemv(self, xq, xs, wq, ws) -> np.ndarray:
+        xq, xs, wq, ws = self._c(xq, np.int8), self._c(xs, np.float32), self._c(wq, np.int8), self._c(ws, np.float32)
+        batch, n = xq.reshape(-1, xq.shape[-1]).shape
+        d = wq.shape[0]
+        out = np.empty((batch, d), np.float32)
+        self._ok(self.lib.orc_q8_gemv(_ptr(out), _ptr(xq), _ptr(xs), _ptr(wq), _ptr(ws), batch, n, d, self.nthreads),
+                 "q8_gemv")
+        return out
+
+    def q8_fused_gemv(self, x, wq, ws) -> np.ndarray:
+        x, wq, ws = self._c(x, np.float32), self._c(wq, np.int8), self._c(ws, np.float32)
+        batch, n = x.reshape(-1, x.shape[-1]).shape
+        d = wq.shape[0]
+        out = np.empty((batch, d), np.float32)
+        self._ok(self.lib.orc_q8_fused_gemv(_ptr(out), _ptr(x), _ptr(wq), _ptr(ws), batch, n, d, self.nthreads),
+                 "q8_fused_gemv")
+        return out
+
+    def swiglu_q8_gemv(self, xq, xs, gq, gs, uq, us) -> np.ndarray:
+        xq, xs = self._c(xq, np.int8), self._c(xs, np.float32)
+        gq, gs, uq, us = self._c(gq, np.int8), self._c(gs, np.float32), self._c(uq, np.int8), self._c(us, np.float32)
+        batch, n = xq.reshape(-1, xq.shape[-1]).shape
+        d = gq.shape[0]
+        out = np.empty((batch, d), np.float32)
+        self._ok(self.lib.orc_swiglu_q8_gemv(_ptr(out), _ptr(xq), _ptr(xs), _ptr(gq), _ptr(gs), _ptr(uq), _ptr(us),
+                                             batch, n, d, self.nthreads), "swiglu_q8_gemv")
+        return out
+
+    def swiglu_f32q8_gemv(self, x, gq, gs, uq, us, single_row_path: bool = False) -> np.ndarray:
+        x = self._c(x, np.float32)
+        gq, gs, uq, us = self._c(gq, np.int8), self._c(gs, np.float32), self._c(uq, np.int8), self._c(us, np.float32)
+        batch, n = x.reshape(-1, x.shape[-1]).shape
+        d = gq.shape[0]
+        out = np.empty((batch, d), np.float32)
+        self._ok(self.lib.orc_swiglu_f32q8_gemv(_ptr(out), _ptr(x), _ptr(gq), _ptr(gs), _ptr(uq), _ptr(us), batch, n, d,
+                                                int(single_row_path), self.nthreads), "swiglu_f32q8_gemv")
+        return out

@@ -428,6 +428,87 @@ static void rope_table_row(float *cs, float *sn, int64_t pos, int half, int stri
 }
 
 /* ------------------------------------------------------------------------ */
+/* Q8-weight GEMVs                                                          */
+/* ------------------------------------------------------------------------ */
+
+/* One activation byte times one weight byte the way vpsignb + vpmaddubsw
+   form it (q8_kernel.inc:22-36, swiglu_q8_kernel.inc:16-33): the weight takes
+   the activation's sign (negated in 8 bits, so -128 stays -128; zero when the
+   activation is zero), times the activation's magnitude as an unsigned byte
+   (|-128| = 128).  Equal to a * w for every weight in [-127, 127], the
+   exporter's contract; no pair sum reaches the int16 saturation bound. */
+static inline int32_t x86_signmul(int8_t a, int8_t w)
+{
+	int32_t ua = a < 0 ? -(int32_t)a : (int32_t)a;
+	int8_t sw = a < 0 ? (int8_t)(uint8_t)(0u - (uint8_t)w) : (a == 0 ? 0 : w);
+	return ua * (int32_t)sw;
+}
+
+/* The 8 int32 lane dots of one 64-byte group: lane l sums bytes 4l..4l+3 of
+   the low 32 bytes and 4l..4l+3 of the high 32 (vpmaddwd pair-adds, then
+   vpaddd low + high). */
+static inline void q8_lane_dots(int32_t dot[8], const int8_t *a, const int8_t *w)
+{
+	for (int l = 0; l < 8; ++l) {
+		int32_t s = 0;
+		for (int k = 0; k < 4; ++k)
+			s += x86_signmul(a[4 * l + k], w[4 * l + k]) + x86_signmul(a[32 + 4 * l + k], w[32 + 4 * l + k]);
+		dot[l] = s;
+	}
+}
+
+/* Q8 x Q8 dot of one weight row with the activation: per group the lane dots
+   converted to float (exact), the weight scale times the activation scale
+   (rounded), one FMA per lane into 8 lane accumulators; HADD_YMM at the end
+   (q8_kernel.inc:141-162, 176-201). */
+static float q8_row_dot(const int8_t *xq, const float *xs, const int8_t *wq, const float *ws, int n)
+{
+	float acc[8] = { 0 };
+	int32_t dot[8];
+	for (int g = 0; g < n / ORC_Q8_GS; ++g) {
+		q8_lane_dots(dot, xq + (int64_t)g * ORC_Q8_GS, wq + (int64_t)g * ORC_Q8_GS);
+		float cs = ws[g] * xs[g];
+		for (int l = 0; l < 8; ++l)
+			acc[l] = fmaf((float)dot[l], cs, acc[l]);
+	}
+	return hadd8(acc);
+}
+
+/* fp32 activation x Q8 weight row, the dual-row arithmetic of
+   swiglu_kernel.inc:30-47,138-249: weight to float times the group scale
+   (rounded), one FMA per element into lane e % 8 of a single accumulator. */
+static float f32q8_row_dot_dual(const float *x, const int8_t *wq, const float *ws, int n)
+{
+	float acc[8] = { 0 };
+	for (int e = 0; e < n; ++e) {
+		float wf = (float)wq[e] * ws[e / ORC_Q8_GS];
+		acc[e % 8] = fmaf(x[e], wf, acc[e % 8]);
+	}
+	return hadd8(acc);
+}
+
+/* The same for the single-row path (the last row of an odd-sized work
+   chunk, swiglu_kernel.inc:253-375): four accumulators, 8-element block b
+   feeding accumulator b % 4 through the 256-element loop and the 64/32/16
+   tails, every later 8-element tail block accumulator 0; merged
+   (acc0 + acc1) + (acc2 + acc3) before HADD_YMM. */
+static float f32q8_row_dot_single(const float *x, const int8_t *wq, const float *ws, int n)
+{
+	float acc[4][8] = { { 0 } };
+	const int n256 = n / 256 * 256;
+	for (int e = 0; e < n; ++e) {
+		int a = e < n256 + 112 ? (e / 8) % 4 : 0;
+		float wf = (float)wq[e] * ws[e / ORC_Q8_GS];
+		acc[a][e % 8] = fmaf(x[e], wf, acc[a][e % 8]);
+	}
+	float s[8];
+	for (int l = 0; l < 8; ++l)
+		s[l] = (acc[0][l] + acc[1][l]) + (acc[2][l] + acc[3][l]);
+	return hadd8(s);
+}
+
+
+/* ------------------------------------------------------------------------ */
 /* row-parallel driver                                                       */
 /* ------------------------------------------------------------------------ */
 
@@ -450,9 +531,53 @@ typedef struct job {
 	int64_t pos0;
 	float eps;
 	const double *freqs;
+	/* GEMV: activation codes / scales (or fp32 activations in fx), weight
+	   matrices 1 (gate or the only one) and 2 (up) */
+	const int8_t *qin;
+	const float *sin_;
+	const int8_t *qw1, *qw2;
+	const float *sw1, *sw2;
+	int d, variant;
 } job;
 
-enum { K_RMSNORM, K_ADD_RMSNORM, K_ROPE, K_SWIGLU, K_QUANT, K_SWIGLU_Q8, K_ADD, K_RMSNORM_Q8, K_ROPE_ONLY, K_ROPE_TABLE };
+enum { K_RMSNORM, K_ADD_RMSNORM, K_ROPE, K_SWIGLU, K_QUANT, K_SWIGLU_Q8, K_ADD, K_RMSNORM_Q8, K_ROPE_ONLY, K_ROPE_TABLE,
+       K_Q8_GEMV, K_SWIGLU_Q8_GEMV, K_SWIGLU_F32Q8_GEMV, K_Q8_FUSED_GEMV };
+
+static void gemv_row(const job *j, int64_t r)
+{
+	const int64_t b = r / j->d, i = r % j->d;
+	const int n = j->n, ng = n / ORC_Q8_GS;
+	const int8_t *w1 = j->qw1 + i * (int64_t)n;
+	const float *s1 = j->sw1 + i * (int64_t)ng;
+	switch (j->kind) {
+	case K_Q8_GEMV:
+		j->fo[r] = q8_row_dot(j->qin + b * (int64_t)n, j->sin_ + b * (int64_t)ng, w1, s1, n);
+		break;
+	case K_Q8_FUSED_GEMV: {
+		int8_t xq[ORC_GEMV_MAX_N];
+		float xs[ORC_GEMV_MAX_N / ORC_Q8_GS];
+		quantize_vec(xq, xs, j->fx + b * (int64_t)n, n);
+		j->fo[r] = q8_row_dot(xq, xs, w1, s1, n);
+		break;
+	}
+	case K_SWIGLU_Q8_GEMV: {
+		const int8_t *xq = j->qin + b * (int64_t)n;
+		const float *xs = j->sin_ + b * (int64_t)ng;
+		float g = q8_row_dot(xq, xs, w1, s1, n);
+		float u = q8_row_dot(xq, xs, j->qw2 + i * (int64_t)n, j->sw2 + i * (int64_t)ng, n);
+		j->fo[r] = swiglu_v7(g, u);
+		break;
+	}
+	case K_SWIGLU_F32Q8_GEMV: {
+		const float *x = j->fx + b * (int64_t)n;
+		float (*dot)(const float *, const int8_t *, const float *, int) = j->variant ? f32q8_row_dot_single : f32q8_row_dot_dual;
+		float g = dot(x, w1, s1, n);
+		float u = dot(x, j->qw2 + i * (int64_t)n, j->sw2 + i * (int64_t)ng, n);
+		j->fo[r] = swiglu_v7(g, u);
+		break;
+	}
+	}
+}
 
 static void run_job(job *j)
 {
@@ -489,6 +614,12 @@ static void run_job(job *j)
 		}
 		case K_ROPE_TABLE: /* rows are positions; n = half, rope_max_dim = row stride */
 			rope_table_row(j->fo + r * j->rope_max_dim, j->fr + r * j->rope_max_dim, j->pos0 + r, j->n, j->rope_max_dim, j->freqs);
+			break;
+		case K_Q8_GEMV:
+		case K_Q8_FUSED_GEMV:
+		case K_SWIGLU_Q8_GEMV:
+		case K_SWIGLU_F32Q8_GEMV: /* rows are (batch, output row) pairs */
+			gemv_row(j, r);
 			break;
 		case K_SWIGLU: /* rows here are chunks of 4096 elements */
 		{
@@ -739,4 +870,80 @@ int orc_rope_only_rows(float *buf, int64_t tokens, int n_heads, int head_dim, co
 	j.pos0 = pos0;
 	j.rope_max_dim = rope_max_dim;
 	return run_rows(&j, tokens, nthreads);
+}
+
+static int gemv_args_ok(int64_t batch, int n, int d)
+{
+	return batch >= 0 && d >= 0 && n > 0 && n % ORC_Q8_GS == 0 && n <= ORC_GEMV_MAX_N;
+}
+
+int orc_q8_gemv(float *out, const int8_t *xq, const float *xs, const int8_t *wq, const float *ws, int64_t batch, int n, int d, int nthreads)
+{
+	if (!gemv_args_ok(batch, n, d))
+		return -1;
+	job j = { 0 };
+	j.kind = K_Q8_GEMV;
+	j.ftz = 1;
+	j.fo = out;
+	j.qin = xq;
+	j.sin_ = xs;
+	j.qw1 = wq;
+	j.sw1 = ws;
+	j.n = n;
+	j.d = d;
+	return run_rows(&j, batch * d, nthreads);
+}
+
+int orc_q8_fused_gemv(float *out, const float *x, const int8_t *wq, const float *ws, int64_t batch, int n, int d, int nthreads)
+{
+	if (!gemv_args_ok(batch, n, d))
+		return -1;
+	job j = { 0 };
+	j.kind = K_Q8_FUSED_GEMV;
+	j.ftz = 1;
+	j.fo = out;
+	j.fx = x;
+	j.qw1 = wq;
+	j.sw1 = ws;
+	j.n = n;
+	j.d = d;
+	return run_rows(&j, batch * d, nthreads);
+}
+
+int orc_swiglu_q8_gemv(float *out, const int8_t *xq, const float *xs, const int8_t *gq, const float *gs, const int8_t *uq, const float *us, int64_t batch, int n, int d, int nthreads)
+{
+	if (!gemv_args_ok(batch, n, d))
+		return -1;
+	job j = { 0 };
+	j.kind = K_SWIGLU_Q8_GEMV;
+	j.ftz = 1;
+	j.fo = out;
+	j.qin = xq;
+	j.sin_ = xs;
+	j.qw1 = gq;
+	j.sw1 = gs;
+	j.qw2 = uq;
+	j.sw2 = us;
+	j.n = n;
+	j.d = d;
+	return run_rows(&j, batch * d, nthreads);
+}
+
+int orc_swiglu_f32q8_gemv(float *out, const float *x, const int8_t *gq, const float *gs, const int8_t *uq, const float *us, int64_t batch, int n, int d, int single_row_path, int nthreads)
+{
+	if (!gemv_args_ok(batch, n, d))
+		return -1;
+	job j = { 0 };
+	j.kind = K_SWIGLU_F32Q8_GEMV;
+	j.ftz = 1;
+	j.fo = out;
+	j.fx = x;
+	j.qw1 = gq;
+	j.sw1 = gs;
+	j.qw2 = uq;
+	j.sw2 = us;
+	j.n = n;
+	j.d = d;
+	j.variant = single_row_path != 0;
+	return run_rows(&j, batch * d, nthreads);
 }

@@ -105,6 +105,32 @@ int orc_rope_freqs(double *freqs, int half, float base, int scaling, float facto
    fsincos, stored as fp32 (fused_f32_kernel.inc:257-302). */
 int orc_rope_tables(float *cos_table, float *sin_table, int64_t pos0, int64_t positions, int half, int stride, const double *freqs, int nthreads);
 
+/* ---- Q8-weight GEMVs (next rows 3 and 4) -------------------------------
+   Weights: codes [d, n] int8 row-major, scales [d, n/64]; activations: batch
+   vectors of n (codes [batch, n] + scales [batch, n/64], or fp32 [batch, n]);
+   out [batch, d].  Contract n % 64 == 0 (FATAL-guarded in the reference),
+   n <= ORC_GEMV_MAX_N.  FTZ+DAZ (dispatched kernels).  Weight bytes are
+   expected in [-127, 127] (the exporter's contract); -128 is multiplied the
+   way vpsignb forms it, as the reference does. */
+#define ORC_GEMV_MAX_N 65536
+
+/* v7d_q8 (q8_kernel.inc:84-207): out = sum of the 8 lane accumulators. */
+int orc_q8_gemv(float *out, const int8_t *xq, const float *xs, const int8_t *wq, const float *ws, int64_t batch, int n, int d, int nthreads);
+
+/* v7d_q8_fused (fused_dispatch.inc:82-114): v7d_quantize of each fp32
+   activation vector, then v7d_q8. */
+int orc_q8_fused_gemv(float *out, const float *x, const int8_t *wq, const float *ws, int64_t batch, int n, int d, int nthreads);
+
+/* v7d_swiglu_q8 (swiglu_q8_kernel.inc:16-286): gate and up Q8 x Q8 dots,
+   then (sigmoid(g) * g) * u with EVAL_SIGMOID. */
+int orc_swiglu_q8_gemv(float *out, const int8_t *xq, const float *xs, const int8_t *gq, const float *gs, const int8_t *uq, const float *us, int64_t batch, int n, int d, int nthreads);
+
+/* v7d_swiglu (swiglu_kernel.inc): fp32 activations x Q8 weights, then the
+   SwiGLU epilogue.  single_row_path = 0: the dual-row arithmetic (every row of
+   an even-sized work chunk); 1: the single-row arithmetic the reference uses
+   for the last row of an odd-sized chunk. */
+int orc_swiglu_f32q8_gemv(float *out, const float *x, const int8_t *gq, const float *gs, const int8_t *uq, const float *us, int64_t batch, int n, int d, int single_row_path, int nthreads);
+
 #ifdef __cplusplus
 }
 #endif

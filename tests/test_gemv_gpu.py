@@ -1,0 +1,123 @@
+"""The Q8-weight GEMVs on the GPU, through the C-ABI, bit for bit against the
+oracle: v7d_q8, v7d_q8_fused, v7d_swiglu_q8 and v7d_swiglu (dual-row
+arithmetic), at the reference validators' model shapes, ragged row counts,
+batches, and the contract's edges (-128 weights, extreme scales, NaN/inf in
+the fp32 activation of the fused quantiser)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from test_parity_gpu import assert_same_f32, dev, host
+from test_oracle_gemv import q8_case
+
+pytestmark = pytest.mark.gpu
+F = np.float32
+
+SHAPES = [(1024, 3072), (2048, 8192), (576, 1536), (960, 2560), (896, 4864), (64, 1), (128, 37), (4096, 100)]
+
+
+def ref_fill(rng, shape, dtype):
+    """The validators' distributions: int8 in [-100, 100], floats 0.1 + k/1000."""
+    if dtype == np.int8:
+        return rng.integers(-100, 101, shape, dtype=np.int8)
+    return (0.1 + rng.integers(0, 100, shape) / 1000).astype(F)
+
+
+@pytest.mark.parametrize("n,d", SHAPES)
+@pytest.mark.parametrize("batch", [1, 3])
+def test_q8_gemv(cuda, oracle, n, d, batch):
+    import v7multiplikator_b200 as v7g
+    rng = np.random.default_rng(n * 7 + d + batch)
+    xq, xs, wq, ws = q8_case(rng, batch, n, d)
+    out = torch.empty(batch, d, device=cuda)
+    v7g.q8_gemv(out, dev(xq), dev(xs), dev(wq), dev(ws))
+    assert_same_f32(host(out), oracle.q8_gemv(xq, xs, wq, ws))
+
+
+@pytest.mark.parametrize("n,d", SHAPES)
+def test_swiglu_q8_gemv(cuda, oracle, n, d):
+    import v7multiplikator_b200 as v7g
+    rng = np.random.default_rng(n + 3 * d)
+    xq, xs = ref_fill(rng, (1, n), np.int8), ref_fill(rng, (1, n // 64), F)
+    gq, gs = ref_fill(rng, (d, n), np.int8), ref_fill(rng, (d, n // 64), F)
+    uq, us = ref_fill(rng, (d, n), np.int8), ref_fill(rng, (d, n // 64), F)
+    out = torch.empty(1, d, device=cuda)
+    v7g.swiglu_q8_gemv(out, dev(xq), dev(xs), dev(gq), dev(gs), dev(uq), dev(us))
+    with np.errstate(all="ignore"):
+        assert_same_f32(host(out), oracle.swiglu_q8_gemv(xq, xs, gq, gs, uq, us))
+
+
+@pytest.mark.parametrize("n,d", SHAPES)
+def test_swiglu_f32q8_gemv(cuda, oracle, n, d):
+    import v7multiplikator_b200 as v7g
+    rng = np.random.default_rng(n + 5 * d)
+    x = ref_fill(rng, (2, n), F)
+    gq, gs = ref_fill(rng, (d, n), np.int8), ref_fill(rng, (d, n // 64), F)
+    uq, us = ref_fill(rng, (d, n), np.int8), ref_fill(rng, (d, n // 64), F)
+    out = torch.empty(2, d, device=cuda)
+    v7g.swiglu_f32q8_gemv(out, dev(x), dev(gq), dev(gs), dev(uq), dev(us))
+    with np.errstate(all="ignore"):
+        assert_same_f32(host(out), oracle.swiglu_f32q8_gemv(x, gq, gs, uq, us))
+
+
+@pytest.mark.parametrize("n,d", [(2048, 8192), (64, 5), (1024, 1000)])
+def test_q8_fused_gemv(cuda, oracle, n, d):
+    import v7multiplikator_b200 as v7g
+    rng = np.random.default_rng(n + d)
+    x = rng.normal(0, 2, (2, n)).astype(F)
+    x[0, 5] = np.nan
+    x[1, 70] = np.inf
+    x[1, 200 % n] = 1e-39
+    _, _, wq, ws = q8_case(rng, 1, n, d)
+    out = torch.empty(2, d, device=cuda)
+    v7g.q8_fused_gemv(out, dev(x), dev(wq), dev(ws))
+    with np.errstate(all="ignore"):
+        assert_same_f32(host(out), oracle.q8_fused_gemv(x, wq, ws))
+
+
+def test_q8_fused_gemv_unaligned_activation(cuda, oracle):
+    import v7multiplikator_b200 as v7g
+    rng = np.random.default_rng(2)
+    n, d = 256, 70
+    x = rng.normal(0, 1, (1, n)).astype(F)
+    _, _, wq, ws = q8_case(rng, 1, n, d)
+    buf = torch.zeros(n + 1, device=cuda)
+    xt = buf[1:].view(1, n)
+    xt.copy_(dev(x))
+    out = torch.empty(1, d, device=cuda)
+    v7g.q8_fused_gemv(out, xt, dev(wq), dev(ws))
+    assert_same_f32(host(out), oracle.q8_fused_gemv(x, wq, ws))
+
+
+def test_gemv_neg128_weights_and_extreme_scales(cuda, oracle):
+    """Outside the exporter's contract (-128 weights) the kernel still
+    reproduces the reference's vpsignb product; scales spanning the fp32
+    range exercise FTZ in the scale product and the accumulation."""
+    import v7multiplikator_b200 as v7g
+    rng = np.random.default_rng(4)
+    n, d = 512, 64
+    xq = rng.integers(-128, 128, (1, n), dtype=np.int8)
+    wq = rng.integers(-128, 128, (d, n), dtype=np.int8)
+    wq[:, ::7] = -128
+    xs = np.exp2(rng.integers(-70, 60, (1, n // 64))).astype(F)
+    ws = np.exp2(rng.integers(-70, 60, (d, n // 64))).astype(F)
+    ws[3, 2] = 1e-39
+    out = torch.empty(1, d, device=cuda)
+    v7g.q8_gemv(out, dev(xq), dev(xs), dev(wq), dev(ws))
+    with np.errstate(all="ignore"):
+        assert_same_f32(host(out), oracle.q8_gemv(xq, xs, wq, ws))
+    out2 = torch.empty(1, d, device=cuda)
+    v7g.swiglu_q8_gemv(out2, dev(xq), dev(xs), dev(wq), dev(ws), dev(wq[::-1].copy()), dev(ws[::-1].copy()))
+    with np.errstate(all="ignore"):
+        assert_same_f32(host(out2), oracle.swiglu_q8_gemv(xq, xs, wq, ws, wq[::-1], ws[::-1]))
+
+
+def test_gemv_rejects_bad_shapes(cuda):
+    import v7multiplikator_b200 as v7g
+    x = torch.zeros(1, 96, dtype=torch.int8, device=cuda)
+    w = torch.zeros(4, 96, dtype=torch.int8, device=cuda)
+    s = torch.zeros(4, 1, device=cuda)
+    with pytest.raises(v7g.V7GError, match="multiple of 64"):
+        v7g.q8_gemv(torch.empty(1, 4, device=cuda), x, torch.zeros(1, 1, device=cuda), w, s)

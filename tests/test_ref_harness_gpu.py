@@ -1,7 +1,7 @@
 """The reference's own validators and loadtests, unchanged, against this
 library on a B200.
 
-oracle/ref.mk compiles tools/v_{rmsnorm,add_inplace,quantize}_validate.cpp and
+oracle/ref.mk compiles tools/v_{rmsnorm,add_inplace,quantize,swiglu}_validate.cpp and
 tools/b_*_loadtest.cpp from the reference's sources into oracle/_ref/ (they
 travel to the GPU box as binaries).  Each loads libv7_threading.so through the
 reference's loader (dlopen + 99 dlsym, ms_abi calls) and drives the hot-path
@@ -46,8 +46,29 @@ def test_reference_validator(cuda, native_lib_path, db, validator, expect):
     assert m and int(m.group(1)) == expect and int(m.group(2)) == 0, tail
 
 
+def test_reference_swiglu_validator(cuda, native_lib_path, db):
+    """tools/v_swiglu_validate.cpp (v7d_swiglu and v7d_swiglu_q8 against the
+    double C references): the library's outputs equal the oracle's bit for
+    bit, so the validator's report -- every case, every printed error -- is
+    the one it gives for the oracle behind the same ABI."""
+    from oracle.pyoracle import ABI_SHIM
+    exe = ref_bin("v_swiglu_validate")
+
+    def run(lib):
+        r = subprocess.run([str(exe), str(lib), "--db", str(db)], capture_output=True, text=True, timeout=900)
+        lines = [ln for ln in r.stdout.splitlines() if str(lib) not in ln]
+        return r.returncode, lines
+
+    rc, ours = run(native_lib_path)
+    assert rc == 0, "\n".join(ours[-40:])
+    assert any("F32xQ8 10 passed" in ln and "0 hard failures" in ln for ln in ours), "\n".join(ours[-40:])
+    _, theirs = run(ABI_SHIM)
+    assert ours == theirs
+
+
 @pytest.mark.parametrize("args", [["b_rmsnorm_loadtest", "2048"], ["b_fused_add_rmsnorm_loadtest", "2048"],
-                                  ["b_add_inplace_loadtest", "2048"], ["b_rmsnorm_rope_loadtest", "16", "128", "7", "128"]])
+                                  ["b_add_inplace_loadtest", "2048"], ["b_rmsnorm_rope_loadtest", "16", "128", "7", "128"],
+                                  ["b_swiglu_q8_loadtest", "2048", "8192"], ["b_swiglu_loadtest", "2048", "8192"]])
 def test_reference_loadtest(cuda, native_lib_path, db, args):
     exe = ref_bin(args[0])
     r = subprocess.run([str(exe), str(native_lib_path), *args[1:], "--db", str(db), "--iterations", "200"],

@@ -24,6 +24,8 @@ from .ops import (  # noqa: F401
     get_rms_eps,
     launch_count,
     lib,
+    q8_fused_gemv,
+    q8_gemv,
     quantize_rows,
     rmsnorm_quantize_rows,
     rmsnorm_rope_rows,
@@ -35,6 +37,8 @@ from .ops import (  # noqa: F401
     selftest_arith,
     set_rms_eps,
     swiglu,
+    swiglu_f32q8_gemv,
+    swiglu_q8_gemv,
     swiglu_q8_rows,
     v7d_quantize,
     v7s_add_inplace,

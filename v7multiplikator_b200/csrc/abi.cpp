@@ -400,6 +400,65 @@ V7_ABI void v7s_rmsnorm_rope_heads(float *buf, int n_heads, int head_dim, float 
 	s.end(v7g_rmsnorm_rope_rows((float *)s.dev(ib), nullptr, 1, n_heads, 0, head_dim, (const float *)s.dev(iw), nullptr, c, sn, pos, 0, *v7g_rms_eps_slot(), s.stream()));
 }
 
+V7_ABI void v7d_q8(float *xout, v7_q8_tensor *x, v7_q8_tensor *w, int n, int d)
+{
+	std::lock_guard<std::mutex> lock(g_mutex);
+	if (!x || !w || n <= 0 || n % 64 != 0 || d < 0) {
+		die("v7d_q8: n %d, d %d or a NULL tensor break the contract n %% 64 == 0", n, d);
+		return;
+	}
+	if (d == 0)
+		return;
+	const size_t ng = (size_t)n / 64;
+	Stager s;
+	int io = s.add(xout, (size_t)d * sizeof(float), false, true);
+	int ixq = s.add(x->q, (size_t)n, true, false), ixs = s.add(x->s, ng * sizeof(float), true, false);
+	int iwq = s.add(w->q, (size_t)d * n, true, false), iws = s.add(w->s, (size_t)d * ng * sizeof(float), true, false);
+	if (!s.begin("v7d_q8"))
+		return;
+	s.end(v7g_q8_gemv((float *)s.dev(io), (const int8_t *)s.dev(ixq), (const float *)s.dev(ixs), (const int8_t *)s.dev(iwq), (const float *)s.dev(iws), 1, n, d, s.stream()));
+}
+
+V7_ABI void v7d_swiglu(float *xout, v7_f32_tensor *x, v7_q8_tensor *gate_w, int n, int d, v7_q8_tensor *up_w)
+{
+	std::lock_guard<std::mutex> lock(g_mutex);
+	if (!x || !gate_w || !up_w || n <= 0 || n % 64 != 0 || d < 0) {
+		die("v7d_swiglu: n %d, d %d or a NULL tensor break the contract n %% 64 == 0", n, d);
+		return;
+	}
+	if (d == 0)
+		return;
+	const size_t ng = (size_t)n / 64;
+	Stager s;
+	int io = s.add(xout, (size_t)d * sizeof(float), false, true);
+	int ix = s.add(x->data, (size_t)n * sizeof(float), true, false);
+	int igq = s.add(gate_w->q, (size_t)d * n, true, false), igs = s.add(gate_w->s, (size_t)d * ng * sizeof(float), true, false);
+	int iuq = s.add(up_w->q, (size_t)d * n, true, false), ius = s.add(up_w->s, (size_t)d * ng * sizeof(float), true, false);
+	if (!s.begin("v7d_swiglu"))
+		return;
+	s.end(v7g_swiglu_f32q8_gemv((float *)s.dev(io), (const float *)s.dev(ix), (const int8_t *)s.dev(igq), (const float *)s.dev(igs), (const int8_t *)s.dev(iuq), (const float *)s.dev(ius), 1, n, d, s.stream()));
+}
+
+V7_ABI void v7d_swiglu_q8(float *xout, v7_q8_tensor *x, v7_q8_tensor *gate_w, int n, int d, v7_q8_tensor *up_w)
+{
+	std::lock_guard<std::mutex> lock(g_mutex);
+	if (!x || !gate_w || !up_w || n <= 0 || n % 64 != 0 || d < 0) {
+		die("v7d_swiglu_q8: n %d, d %d or a NULL tensor break the contract n %% 64 == 0", n, d);
+		return;
+	}
+	if (d == 0)
+		return;
+	const size_t ng = (size_t)n / 64;
+	Stager s;
+	int io = s.add(xout, (size_t)d * sizeof(float), false, true);
+	int ixq = s.add(x->q, (size_t)n, true, false), ixs = s.add(x->s, ng * sizeof(float), true, false);
+	int igq = s.add(gate_w->q, (size_t)d * n, true, false), igs = s.add(gate_w->s, (size_t)d * ng * sizeof(float), true, false);
+	int iuq = s.add(up_w->q, (size_t)d * n, true, false), ius = s.add(up_w->s, (size_t)d * ng * sizeof(float), true, false);
+	if (!s.begin("v7d_swiglu_q8"))
+		return;
+	s.end(v7g_swiglu_q8_gemv((float *)s.dev(io), (const int8_t *)s.dev(ixq), (const float *)s.dev(ixs), (const int8_t *)s.dev(igq), (const float *)s.dev(igs), (const int8_t *)s.dev(iuq), (const float *)s.dev(ius), 1, n, d, s.stream()));
+}
+
 V7_ABI void v7s_rope_only_heads(float *buf, int n_heads, int head_dim, float *cos_table, float *sin_table, int pos, int rope_max_dim)
 {
 	std::lock_guard<std::mutex> lock(g_mutex);

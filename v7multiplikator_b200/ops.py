@@ -61,6 +61,12 @@ _SIGNATURES = {
     "v7g_rope_tables": [c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_void_p, c_void_p],
     "v7g_rope_init": [c_int, c_float, c_int, c_float, c_float, c_float, c_int],
     "v7g_get_rope_tables": [c_void_p, c_void_p, c_void_p],
+    "v7g_q8_gemv": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_void_p],
+    "v7g_q8_fused_gemv": [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_void_p],
+    "v7g_swiglu_q8_gemv": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int,
+                           c_void_p],
+    "v7g_swiglu_f32q8_gemv": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int,
+                              c_void_p],
 }
 
 # Positions of the tables rope_init builds (V7G_ROPE_TABLE_POSITIONS).
@@ -327,6 +333,71 @@ def rmsnorm_quantize_rows(codes: torch.Tensor, scales: torch.Tensor, x: torch.Te
         _want(codes, "codes", torch.int8, d), _want(scales, "scales", torch.float32, d),
         _want(x, "x", torch.float32, d), _want(weight, "weight", torch.float32, d), rows, n, eps,
         _stream(x, stream)))
+
+
+def _gemv_dims(x: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor, out: torch.Tensor):
+    if x.dim() != 2 or wq.dim() != 2:
+        raise ValueError("activations must be [batch, n], weight codes [d, n]")
+    batch, n = x.shape
+    d = wq.shape[0]
+    if wq.shape[1] != n or ws.numel() != d * (n // 64) or out.shape != (batch, d):
+        raise ValueError("shape mismatch: weights [d, n] + [d, n/64] scales, out [batch, d]")
+    return batch, n, d
+
+
+def q8_gemv(out: torch.Tensor, xq: torch.Tensor, xs: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor,
+            stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """out[b, i] = dot(x_b, w_i), Q8 activation (codes [batch, n], scales
+    [batch, n/64]) times Q8 weights (codes [d, n], scales [d, n/64]) -- v7d_q8
+    (q8_kernel.inc:84-207)."""
+    batch, n, d = _gemv_dims(xq, wq, ws, out)
+    dv = xq.device
+    _check(lib().v7g_q8_gemv(_want(out, "out", torch.float32, dv), _want(xq, "xq", torch.int8, dv),
+                             _want(xs, "xs", torch.float32, dv), _want(wq, "wq", torch.int8, dv),
+                             _want(ws, "ws", torch.float32, dv), batch, n, d, _stream(xq, stream)))
+    return out
+
+
+def q8_fused_gemv(out: torch.Tensor, x: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor,
+                  stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """v7d_q8_fused (fused_dispatch.inc:82-114): quantise each fp32 activation
+    row with v7d_quantize's rules, then v7d_q8, in one kernel."""
+    batch, n, d = _gemv_dims(x, wq, ws, out)
+    dv = x.device
+    _check(lib().v7g_q8_fused_gemv(_want(out, "out", torch.float32, dv), _want(x, "x", torch.float32, dv),
+                                   _want(wq, "wq", torch.int8, dv), _want(ws, "ws", torch.float32, dv), batch, n, d,
+                                   _stream(x, stream)))
+    return out
+
+
+def swiglu_q8_gemv(out: torch.Tensor, xq: torch.Tensor, xs: torch.Tensor, gate_q: torch.Tensor, gate_s: torch.Tensor,
+                   up_q: torch.Tensor, up_s: torch.Tensor, stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """v7d_swiglu_q8 (swiglu_q8_kernel.inc:16-286): out[b, i] =
+    swiglu(dot(x_b, gate_i), dot(x_b, up_i)) with a Q8 activation."""
+    batch, n, d = _gemv_dims(xq, gate_q, gate_s, out)
+    if up_q.shape != gate_q.shape or up_s.numel() != gate_s.numel():
+        raise ValueError("gate and up weights must have the same shape")
+    dv = xq.device
+    _check(lib().v7g_swiglu_q8_gemv(
+        _want(out, "out", torch.float32, dv), _want(xq, "xq", torch.int8, dv), _want(xs, "xs", torch.float32, dv),
+        _want(gate_q, "gate_q", torch.int8, dv), _want(gate_s, "gate_s", torch.float32, dv),
+        _want(up_q, "up_q", torch.int8, dv), _want(up_s, "up_s", torch.float32, dv), batch, n, d, _stream(xq, stream)))
+    return out
+
+
+def swiglu_f32q8_gemv(out: torch.Tensor, x: torch.Tensor, gate_q: torch.Tensor, gate_s: torch.Tensor,
+                      up_q: torch.Tensor, up_s: torch.Tensor, stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """v7d_swiglu (swiglu_kernel.inc): fp32 activation times Q8 gate/up, SwiGLU
+    epilogue, with the reference's dual-row arithmetic."""
+    batch, n, d = _gemv_dims(x, gate_q, gate_s, out)
+    if up_q.shape != gate_q.shape or up_s.numel() != gate_s.numel():
+        raise ValueError("gate and up weights must have the same shape")
+    dv = x.device
+    _check(lib().v7g_swiglu_f32q8_gemv(
+        _want(out, "out", torch.float32, dv), _want(x, "x", torch.float32, dv),
+        _want(gate_q, "gate_q", torch.int8, dv), _want(gate_s, "gate_s", torch.float32, dv),
+        _want(up_q, "up_q", torch.int8, dv), _want(up_s, "up_s", torch.float32, dv), batch, n, d, _stream(x, stream)))
+    return out
 
 
 def fill_normal(dst: torch.Tensor, seed: int, mean: float, std: float, row0: int = 0,
