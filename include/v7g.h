@@ -152,6 +152,11 @@ int v7g_swiglu_q8_gemv(float *out, const int8_t *xq, const float *xs, const int8
    the sums differently and can differ in the last bits). */
 int v7g_swiglu_f32q8_gemv(float *out, const float *x, const int8_t *gate_q, const float *gate_s, const int8_t *up_q, const float *up_s, int64_t batch, int n, int d, void *stream);
 
+/* Number of bounded waits in the pipelined GEMV kernels that gave up since
+   the library was loaded (a kernel that gives up writes no result for the
+   rows it was computing).  0 in every correct run. */
+unsigned int v7g_pipeline_timeouts(void);
+
 /* ---- runtime ---------------------------------------------------------- */
 
 /* RMS epsilon used by the reference-ABI entries (v7s_rmsnorm & co.), which

@@ -24,6 +24,7 @@ from .ops import (  # noqa: F401
     get_rms_eps,
     launch_count,
     lib,
+    pipeline_timeouts,
     q8_fused_gemv,
     q8_gemv,
     quantize_rows,

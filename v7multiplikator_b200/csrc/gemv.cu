@@ -24,6 +24,7 @@
 // groups are issued before their arithmetic.  The weights are read exactly
 // once: HBM-bound at d x n x (1 + 4/64) bytes per matrix.
 #include "internal.h"
+#include "pipeline.cuh"
 #include "q8.cuh"
 
 namespace v7g {
@@ -40,7 +41,7 @@ constexpr int kMaxN = 65536;                  // activation staged in shared mem
 // a * (-128), i.e. 256 * a more than the true product.  The exporter never
 // writes -128 (swiglu_q8_kernel.inc:17-23), so this runs only on inputs
 // outside that contract.
-__device__ __noinline__ int neg128_correction(uint32_t a, uint32_t w)
+__device__ __forceinline__ int neg128_correction(uint32_t a, uint32_t w)
 {
 	int c = 0;
 #pragma unroll
@@ -60,13 +61,19 @@ __device__ __forceinline__ uint32_t has_neg128(uint32_t w)
 	return (t - 0x01010101u) & ~t & 0x80808080u;
 }
 
-// One lane's dot over one group: the low word and the high word.
-__device__ __forceinline__ int lane_dot(uint32_t a_lo, uint32_t w_lo, uint32_t a_hi, uint32_t w_hi)
+// One lane's dot over one group (the low word and the high word) as the
+// true products; *flag collects whether a -128 weight byte needs the
+// correction, which the callers apply once per batch of groups so that the
+// groups' dots stay free of branches.
+__device__ __forceinline__ int lane_dot(uint32_t a_lo, uint32_t w_lo, uint32_t a_hi, uint32_t w_hi, uint32_t &flag)
 {
-	int d = __dp4a((int)a_hi, (int)w_hi, __dp4a((int)a_lo, (int)w_lo, 0));
-	if (has_neg128(w_lo) | has_neg128(w_hi))
-		d += neg128_correction(a_lo, w_lo) + neg128_correction(a_hi, w_hi);
-	return d;
+	flag |= has_neg128(w_lo) | has_neg128(w_hi);
+	return __dp4a((int)a_hi, (int)w_hi, __dp4a((int)a_lo, (int)w_lo, 0));
+}
+
+__device__ __forceinline__ int lane_dot_correction(uint32_t a_lo, uint32_t w_lo, uint32_t a_hi, uint32_t w_hi)
+{
+	return neg128_correction(a_lo, w_lo) + neg128_correction(a_hi, w_hi);
 }
 
 // HADD_YMM over the row's eight lane threads (consecutive lanes of a warp):
@@ -91,13 +98,13 @@ struct GemvArgs {
 
 // Quantise the CTA's activation row into shared memory with v7d_quantize's
 // rules (quantize_kernel.inc:43-106): half a warp per 64-element group, one
-// float4 per lane.
-__device__ void stage_quantized(const float *x, int n, uint32_t *sq, float *ss)
+// float4 per lane; `nthreads` (a multiple of 32) threads take part.
+__device__ void stage_quantized(const float *x, int n, uint32_t *sq, float *ss, int nthreads = kBlock)
 {
 	const int lane = threadIdx.x & 31, half = lane >> 4, hl = lane & 15;
 	const int groups = n / kQ8Group;
 	const bool vec = (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
-	for (int g = (threadIdx.x >> 5) * 2 + half; g - half < groups; g += (kBlock / 32) * 2) {
+	for (int g = (threadIdx.x >> 5) * 2 + half; g - half < groups; g += (nthreads / 32) * 2) {
 		float4 h = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 		if (g < groups) {
 			const float *p = x + (int64_t)g * kQ8Group + 4 * hl;
@@ -120,7 +127,7 @@ __global__ void __launch_bounds__(kBlock) k_q8_gemv(GemvArgs p)
 {
 	using M = F<true>;
 	constexpr int NM = MODE == 1 ? 2 : 1;
-	extern __shared__ __align__(16) unsigned char smem[];
+	extern __shared__ __align__(128) unsigned char smem[];
 	const int n = p.n, groups = n / kQ8Group;
 	uint32_t *sq = reinterpret_cast<uint32_t *>(smem);
 	float *ss = reinterpret_cast<float *>(smem + n);
@@ -165,17 +172,34 @@ __global__ void __launch_bounds__(kBlock) k_q8_gemv(GemvArgs p)
 					sc[m][u] = __ldg(s[m] + g0 + u);
 				}
 			}
+		int dots[NM][kUnroll];
+		uint32_t alo[kUnroll], ahi[kUnroll];
+		uint32_t flag = 0;
 #pragma unroll
 		for (int u = 0; u < kUnroll; ++u)
 			if (g0 + u < gend) {
 				const int g = g0 + u;
-				const uint32_t a_lo = sq[g * 16 + l], a_hi = sq[g * 16 + 8 + l];
-				const float xsg = ss[g];
+				alo[u] = sq[g * 16 + l];
+				ahi[u] = sq[g * 16 + 8 + l];
 #pragma unroll
-				for (int m = 0; m < NM; ++m) {
-					const int dot = lane_dot(a_lo, lo[m][u], a_hi, hi[m][u]);
-					acc[m] = M::fma((float)dot, M::mul(sc[m][u], xsg), acc[m]);
-				}
+				for (int m = 0; m < NM; ++m)
+					dots[m][u] = lane_dot(alo[u], lo[m][u], ahi[u], hi[m][u], flag);
+			}
+		if (flag) {
+#pragma unroll
+			for (int u = 0; u < kUnroll; ++u)
+				if (g0 + u < gend)
+#pragma unroll
+					for (int m = 0; m < NM; ++m)
+						dots[m][u] += lane_dot_correction(alo[u], lo[m][u], ahi[u], hi[m][u]);
+		}
+#pragma unroll
+		for (int u = 0; u < kUnroll; ++u)
+			if (g0 + u < gend) {
+				const float xsg = ss[g0 + u];
+#pragma unroll
+				for (int m = 0; m < NM; ++m)
+					acc[m] = M::fma((float)dots[m][u], M::mul(sc[m][u], xsg), acc[m]);
 			}
 	}
 	float r[NM];
@@ -184,6 +208,198 @@ __global__ void __launch_bounds__(kBlock) k_q8_gemv(GemvArgs p)
 		r[m] = hadd_lanes(acc[m]);
 	if (l == 0 && valid)
 		p.out[b * p.d + row] = MODE == 1 ? v7_swiglu(r[0], r[1]) : r[0];
+}
+
+// Wait-bound events of the pipelined kernels (device word, read by
+// v7g_pipeline_timeouts); 0 in every correct run.
+__device__ unsigned int g_pipeline_timeouts;
+
+// ---- pipelined Q8 x Q8 GEMV ------------------------------------------------
+// The arithmetic of k_q8_gemv with the weights streamed through shared
+// memory: a CTA owns R consecutive rows; one producer thread issues 1-D bulk
+// copies of kChunkGroups groups (1 KB) of every row and matrix per stage
+// into a ring of `stages` stages (transaction-counting mbarriers), the R x 8
+// consumer threads (one per row lane, as in k_q8_gemv) take the words of
+// their lane from shared memory.  Tens of KB stay in flight per SM whatever d
+// is, so small matrices stream near HBM speed too.
+constexpr int kChunkGroups = 16;
+// A row's slot in a stage: the 1024 bytes of its chunk and 32 bytes of
+// padding, so the four rows a warp reads start 8 banks apart.
+constexpr int kRowSlot = kChunkGroups * kQ8Group + 32;
+
+// The chains of one row lane over the gk (<= G) groups of a stage: all dots
+// first (no branch between groups), the rare -128 correction once, then the
+// fused multiply-adds in group order.  st: the row's slot of matrix 0 (matrix
+// m at + m * R slots); a: activation words of the first group; cs: the row's
+// combined scales (weight scale times activation scale) from the first group
+// (matrix m at + m * R * sstride).
+template <int NM, int R, int G>
+__device__ __forceinline__ void chunk_chains(float (&acc)[NM], const uint32_t *st, const uint32_t *a, const float *cs, int sstride, int l, int gk)
+{
+	using M = F<true>;
+	constexpr int SB = 4; // groups per batch: bounds the registers the dots hold
+#pragma unroll 1
+	for (int b0 = 0; b0 < G; b0 += SB) {
+		if (b0 >= gk)
+			break;
+		int dots[NM][SB];
+		uint32_t flag = 0;
+#pragma unroll
+		for (int j = 0; j < SB; ++j)
+			if (b0 + j < gk)
+#pragma unroll
+				for (int m = 0; m < NM; ++m) {
+					const uint32_t *wr = st + m * R * (kRowSlot / 4) + (b0 + j) * 16;
+					dots[m][j] = lane_dot(a[(b0 + j) * 16 + l], wr[l], a[(b0 + j) * 16 + 8 + l], wr[8 + l], flag);
+				}
+		if (flag) {
+#pragma unroll
+			for (int j = 0; j < SB; ++j)
+				if (b0 + j < gk)
+#pragma unroll
+					for (int m = 0; m < NM; ++m) {
+						const uint32_t *wr = st + m * R * (kRowSlot / 4) + (b0 + j) * 16;
+						dots[m][j] += lane_dot_correction(a[(b0 + j) * 16 + l], wr[l], a[(b0 + j) * 16 + 8 + l], wr[8 + l]);
+					}
+		}
+#pragma unroll
+		for (int j = 0; j < SB; ++j)
+			if (b0 + j < gk)
+#pragma unroll
+				for (int m = 0; m < NM; ++m)
+					acc[m] = M::fma((float)dots[m][j], cs[m * R * sstride + b0 + j], acc[m]);
+	}
+}
+
+template <int MODE, bool FUSED, int R>
+__global__ void __launch_bounds__(R * kLanes + 32) k_q8_gemv_tma(GemvArgs p, int stages)
+{
+	using M = F<true>;
+	constexpr int NM = MODE == 1 ? 2 : 1;
+	constexpr int kConsumers = R * kLanes;
+	constexpr int kStageBytes = NM * R * kRowSlot;
+	extern __shared__ __align__(128) unsigned char smem[];
+	const int n = p.n, groups = n / kQ8Group;
+	const int nchunks = (groups + kChunkGroups - 1) / kChunkGroups;
+	const int64_t row0 = (int64_t)blockIdx.x * R;
+	const int rows = (int)min((int64_t)R, p.d - row0);
+	// layout: stages | activation codes [n] | activation scales [groups] |
+	// combined scales [NM][R][groups + 1] | full[stages] | empty[stages]
+	const int sstride = groups + 1; // odd row stride: the warp's four rows hit four banks
+	unsigned char *ring = smem;
+	uint32_t *sq = reinterpret_cast<uint32_t *>(smem + (size_t)stages * kStageBytes);
+	float *ss = reinterpret_cast<float *>(reinterpret_cast<unsigned char *>(sq) + n);
+	float *sws = ss + groups;
+	uint64_t *full = reinterpret_cast<uint64_t *>(sws + NM * R * sstride + ((NM * R * sstride + groups) & 1));
+	uint64_t *empty = full + stages;
+	const int64_t b = blockIdx.y;
+	if (threadIdx.x == 0) {
+		for (int s = 0; s < stages; ++s) {
+			mbar_init(full + s, 1);
+			mbar_init(empty + s, kConsumers / 32);
+		}
+		mbar_init_fence();
+	}
+	__syncthreads();
+	if (threadIdx.x >= kConsumers) {
+		// producer warp: lane 0 waits for the slot and posts the byte count,
+		// then every lane issues one row's copy (NM * R <= 32)
+		const int lane = threadIdx.x & 31;
+		for (int k = 0; k < nchunks; ++k) {
+			const int s = k % stages;
+			bool ok = true;
+			if (k >= stages && lane == 0)
+				ok = mbar_wait(empty + s, ((k / stages) - 1) & 1, &g_pipeline_timeouts);
+			if (!__shfl_sync(0xffffffffu, ok, 0))
+				break;
+			const int g0 = k * kChunkGroups;
+			const int gk = min(kChunkGroups, groups - g0);
+			const uint32_t bytes = (uint32_t)(gk * kQ8Group);
+			if (lane == 0)
+				mbar_arrive_expect_tx(full + s, bytes * NM * rows);
+			__syncwarp();
+			if (lane < NM * rows) {
+				const int m = lane / rows, r = lane - m * rows;
+				// a select, not p.wq[m]: a runtime index into the parameter
+				// array would copy it to local memory
+				const int8_t *wm = m == 0 ? p.wq[0] : p.wq[NM - 1];
+				bulk_copy_g2s(ring + (size_t)s * kStageBytes + (m * R + r) * kRowSlot, wm + (row0 + r) * n + (int64_t)g0 * kQ8Group,
+				              bytes, full + s);
+			}
+		}
+		// leave only once the copies of the last stages have landed
+		if (lane == 0)
+			for (int k = max(0, nchunks - stages); k < nchunks; ++k)
+				if (!mbar_wait(full + k % stages, (k / stages) & 1, &g_pipeline_timeouts))
+					break;
+		return;
+	}
+	// consumers: stage the activation and the weight scales, then the chains
+	if (FUSED) {
+		stage_quantized(p.xf + b * n, n, sq, ss, kConsumers);
+	} else {
+		const uint4 *src = reinterpret_cast<const uint4 *>(p.xq + b * n);
+		for (int i = threadIdx.x; i < n / 16; i += kConsumers)
+			reinterpret_cast<uint4 *>(sq)[i] = __ldg(src + i);
+		for (int i = threadIdx.x; i < groups; i += kConsumers)
+			ss[i] = __ldg(p.xs + b * groups + i);
+	}
+	// raw weight scales now (their loads overlap the activation's), each
+	// thread's entries turned into combined scales -- weight scale x
+	// activation scale, rounded once as the reference's vmulps -- once the
+	// activation scales are in place
+	for (int m = 0; m < NM; ++m)
+		for (int i = threadIdx.x; i < rows * groups; i += kConsumers)
+			sws[(m * R + i / groups) * sstride + i % groups] = __ldg(p.ws[m] + row0 * groups + i);
+	named_sync(1, kConsumers);
+	for (int m = 0; m < NM; ++m)
+		for (int i = threadIdx.x; i < rows * groups; i += kConsumers) {
+			float *c = sws + (m * R + i / groups) * sstride + i % groups;
+			*c = M::mul(*c, ss[i % groups]);
+		}
+	named_sync(1, kConsumers);
+	const int r = threadIdx.x >> 3, l = threadIdx.x & (kLanes - 1);
+	const bool valid = r < rows;
+	float acc[NM];
+#pragma unroll
+	for (int m = 0; m < NM; ++m)
+		acc[m] = 0.0f;
+	bool ok = true;
+	for (int k = 0; k < nchunks; ++k) {
+		const int s = k % stages;
+		// the warp leaves together if any lane's wait ran out
+		if (!__all_sync(0xffffffffu, mbar_wait(full + s, (k / stages) & 1, &g_pipeline_timeouts))) {
+			ok = false;
+			break;
+		}
+		const int g0 = k * kChunkGroups;
+		const int gk = min(kChunkGroups, groups - g0);
+		if (valid) {
+			const uint32_t *st = reinterpret_cast<const uint32_t *>(ring + (size_t)s * kStageBytes) + r * (kRowSlot / 4);
+			const float *cs = sws + r * sstride + g0;
+			if (gk == kChunkGroups)
+				chunk_chains<NM, R, kChunkGroups>(acc, st, sq + g0 * 16, cs, sstride, l, kChunkGroups);
+			else
+				chunk_chains<NM, R, kChunkGroups>(acc, st, sq + g0 * 16, cs, sstride, l, gk);
+		}
+		__syncwarp();
+		if ((threadIdx.x & 31) == 0)
+			mbar_arrive(empty + s);
+	}
+	float res[NM];
+#pragma unroll
+	for (int m = 0; m < NM; ++m)
+		res[m] = hadd_lanes(acc[m]);
+	if (ok && valid && l == 0)
+		p.out[b * p.d + row0 + r] = MODE == 1 ? v7_swiglu(res[0], res[1]) : res[0];
+}
+
+// Shared memory of k_q8_gemv_tma for `stages` stages.
+size_t tma_smem(int nm, int rows, int n, int stages)
+{
+	const int groups = n / kQ8Group;
+	const size_t fixed = (size_t)n + 4 * ((size_t)groups + (size_t)nm * rows * (groups + 1)) + 8 + 16 * (size_t)stages;
+	return (size_t)stages * nm * rows * kRowSlot + fixed;
 }
 
 // fp32 activation x Q8 weights, SwiGLU epilogue (v7d_swiglu, dual-row path):
@@ -252,6 +468,64 @@ int launch_gemv(Kernel kernel, const char *what, const GemvArgs &a, int64_t batc
 
 bool weights_ok(const int8_t *q, const float *s) { return q && s && (reinterpret_cast<uintptr_t>(q) & 3) == 0; }
 
+constexpr size_t kTmaSmemBudget = 200 * 1024;
+constexpr int kMaxDevicesTracked = 64;
+
+// The pipelined kernel: R = 16 rows per CTA when that still gives two CTAs
+// per SM, else 8; as many stages (up to 6) as the shared-memory budget
+// allows.  Returns V7G_ERR_UNSUPPORTED when even two stages do not fit (a
+// very long activation row), for the caller to fall back.
+template <int MODE, bool FUSED>
+int launch_gemv_tma(const char *what, const GemvArgs &a, int64_t batch, void *stream)
+{
+	DeviceInfo dev;
+	int rc = current_device(&dev);
+	if (rc != V7G_OK)
+		return rc;
+	constexpr int NM = MODE == 1 ? 2 : 1;
+	const bool wide = a.d >= 2 * 16 * (int64_t)dev.sm_count;
+	const int R = wide ? 16 : 8;
+	// up to 4 stages while a CTA stays under ~112 KB (two per SM), at least 2
+	int stages = 4;
+	while (stages > 2 && tma_smem(NM, R, a.n, stages) > 112 * 1024)
+		--stages;
+	while (stages > 2 && tma_smem(NM, R, a.n, stages) > kTmaSmemBudget)
+		--stages;
+	const size_t smem = tma_smem(NM, R, a.n, stages);
+	if (smem > kTmaSmemBudget)
+		return V7G_ERR_UNSUPPORTED;
+	const void *kernel = wide ? (const void *)k_q8_gemv_tma<MODE, FUSED, 16> : (const void *)k_q8_gemv_tma<MODE, FUSED, 8>;
+	// the shared-memory ceiling of each kernel is raised once per device
+	static bool raised[2][kMaxDevicesTracked];
+	if (dev.device < kMaxDevicesTracked && !raised[wide][dev.device]) {
+		if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTmaSmemBudget) != cudaSuccess)
+			return check_launch(what);
+		raised[wide][dev.device] = true;
+	} else if (dev.device >= kMaxDevicesTracked &&
+	           cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTmaSmemBudget) != cudaSuccess) {
+		return check_launch(what);
+	}
+	const dim3 grid((unsigned)((a.d + R - 1) / R), (unsigned)batch);
+	if (wide)
+		k_q8_gemv_tma<MODE, FUSED, 16><<<grid, 16 * kLanes + 32, smem, (cudaStream_t)stream>>>(a, stages);
+	else
+		k_q8_gemv_tma<MODE, FUSED, 8><<<grid, 8 * kLanes + 32, smem, (cudaStream_t)stream>>>(a, stages);
+	return check_launch(what);
+}
+
+// The pipelined kernel when the weights allow bulk copies (16-byte aligned),
+// else (or when it does not fit) the direct-load kernel.
+template <int MODE, bool FUSED>
+int run_q8_gemv(const char *what, const GemvArgs &a, int64_t batch, void *stream, bool tma)
+{
+	if (tma) {
+		const int rc = launch_gemv_tma<MODE, FUSED>(what, a, batch, stream);
+		if (rc != V7G_ERR_UNSUPPORTED)
+			return rc;
+	}
+	return launch_gemv(k_q8_gemv<MODE, FUSED>, what, a, batch, (size_t)a.n + (size_t)a.n / 16, stream);
+}
+
 } // namespace
 } // namespace v7g
 
@@ -270,7 +544,7 @@ int v7g_q8_gemv(float *out, const int8_t *xq, const float *xs, const int8_t *wq,
 	if (!xq || !xs || !aligned16(xq) || !weights_ok(wq, ws))
 		return set_error(V7G_ERR_ARG, "%s: NULL pointer, activation codes not 16-byte or weight codes not 4-byte aligned", what);
 	GemvArgs a{out, xq, xs, nullptr, {wq, wq}, {ws, ws}, n, d};
-	return launch_gemv(k_q8_gemv<0, false>, what, a, batch, (size_t)n + (size_t)n / 16, stream);
+	return run_q8_gemv<0, false>(what, a, batch, stream, aligned16(wq));
 }
 
 int v7g_q8_fused_gemv(float *out, const float *x, const int8_t *wq, const float *ws, int64_t batch, int n, int d, void *stream)
@@ -284,7 +558,7 @@ int v7g_q8_fused_gemv(float *out, const float *x, const int8_t *wq, const float 
 	if (!x || !weights_ok(wq, ws))
 		return set_error(V7G_ERR_ARG, "%s: NULL pointer or weight codes not 4-byte aligned", what);
 	GemvArgs a{out, nullptr, nullptr, x, {wq, wq}, {ws, ws}, n, d};
-	return launch_gemv(k_q8_gemv<0, true>, what, a, batch, (size_t)n + (size_t)n / 16, stream);
+	return run_q8_gemv<0, true>(what, a, batch, stream, aligned16(wq));
 }
 
 int v7g_swiglu_q8_gemv(float *out, const int8_t *xq, const float *xs, const int8_t *gate_q, const float *gate_s, const int8_t *up_q, const float *up_s, int64_t batch, int n, int d, void *stream)
@@ -298,7 +572,7 @@ int v7g_swiglu_q8_gemv(float *out, const int8_t *xq, const float *xs, const int8
 	if (!xq || !xs || !aligned16(xq) || !weights_ok(gate_q, gate_s) || !weights_ok(up_q, up_s))
 		return set_error(V7G_ERR_ARG, "%s: NULL pointer, activation codes not 16-byte or weight codes not 4-byte aligned", what);
 	GemvArgs a{out, xq, xs, nullptr, {gate_q, up_q}, {gate_s, up_s}, n, d};
-	return launch_gemv(k_q8_gemv<1, false>, what, a, batch, (size_t)n + (size_t)n / 16, stream);
+	return run_q8_gemv<1, false>(what, a, batch, stream, aligned16(gate_q) && aligned16(up_q));
 }
 
 int v7g_swiglu_f32q8_gemv(float *out, const float *x, const int8_t *gate_q, const float *gate_s, const int8_t *up_q, const float *up_s, int64_t batch, int n, int d, void *stream)
@@ -313,6 +587,16 @@ int v7g_swiglu_f32q8_gemv(float *out, const float *x, const int8_t *gate_q, cons
 		return set_error(V7G_ERR_ARG, "%s: NULL pointer", what);
 	GemvArgs a{out, nullptr, nullptr, x, {gate_q, up_q}, {gate_s, up_s}, n, d};
 	return launch_gemv(k_f32q8_swiglu_gemv, what, a, batch, 0, stream);
+}
+
+unsigned int v7g_pipeline_timeouts(void)
+{
+	unsigned int v = 0;
+	if (cudaMemcpyFromSymbol(&v, g_pipeline_timeouts, sizeof(v)) != cudaSuccess) {
+		cudaGetLastError();
+		return 0xffffffffu;
+	}
+	return v;
 }
 
 } // extern "C"

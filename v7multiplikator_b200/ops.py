@@ -95,6 +95,7 @@ def lib() -> ctypes.CDLL:
         L.v7g_last_error.restype = c_char_p
         L.v7g_launch_count.restype = c_uint64
         L.v7g_version.restype = c_char_p
+        L.v7g_pipeline_timeouts.restype = ctypes.c_uint
         _lib = L
     return _lib
 
@@ -478,6 +479,11 @@ def selftest_arith(device: Optional[torch.device] = None) -> list[int]:
     counts = torch.zeros(5, dtype=torch.int64, device=device)
     _check(lib().v7g_selftest_arith(counts.data_ptr(), _stream(counts, None)))
     return [int(c) for c in counts.cpu().tolist()]
+
+
+def pipeline_timeouts() -> int:
+    """Bounded waits of the pipelined kernels that gave up (0 when healthy)."""
+    return int(lib().v7g_pipeline_timeouts())
 
 
 def launch_count() -> int:
