@@ -174,7 +174,7 @@ uint64_t v7g_launch_count(void);
 /* Exhaustive device self-check of the library's fast arithmetic (the
    Markstein-corrected reciprocal, the fast Q8 scale, the packed-pair SiLU and
    Q8 code paths) against the plain IEEE instructions, over every input each can
-   receive.  dev_counts: 5 zeroed device counters, incremented by the number of
+   receive.  dev_counts: 6 zeroed device counters, incremented by the number of
    mismatches of each test (all must stay 0).  Asynchronous on `stream`. */
 int v7g_selftest_arith(unsigned long long *dev_counts, void *stream);
 

@@ -54,7 +54,7 @@ def test_selftest_arith_exhaustive(cuda):
     equal the IEEE instructions on every input they can receive (2^23
     mantissas x every exponent, all 2^32 patterns for the SiLU and codes)."""
     import v7multiplikator_b200 as v7g
-    assert v7g.selftest_arith() == [0, 0, 0, 0, 0]
+    assert v7g.selftest_arith() == [0, 0, 0, 0, 0, 0]
 
 
 # --------------------------------------------------------------- RMSNorm rows
@@ -345,6 +345,30 @@ def test_rmsnorm_quantize_rows(cuda, oracle, rows, n):
     s2 = torch.empty_like(scales)
     v7g.quantize_rows(c2, s2, xb)
     np.testing.assert_array_equal(host(c2), host(codes))
+
+
+def test_rmsnorm_quantize_specials_at_every_group_position(cuda, oracle):
+    """NaN and infinities in gamma at each of a group's 64 positions (and in
+    every group slot of a warp): the absmax must follow the reference's MAXPS
+    tree order, which decides which NaN survives."""
+    import v7multiplikator_b200 as v7g
+    rng = np.random.default_rng(77)
+    rows, n = 3, 256
+    x = rng.uniform(-1, 1, (rows, n)).astype(F)
+    codes = torch.empty(rows, n, dtype=torch.int8, device=cuda)
+    scales = torch.empty(rows, n // 64, device=cuda)
+    for p in range(64):
+        w = rng.uniform(0.5, 1.5, n).astype(F)
+        w[p] = np.nan                      # group 0
+        w[64 + (p * 7) % 64] = -np.inf     # group 1
+        w[128 + p] = np.inf                # group 2
+        w[128 + (p + 32) % 64] = np.nan
+        w[192 + (p * 5) % 64] = 1e-39      # group 3: subnormal gamma (DAZ)
+        v7g.rmsnorm_quantize_rows(codes, scales, dev(x), dev(w), 1e-6)
+        with np.errstate(all="ignore"):
+            wq, ws = oracle.rmsnorm_quantize(x, w, 1e-6)
+        np.testing.assert_array_equal(host(codes), wq, err_msg=f"position {p}")
+        assert_same_f32(host(scales), ws, f"position {p}")
 
 
 def test_rmsnorm_quantize_rejects_unaligned_codes(cuda):

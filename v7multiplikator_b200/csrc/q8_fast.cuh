@@ -48,17 +48,41 @@ __device__ __forceinline__ float4 v7_swiglu4(float4 g, float4 u)
 	return make_float4(a.x, a.y, b.x, b.y);
 }
 
-// q8_scale with the Markstein reciprocal for a finite maximum; an inf or a
-// NaN that survived the tree takes the IEEE instructions.
+// q8_scale for a finite maximum without the general divide: wmax / 127 as a
+// double product rounded once to float.  That is the correctly rounded
+// quotient for every wmax here: the product carries a relative error below
+// 2.2 * 2^-53, so a wrong float rounding would need the exact quotient within
+// that distance of a float rounding boundary, i.e. 27 equal bits after its
+// 25th significant bit; the expansion of an integer over 127 repeats with
+// period 7 (2^7 = 1 mod 127), so such a run only occurs when the quotient is
+// exact.  The reciprocal takes the Markstein form.  An inf or a NaN that
+// survived the tree takes the IEEE instructions.  v7g_selftest_arith checks
+// scale and reciprocal against div.rn / rcp.rn for every possible maximum.
 __device__ __forceinline__ void q8_scale_fast(float wmax, float &scale, float &recip)
 {
 	wmax = x86_max(wmax, kQ8WmaxFloor);
 	if (wmax <= 3.402823466e38f) {
-		scale = F<true>::div(wmax, 127.0f);
+		scale = __double2float_rn(__dmul_rn((double)wmax, 1.0 / 127.0));
 		recip = rcp_nr(scale); // scale in [FLT_MIN, FLT_MAX/127]: reciprocal normal
 	} else {
 		q8_scale(wmax, scale, recip);
 	}
+}
+
+// Codes of four values whose products p = h * recip satisfy |p| < 127.5 (a
+// group with neither NaN nor infinity, quantised with its own scale: |p| is
+// at most 127 (1 + 3 * 2^-24)): round to nearest even through the 1.5 * 2^23
+// addition and keep the low byte.  For such p the reference's conversion,
+// saturating packs and -127 floor change nothing, so no clamp or range test
+// is needed.  Checked against q8_code_bits over every such p by
+// v7g_selftest_arith.
+__device__ __forceinline__ uint32_t q8_codes4_small(float4 h, float recip)
+{
+	const float2 p01 = mul2(make_float2(h.x, h.y), splat2(recip));
+	const float2 p23 = mul2(make_float2(h.z, h.w), splat2(recip));
+	const float2 b01 = add2(p01, splat2(kRoundMagic));
+	const float2 b23 = add2(p23, splat2(kRoundMagic));
+	return pack4_low_bytes(__float_as_uint(b01.x), __float_as_uint(b01.y), __float_as_uint(b23.x), __float_as_uint(b23.y));
 }
 
 // q8_codes4 with pair arithmetic.

@@ -9,6 +9,8 @@
 //           of p = h * recip (recip = 1, so p = h)
 //   test 4  q8_scale_fast == q8_scale (scale and reciprocal) for every normal
 //           absmax in [2^-127, 2^128) plus inf and NaN
+//   test 5  q8_codes4_small code == q8_code_bits code for every p with
+//           |p| < 127.5 (recip = 1, so p = h)
 // The counts of mismatches are the kernel's output (all zero when the fast
 // forms are exact over their whole input range).
 #include "internal.h"
@@ -25,7 +27,7 @@ __global__ void __launch_bounds__(kBlock) k_selftest(unsigned long long *counts)
 {
 	const uint64_t stride = (uint64_t)gridDim.x * kBlock;
 	const uint64_t tid = (uint64_t)blockIdx.x * kBlock + threadIdx.x;
-	unsigned long long bad[5] = {0, 0, 0, 0, 0};
+	unsigned long long bad[6] = {0, 0, 0, 0, 0, 0};
 	// test 0: exponents -126 .. 125
 	for (uint64_t i = tid; i < (252ull << 23); i += stride) {
 		const float d = from_exp_mant((int)(i >> 23) - 126, (uint32_t)(i & 0x7fffff));
@@ -62,7 +64,14 @@ __global__ void __launch_bounds__(kBlock) k_selftest(unsigned long long *counts)
 		const bool same_r = __float_as_uint(r_fast) == __float_as_uint(r_ref) || (r_fast != r_fast && r_ref != r_ref);
 		bad[4] += !(same_s && same_r);
 	}
-	for (int t = 0; t < 5; ++t)
+	// test 5: magnitudes below 127.5 (bit patterns up to 0x42FEFFFF), both signs
+	for (uint64_t i = tid; i < 0x42ff0000ull; i += stride) {
+		const float p0 = __uint_as_float((uint32_t)i), p1 = __uint_as_float((uint32_t)i | 0x80000000u);
+		const uint32_t packed = q8_codes4_small(make_float4(p0, p1, p1, p0), 1.0f);
+		const uint32_t want = pack4_low_bytes(q8_code_bits(p0), q8_code_bits(p1), q8_code_bits(p1), q8_code_bits(p0));
+		bad[5] += packed != want;
+	}
+	for (int t = 0; t < 6; ++t)
 		if (bad[t])
 			atomicAdd(counts + t, bad[t]);
 }
