@@ -157,6 +157,26 @@ int v7g_swiglu_f32q8_gemv(float *out, const float *x, const int8_t *gate_q, cons
    rows it was computing).  0 in every correct run. */
 unsigned int v7g_pipeline_timeouts(void);
 
+/* RMSNorm rows on HOST buffers with no device allocation.  No counterpart in
+   the reference: it is the host-buffer path of v7s_rmsnorm for callers that
+   must not have a library allocate device memory -- a program that shares the
+   GPU with a framework whose caching allocator holds nearly all of it, a
+   latency-critical loop that cannot take the device-wide synchronisation of
+   cudaMalloc / cudaFree, or a deployment that forbids allocation after
+   start-up.  o, x [rows, n] and w [n] may be host (pageable or pinned) or
+   device memory; they are staged through a static device array of
+   V7G_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds until the
+   process exits.  Work beyond that (gamma plus x and o, each rounded up to 256
+   bytes) is rejected with V7G_ERR_ARG.  The first call on a device looks up
+   the array's device address (cudaGetSymbolAddress), so make it before any
+   stream capture.  Synchronous: returns when o is written.  Calls share the
+   array; they are serialised and each waits for `stream`, so they never
+   overlap on the GPU -- calls that did overlap would race.  Nothing needs
+   clearing between calls: each copies its whole input in and output out.
+   Results equal v7g_rmsnorm_rows bit for bit.  Contract: n % 32 == 0. */
+#define V7G_NOALLOC_SCRATCH_BYTES (4u << 20)
+int v7g_rmsnorm_rows_noalloc(float *o, const float *x, const float *w, int64_t rows, int n, float eps, void *stream);
+
 /* ---- runtime ---------------------------------------------------------- */
 
 /* RMS epsilon used by the reference-ABI entries (v7s_rmsnorm & co.), which

@@ -31,6 +31,7 @@ from .ops import (  # noqa: F401
     rmsnorm_quantize_rows,
     rmsnorm_rope_rows,
     rmsnorm_rows,
+    rmsnorm_rows_noalloc,
     rope_freqs,
     rope_init,
     rope_only_rows,

@@ -33,7 +33,7 @@ NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xptxas"
 CXX_FLAGS = ["-O2", "-std=c++17", "-fPIC", "-Wall", "-Wno-unused-parameter", f"-I{CUDA_HOME / 'include'}"]
 
 KERNEL_SOURCES = ["runtime.cu", "norm.cu", "norm_q8.cu", "rope.cu", "rope_only.cu", "rope_tables.cu", "swiglu.cu", "add.cu",
-                  "gemv.cu", "selftest.cu"]
+                  "gemv.cu", "noalloc.cu", "selftest.cu"]
 # Units whose kernels the reference runs with MXCSR FTZ+DAZ and that use the
 # packed-pair intrinsics, whose denormal mode follows -ftz (csrc/arith.cuh).
 # Explicit-PTX arithmetic elsewhere carries its own .ftz or not.

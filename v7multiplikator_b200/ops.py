@@ -67,7 +67,11 @@ _SIGNATURES = {
                            c_void_p],
     "v7g_swiglu_f32q8_gemv": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int,
                               c_void_p],
+    "v7g_rmsnorm_rows_noalloc": [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_float, c_void_p],
 }
+
+# Size of the static device staging array of rmsnorm_rows_noalloc (per GPU).
+NOALLOC_SCRATCH_BYTES = 4 << 20
 
 # Positions of the tables rope_init builds (V7G_ROPE_TABLE_POSITIONS).
 ROPE_TABLE_POSITIONS = 131072
@@ -398,6 +402,24 @@ def swiglu_f32q8_gemv(out: torch.Tensor, x: torch.Tensor, gate_q: torch.Tensor, 
         _want(out, "out", torch.float32, dv), _want(x, "x", torch.float32, dv),
         _want(gate_q, "gate_q", torch.int8, dv), _want(gate_s, "gate_s", torch.float32, dv),
         _want(up_q, "up_q", torch.int8, dv), _want(up_s, "up_s", torch.float32, dv), batch, n, d, _stream(x, stream)))
+    return out
+
+
+def rmsnorm_rows_noalloc(out, x, weight, eps: float, stream: Optional[torch.cuda.Stream] = None):
+    """rmsnorm_rows for callers that must not have the library allocate
+    device memory: host numpy arrays (or any memory the GPU can address) go
+    through a static device array of NOALLOC_SCRATCH_BYTES per GPU, so the
+    call never reaches cudaMalloc.  Synchronous; raises V7GError when
+    gamma + x + out do not fit in the array."""
+    import numpy as np
+    for name, a in (("out", out), ("x", x), ("weight", weight)):
+        if not isinstance(a, np.ndarray) or a.dtype != np.float32 or not a.flags.c_contiguous:
+            raise TypeError(f"{name} must be a C-contiguous float32 numpy array")
+    if x.ndim != 2 or out.shape != x.shape or weight.size != x.shape[1]:
+        raise ValueError("shape mismatch: x and out [rows, n], weight [n]")
+    s = stream.cuda_stream if stream is not None else None
+    _check(lib().v7g_rmsnorm_rows_noalloc(out.ctypes.data, x.ctypes.data, weight.ctypes.data, x.shape[0], x.shape[1],
+                                          eps, s))
     return out
 
 
