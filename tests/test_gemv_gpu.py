@@ -135,6 +135,12 @@ def test_gemv_pipeline_and_direct_kernels_agree(cuda, oracle, n, d):
         v7g.swiglu_q8_gemv(out, dev(xq), dev(xs), gt, dev(gs), ut, dev(us))
         with np.errstate(all="ignore"):
             assert_same_f32(host(out), want, f"weights offset {shift}")
+        # the fp32-activation kernel on the same weights
+        xf = rng.normal(0, 1, (2, n)).astype(F)
+        out2 = torch.empty(2, d, device=cuda)
+        v7g.swiglu_f32q8_gemv(out2, dev(xf), gt, dev(gs), ut, dev(us))
+        with np.errstate(all="ignore"):
+            assert_same_f32(host(out2), oracle.swiglu_f32q8_gemv(xf, gq, gs, uq, us), f"fp32 activation, offset {shift}")
     assert v7g.pipeline_timeouts() == before == 0
 
 

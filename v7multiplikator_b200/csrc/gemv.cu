@@ -23,6 +23,7 @@
 // and scales are staged once per CTA in shared memory.  Loads for kUnroll
 // groups are issued before their arithmetic.  The weights are read exactly
 // once: HBM-bound at d x n x (1 + 4/64) bytes per matrix.
+#include "arith.cuh"
 #include "internal.h"
 #include "pipeline.cuh"
 #include "q8.cuh"
@@ -271,11 +272,53 @@ __device__ __forceinline__ void chunk_chains(float (&acc)[NM], const uint32_t *s
 	}
 }
 
+// fp32 activation x Q8 weights over the gk groups of a stage for row lane l
+// (elements e = l mod 8), gate and up as the two halves of a pair: the
+// weight byte to float by placing it in the mantissa of 2^23 + 128 and
+// subtracting (exact), times its group scale (rounded), fused multiply-add
+// with x_e -- the dual-row arithmetic of swiglu_kernel.inc:30-47.  The lane's
+// byte of step k is byte l % 4 of word 2k + l / 4 of the group.  st: the row's
+// gate slot (up at + R slots); xl: the lane's activations from the first
+// group, 8 per group; sw: the row's gate scales (up at + R * sstride).
+template <int R>
+__device__ __forceinline__ void chunk_f32(float (&acc)[2], const uint32_t *st, const float *xl, const float *sw, int sstride, int l, int gk)
+{
+	const bool odd = (l & 4) != 0;
+	const uint32_t sel = 0x7540u | (uint32_t)(l & 3); // byte l % 4, then 0, 0, 0x4B
+	const float2 bias = splat2(-8388736.0f);            // -(2^23 + 128)
+	float2 a = make_float2(acc[0], acc[1]);
+#pragma unroll 2
+	for (int gi = 0; gi < gk; ++gi) {
+		const uint4 *wg = reinterpret_cast<const uint4 *>(st + gi * 16);
+		const uint4 *wu = reinterpret_cast<const uint4 *>(st + R * (kRowSlot / 4) + gi * 16);
+		const float4 x0 = *reinterpret_cast<const float4 *>(xl + gi * 8);
+		const float4 x1 = *reinterpret_cast<const float4 *>(xl + gi * 8 + 4);
+		const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+		const float2 sc = make_float2(sw[gi], sw[R * sstride + gi]);
+#pragma unroll
+		for (int j = 0; j < 4; ++j) {
+			const uint4 g4 = wg[j], u4 = wu[j];
+			const uint32_t gw[2] = {odd ? g4.y : g4.x, odd ? g4.w : g4.z};
+			const uint32_t uw[2] = {odd ? u4.y : u4.x, odd ? u4.w : u4.z};
+#pragma unroll
+			for (int h = 0; h < 2; ++h) {
+				const float2 raw = make_float2(__uint_as_float(__byte_perm(gw[h] ^ 0x80808080u, 0x4B000000u, sel)),
+				                               __uint_as_float(__byte_perm(uw[h] ^ 0x80808080u, 0x4B000000u, sel)));
+				a = fma2(splat2(xv[2 * j + h]), mul2(add2(raw, bias), sc), a);
+			}
+		}
+	}
+	acc[0] = a.x;
+	acc[1] = a.y;
+}
+
+// MODE 0: v7d_q8, 1: v7d_swiglu_q8, 2: v7d_swiglu (fp32 activation; the
+// activation is staged transposed, lane-major, instead of as codes).
 template <int MODE, bool FUSED, int R>
-__global__ void __launch_bounds__(R * kLanes + 32) k_q8_gemv_tma(GemvArgs p, int stages)
+__global__ void __launch_bounds__(R * kLanes + 32, 2) k_q8_gemv_tma(GemvArgs p, int stages)
 {
 	using M = F<true>;
-	constexpr int NM = MODE == 1 ? 2 : 1;
+	constexpr int NM = MODE == 0 ? 1 : 2;
 	constexpr int kConsumers = R * kLanes;
 	constexpr int kStageBytes = NM * R * kRowSlot;
 	extern __shared__ __align__(128) unsigned char smem[];
@@ -283,14 +326,17 @@ __global__ void __launch_bounds__(R * kLanes + 32) k_q8_gemv_tma(GemvArgs p, int
 	const int nchunks = (groups + kChunkGroups - 1) / kChunkGroups;
 	const int64_t row0 = (int64_t)blockIdx.x * R;
 	const int rows = (int)min((int64_t)R, p.d - row0);
-	// layout: stages | activation codes [n] | activation scales [groups] |
-	// combined scales [NM][R][groups + 1] | full[stages] | empty[stages]
+	// layout: stages | activation codes [n] and scales [groups] (MODE 2: the
+	// fp32 activation, lane-major [8][xstride]) | weight or combined scales
+	// [NM][R][groups + 1] | full[stages] | empty[stages]
 	const int sstride = groups + 1; // odd row stride: the warp's four rows hit four banks
+	const int xstride = groups * 8 + 4; // MODE 2: padded so the 8 lanes' rows start 4 banks apart
 	unsigned char *ring = smem;
 	uint32_t *sq = reinterpret_cast<uint32_t *>(smem + (size_t)stages * kStageBytes);
-	float *ss = reinterpret_cast<float *>(reinterpret_cast<unsigned char *>(sq) + n);
-	float *sws = ss + groups;
-	uint64_t *full = reinterpret_cast<uint64_t *>(sws + NM * R * sstride + ((NM * R * sstride + groups) & 1));
+	float *xt = reinterpret_cast<float *>(sq);
+	float *ss = reinterpret_cast<float *>(reinterpret_cast<unsigned char *>(sq) + (MODE == 2 ? 32 * xstride : n));
+	float *sws = ss + (MODE == 2 ? 0 : groups);
+	uint64_t *full = reinterpret_cast<uint64_t *>(sws + NM * R * sstride + ((NM * R * sstride + (MODE == 2 ? 0 : groups)) & 1));
 	uint64_t *empty = full + stages;
 	const int64_t b = blockIdx.y;
 	if (threadIdx.x == 0) {
@@ -335,7 +381,11 @@ __global__ void __launch_bounds__(R * kLanes + 32) k_q8_gemv_tma(GemvArgs p, int
 		return;
 	}
 	// consumers: stage the activation and the weight scales, then the chains
-	if (FUSED) {
+	if (MODE == 2) {
+		const float *xb = p.xf + b * n;
+		for (int i = threadIdx.x; i < n; i += kConsumers)
+			xt[(i & 7) * xstride + (i >> 6) * 8 + ((i >> 3) & 7)] = __ldg(xb + i);
+	} else if (FUSED) {
 		stage_quantized(p.xf + b * n, n, sq, ss, kConsumers);
 	} else {
 		const uint4 *src = reinterpret_cast<const uint4 *>(p.xq + b * n);
@@ -352,12 +402,14 @@ __global__ void __launch_bounds__(R * kLanes + 32) k_q8_gemv_tma(GemvArgs p, int
 		for (int i = threadIdx.x; i < rows * groups; i += kConsumers)
 			sws[(m * R + i / groups) * sstride + i % groups] = __ldg(p.ws[m] + row0 * groups + i);
 	named_sync(1, kConsumers);
-	for (int m = 0; m < NM; ++m)
-		for (int i = threadIdx.x; i < rows * groups; i += kConsumers) {
-			float *c = sws + (m * R + i / groups) * sstride + i % groups;
-			*c = M::mul(*c, ss[i % groups]);
-		}
-	named_sync(1, kConsumers);
+	if (MODE != 2) {
+		for (int m = 0; m < NM; ++m)
+			for (int i = threadIdx.x; i < rows * groups; i += kConsumers) {
+				float *c = sws + (m * R + i / groups) * sstride + i % groups;
+				*c = M::mul(*c, ss[i % groups]);
+			}
+		named_sync(1, kConsumers);
+	}
 	const int r = threadIdx.x >> 3, l = threadIdx.x & (kLanes - 1);
 	const bool valid = r < rows;
 	float acc[NM];
@@ -377,7 +429,9 @@ __global__ void __launch_bounds__(R * kLanes + 32) k_q8_gemv_tma(GemvArgs p, int
 		if (valid) {
 			const uint32_t *st = reinterpret_cast<const uint32_t *>(ring + (size_t)s * kStageBytes) + r * (kRowSlot / 4);
 			const float *cs = sws + r * sstride + g0;
-			if (gk == kChunkGroups)
+			if constexpr (MODE == 2)
+				chunk_f32<R>(acc, st, xt + l * xstride + g0 * 8, cs, sstride, l, gk);
+			else if (gk == kChunkGroups)
 				chunk_chains<NM, R, kChunkGroups>(acc, st, sq + g0 * 16, cs, sstride, l, kChunkGroups);
 			else
 				chunk_chains<NM, R, kChunkGroups>(acc, st, sq + g0 * 16, cs, sstride, l, gk);
@@ -391,14 +445,16 @@ __global__ void __launch_bounds__(R * kLanes + 32) k_q8_gemv_tma(GemvArgs p, int
 	for (int m = 0; m < NM; ++m)
 		res[m] = hadd_lanes(acc[m]);
 	if (ok && valid && l == 0)
-		p.out[b * p.d + row0 + r] = MODE == 1 ? v7_swiglu(res[0], res[1]) : res[0];
+		p.out[b * p.d + row0 + r] = MODE == 0 ? res[0] : v7_swiglu(res[0], res[NM - 1]);
 }
 
 // Shared memory of k_q8_gemv_tma for `stages` stages.
-size_t tma_smem(int nm, int rows, int n, int stages)
+size_t tma_smem(int mode, int rows, int n, int stages)
 {
+	const int nm = mode == 0 ? 1 : 2;
 	const int groups = n / kQ8Group;
-	const size_t fixed = (size_t)n + 4 * ((size_t)groups + (size_t)nm * rows * (groups + 1)) + 8 + 16 * (size_t)stages;
+	const size_t act = mode == 2 ? 32 * ((size_t)groups * 8 + 4) : (size_t)n + 4 * (size_t)groups;
+	const size_t fixed = act + 4 * (size_t)nm * rows * (groups + 1) + 8 + 16 * (size_t)stages;
 	return (size_t)stages * nm * rows * kRowSlot + fixed;
 }
 
@@ -482,16 +538,15 @@ int launch_gemv_tma(const char *what, const GemvArgs &a, int64_t batch, void *st
 	int rc = current_device(&dev);
 	if (rc != V7G_OK)
 		return rc;
-	constexpr int NM = MODE == 1 ? 2 : 1;
 	const bool wide = a.d >= 2 * 16 * (int64_t)dev.sm_count;
 	const int R = wide ? 16 : 8;
 	// up to 4 stages while a CTA stays under ~112 KB (two per SM), at least 2
 	int stages = 4;
-	while (stages > 2 && tma_smem(NM, R, a.n, stages) > 112 * 1024)
+	while (stages > 2 && tma_smem(MODE, R, a.n, stages) > 112 * 1024)
 		--stages;
-	while (stages > 2 && tma_smem(NM, R, a.n, stages) > kTmaSmemBudget)
+	while (stages > 2 && tma_smem(MODE, R, a.n, stages) > kTmaSmemBudget)
 		--stages;
-	const size_t smem = tma_smem(NM, R, a.n, stages);
+	const size_t smem = tma_smem(MODE, R, a.n, stages);
 	if (smem > kTmaSmemBudget)
 		return V7G_ERR_UNSUPPORTED;
 	const void *kernel = wide ? (const void *)k_q8_gemv_tma<MODE, FUSED, 16> : (const void *)k_q8_gemv_tma<MODE, FUSED, 8>;
@@ -586,6 +641,11 @@ int v7g_swiglu_f32q8_gemv(float *out, const float *x, const int8_t *gate_q, cons
 	if (!x || !gate_q || !gate_s || !up_q || !up_s)
 		return set_error(V7G_ERR_ARG, "%s: NULL pointer", what);
 	GemvArgs a{out, nullptr, nullptr, x, {gate_q, up_q}, {gate_s, up_s}, n, d};
+	if (aligned16(gate_q) && aligned16(up_q)) {
+		const int rc2 = launch_gemv_tma<2, false>(what, a, batch, stream);
+		if (rc2 != V7G_ERR_UNSUPPORTED)
+			return rc2;
+	}
 	return launch_gemv(k_f32q8_swiglu_gemv, what, a, batch, 0, stream);
 }
 
