@@ -102,21 +102,34 @@ struct GemvArgs {
 // float4 per lane; `nthreads` (a multiple of 32) threads take part.
 __device__ void stage_quantized(const float *x, int n, uint32_t *sq, float *ss, int nthreads = kBlock)
 {
+	constexpr int U = 8; // group pairs per warp loaded before any is processed: one L2 latency per U
 	const int lane = threadIdx.x & 31, half = lane >> 4, hl = lane & 15;
 	const int groups = n / kQ8Group;
+	const int step = (nthreads / 32) * 2;
 	const bool vec = (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
-	for (int g = (threadIdx.x >> 5) * 2 + half; g - half < groups; g += (nthreads / 32) * 2) {
-		float4 h = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-		if (g < groups) {
-			const float *p = x + (int64_t)g * kQ8Group + 4 * hl;
-			h = vec ? __ldg(reinterpret_cast<const float4 *>(p)) : make_float4(__ldg(p), __ldg(p + 1), __ldg(p + 2), __ldg(p + 3));
+	for (int g0 = (threadIdx.x >> 5) * 2; g0 < groups; g0 += U * step) {
+		float4 h[U];
+#pragma unroll
+		for (int u = 0; u < U; ++u) {
+			const int g = g0 + u * step + half;
+			h[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+			if (g < groups) {
+				const float *p = x + (int64_t)g * kQ8Group + 4 * hl;
+				h[u] = vec ? __ldg(reinterpret_cast<const float4 *>(p)) : make_float4(__ldg(p), __ldg(p + 1), __ldg(p + 2), __ldg(p + 3));
+			}
 		}
-		float scale, recip;
-		q8_scale(group_absmax_f4(h, lane), scale, recip);
-		if (g < groups) {
-			sq[g * 16 + hl] = q8_codes4(h, recip);
-			if (hl == 0)
-				ss[g] = scale;
+#pragma unroll
+		for (int u = 0; u < U; ++u) {
+			if (g0 + u * step >= groups) // warp-uniform: both halves stop together
+				break;
+			const int g = g0 + u * step + half;
+			float scale, recip;
+			q8_scale(group_absmax_f4(h[u], lane), scale, recip);
+			if (g < groups) {
+				sq[g * 16 + hl] = q8_codes4(h[u], recip);
+				if (hl == 0)
+					ss[g] = scale;
+			}
 		}
 	}
 }

@@ -13,6 +13,9 @@ namespace v7g {
 namespace {
 
 constexpr int kBlock = 256;
+// four CTAs per SM (at most 64 registers a thread): 4096 rows of one warp each
+// fit in one wave on 148 SMs, with no half-empty second wave
+constexpr int kMinBlocks = 4;
 constexpr int kWarpsPerBlock = kBlock / 32;
 
 // --- A1  RMSNorm rows (rmsnorm_kernel.inc:12-75), caller's MXCSR: no FTZ ---
@@ -23,7 +26,7 @@ constexpr int kWarpsPerBlock = kBlock / 32;
 // chain (measured on B200: +17 % over the unpipelined form, and well ahead of
 // holding the whole row in registers, which limits residency).
 template <int C>
-__global__ void __launch_bounds__(kBlock) k_rmsnorm_rows(float *o, const float *x, const float *__restrict__ w, int64_t rows, int n, float eps)
+__global__ void __launch_bounds__(kBlock, kMinBlocks) k_rmsnorm_rows(float *o, const float *x, const float *__restrict__ w, int64_t rows, int n, float eps)
 {
 	using M = F<false>;
 	const int lane = threadIdx.x & 31;
@@ -82,7 +85,7 @@ __global__ void __launch_bounds__(kBlock) k_rmsnorm_rows(float *o, const float *
 // writes the new residual as it goes; pass 2 re-reads it (L2) for the output;
 // both pipelined as in k_rmsnorm_rows.
 template <int C>
-__global__ void __launch_bounds__(kBlock) k_fused_add_rmsnorm_rows(float *o, float *res, const float *add, const float *__restrict__ w, int64_t rows, int n, float eps)
+__global__ void __launch_bounds__(kBlock, kMinBlocks) k_fused_add_rmsnorm_rows(float *o, float *res, const float *add, const float *__restrict__ w, int64_t rows, int n, float eps)
 {
 	using M = F<false>;
 	const int lane = threadIdx.x & 31;
@@ -162,9 +165,9 @@ __global__ void __launch_bounds__(kBlock) k_fused_add_rmsnorm_rows(float *o, flo
 	}
 }
 
-// slots per lane per pipelined chunk (measured best on B200 for 2048-wide rows)
-constexpr int kRmsChunk = 16;
-constexpr int kAddChunk = 8;
+// slots per lane per pipelined chunk: as deep as 64 registers allow without spills
+constexpr int kRmsChunk = 12;
+constexpr int kAddChunk = 6;
 
 // `oversubscribe` x the resident CTAs, at most one warp per row.
 template <typename Kernel, typename... Args>
