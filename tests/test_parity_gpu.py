@@ -60,7 +60,8 @@ def test_selftest_arith_exhaustive(cuda):
 # --------------------------------------------------------------- RMSNorm rows
 
 
-@pytest.mark.parametrize("rows,n", [(1, 32), (3, 64), (17, 96), (64, 2048), (5, 3072), (2, 8192), (7, 4096), (300, 256)])
+@pytest.mark.parametrize("rows,n", [(1, 32), (3, 64), (17, 96), (64, 2048), (5, 3072), (2, 8192), (7, 4096), (300, 256),
+                                    (1025, 96), (2000, 2048)])
 @pytest.mark.parametrize("eps", [0.0, 1e-6])
 def test_rmsnorm_rows(cuda, oracle, rows, n, eps):
     import v7multiplikator_b200 as v7g
@@ -107,7 +108,8 @@ def test_rmsnorm_reference_validator_cases(cuda, oracle, golden, size, seed):
 # --------------------------------------------------- fused add + RMSNorm rows
 
 
-@pytest.mark.parametrize("rows,n", [(1, 8), (3, 16), (2, 24), (5, 48), (4, 64), (33, 2048), (3, 3072), (2, 8192), (9, 40)])
+@pytest.mark.parametrize("rows,n", [(1, 8), (3, 16), (2, 24), (5, 48), (4, 64), (33, 2048), (3, 3072), (2, 8192), (9, 40),
+                                    (1025, 40), (2000, 2048)])
 def test_fused_add_rmsnorm_rows(cuda, oracle, rows, n):
     import v7multiplikator_b200 as v7g
     rng = np.random.default_rng(rows * 7 + n)

@@ -25,8 +25,8 @@ constexpr int kWarpsPerBlock = kBlock / 32;
 // chunk k0's arithmetic, so a warp keeps C loads in flight through its FMA
 // chain (measured on B200: +17 % over the unpipelined form, and well ahead of
 // holding the whole row in registers, which limits residency).
-template <int C>
-__global__ void __launch_bounds__(kBlock, kMinBlocks) k_rmsnorm_rows(float *o, const float *x, const float *__restrict__ w, int64_t rows, int n, float eps)
+template <int C, int MINB = kMinBlocks>
+__global__ void __launch_bounds__(kBlock, MINB) k_rmsnorm_rows(float *o, const float *x, const float *__restrict__ w, int64_t rows, int n, float eps)
 {
 	using M = F<false>;
 	const int lane = threadIdx.x & 31;
@@ -84,8 +84,8 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) k_rmsnorm_rows(float *o, c
 // groups from block L on; chain lane l then covers e = 8L + l + 32k.  Pass 1
 // writes the new residual as it goes; pass 2 re-reads it (L2) for the output;
 // both pipelined as in k_rmsnorm_rows.
-template <int C>
-__global__ void __launch_bounds__(kBlock, kMinBlocks) k_fused_add_rmsnorm_rows(float *o, float *res, const float *add, const float *__restrict__ w, int64_t rows, int n, float eps)
+template <int C, int MINB = kMinBlocks>
+__global__ void __launch_bounds__(kBlock, MINB) k_fused_add_rmsnorm_rows(float *o, float *res, const float *add, const float *__restrict__ w, int64_t rows, int n, float eps)
 {
 	using M = F<false>;
 	const int lane = threadIdx.x & 31;
@@ -168,6 +168,13 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) k_fused_add_rmsnorm_rows(f
 // slots per lane per pipelined chunk: as deep as 64 registers allow without spills
 constexpr int kRmsChunk = 12;
 constexpr int kAddChunk = 6;
+// Few rows (a decode step, a single vector) leave the GPU mostly idle and
+// the time is the row's own latency: then a deeper chunk without the
+// occupancy cap puts a 2048-wide row's loads in flight at once.  Same
+// arithmetic in the same order, so results are identical.
+constexpr int64_t kFewRows = 1024;
+constexpr int kRmsChunkFew = 32;
+constexpr int kAddChunkFew = 16;
 
 // `oversubscribe` x the resident CTAs, at most one warp per row.
 template <typename Kernel, typename... Args>
@@ -203,6 +210,8 @@ int v7g_rmsnorm_rows(float *o, const float *x, const float *w, int64_t rows, int
 		return clear_error();
 	if (!o || !x || !w)
 		return set_error(V7G_ERR_ARG, "v7g_rmsnorm_rows: NULL pointer");
+	if (rows <= kFewRows)
+		return launch_rows(k_rmsnorm_rows<kRmsChunkFew, 1>, "v7g_rmsnorm_rows", rows, 1, stream, o, x, w, rows, n, eps);
 	return launch_rows(k_rmsnorm_rows<kRmsChunk>, "v7g_rmsnorm_rows", rows, 1, stream, o, x, w, rows, n, eps);
 }
 
@@ -216,6 +225,8 @@ int v7g_fused_add_rmsnorm_rows(float *o, float *residual, const float *add, cons
 		return clear_error();
 	if (!o || !residual || !add || !w)
 		return set_error(V7G_ERR_ARG, "v7g_fused_add_rmsnorm_rows: NULL pointer");
+	if (rows <= kFewRows)
+		return launch_rows(k_fused_add_rmsnorm_rows<kAddChunkFew, 1>, "v7g_fused_add_rmsnorm_rows", rows, 4, stream, o, residual, add, w, rows, n, eps);
 	return launch_rows(k_fused_add_rmsnorm_rows<kAddChunk>, "v7g_fused_add_rmsnorm_rows", rows, 4, stream, o, residual, add, w, rows, n, eps);
 }
 
