@@ -62,14 +62,22 @@ __device__ __forceinline__ float group_absmax8(const float (&h)[8], int q, uint3
 	return __uint_as_float(mb);
 }
 
+// Codes of a group holding an inf or a NaN: the general conversion with its
+// range tests.  Out of line so that the common finite case stays a short
+// straight path instead of both forms being computed and selected.
+__device__ __noinline__ uint2 codes8_general(float4 h0, float4 h1, float recip)
+{
+	return make_uint2(q8_codes4_x2(h0, recip), q8_codes4_x2(h1, recip));
+}
+
 // Pass 1 accumulates the sum of squares in the chain layout (lane l: elements
-// l + 32k, pipelined as in norm.cu).  Pass 2 re-reads the row from L2 in the
-// quantiser's layout -- four 64-element groups per warp, eight consecutive
-// floats per lane, so the per-group work (absmax reduction, scale,
-// reciprocal) is shared by four groups per instruction -- normalises as
-// (scale * x) * w and quantises; the loads of the next four groups are issued
-// before the current ones are processed.  x and w must be 16-byte aligned,
-// codes 8-byte aligned.
+// l + 32k) in unguarded chunks of C loads.  Pass 2 re-reads the row from L2 in
+// the quantiser's layout -- four 64-element groups per warp, eight
+// consecutive floats per lane, so the per-group work (absmax reduction,
+// scale, reciprocal) is shared by four groups per instruction -- normalises
+// as (scale * x) * w and quantises.  Latency is covered by the four resident
+// CTAs per SM rather than by prefetch buffers, which cost register moves on
+// every element.  x and w must be 16-byte aligned, codes 8-byte aligned.
 template <int C>
 __global__ void __launch_bounds__(kBlock, kMinBlocks) k_rmsnorm_quantize_rows(uint2 *codes, float *scales, const float *x, const float *__restrict__ w, int64_t rows, int n, float eps)
 {
@@ -85,24 +93,21 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) k_rmsnorm_quantize_rows(ui
 	for (int64_t row = ((int64_t)blockIdx.x * kBlock + threadIdx.x) >> 5; row < rows; row += nwarps) {
 		const float *xr = x + row * n + lane;
 		float acc = 0.0f;
-		float v[C];
-#pragma unroll
-		for (int k = 0; k < C; ++k)
-			if (k < vpl)
-				v[k] = xr[32 * k];
-		for (int k0 = 0; k0 < vpl; k0 += C) {
-			float vn[C];
+		// full chunks: C loads in flight per lane, no per-slot guards (the
+		// resident warps, not a prefetch buffer, cover the latency)
+		int k0 = 0;
+		for (; k0 + C <= vpl; k0 += C) {
+			float v[C];
 #pragma unroll
 			for (int k = 0; k < C; ++k)
-				if (k0 + C + k < vpl)
-					vn[k] = xr[32 * (k0 + C + k)];
+				v[k] = xr[32 * (k0 + k)];
 #pragma unroll
 			for (int k = 0; k < C; ++k)
-				if (k0 + k < vpl)
-					acc = M::fma(v[k], v[k], acc);
-#pragma unroll
-			for (int k = 0; k < C; ++k)
-				v[k] = vn[k];
+				acc = M::fma(v[k], v[k], acc);
+		}
+		for (; k0 < vpl; ++k0) {
+			const float v = xr[32 * k0];
+			acc = M::fma(v, v, acc);
 		}
 		const float scale = rms_scale<true>(reduce_chains_4x8<true>(acc), nf, eps);
 		const float4 *x4 = reinterpret_cast<const float4 *>(x + row * n);
@@ -120,46 +125,47 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) k_rmsnorm_quantize_rows(ui
 				}
 			}
 		};
-		float4 xv[2], wv[2];
-		load(0, xv, wv);
-		for (int j = 0; 4 * j < ngr; ++j) {
-			float4 xn[2], wn[2];
-			load(j + 1, xn, wn);
-			const int g = 4 * j + slot;
-			// (scale * x) * w, the reference's order (rmsnorm_quantize_kernel.inc:52-57)
-			float h[8];
+		// two rounds of four groups per L2 round trip
+		for (int j = 0; 4 * j < ngr; j += 2) {
+			float4 xv[2][2], wv[2][2];
+			load(j, xv[0], wv[0]);
+			load(j + 1, xv[1], wv[1]);
 #pragma unroll
-			for (int u = 0; u < 2; ++u) {
-				const float2 h01 = mul2(mul2(s2, make_float2(xv[u].x, xv[u].y)), make_float2(wv[u].x, wv[u].y));
-				const float2 h23 = mul2(mul2(s2, make_float2(xv[u].z, xv[u].w)), make_float2(wv[u].z, wv[u].w));
-				h[4 * u] = h01.x;
-				h[4 * u + 1] = h01.y;
-				h[4 * u + 2] = h23.x;
-				h[4 * u + 3] = h23.y;
-			}
-			float gscale, recip;
-			uint32_t maxbits;
-			q8_scale_fast(group_absmax8(h, q, maxbits), gscale, recip);
-			if (g < ngr) {
-				const float4 h0 = make_float4(h[0], h[1], h[2], h[3]), h1 = make_float4(h[4], h[5], h[6], h[7]);
-				// a finite group's products stay within 127.5: the short code path
-				const uint2 c = maxbits <= 0x7f7fffffu ? make_uint2(q8_codes4_small(h0, recip), q8_codes4_small(h1, recip))
-				                                      : make_uint2(q8_codes4_x2(h0, recip), q8_codes4_x2(h1, recip));
-				__stcs(qr + g * 8 + q, c);
-				if (q == 0)
-					__stcs(sr + g, gscale);
-			}
+			for (int t = 0; t < 2; ++t) {
+				if (4 * (j + t) >= ngr) // warp-uniform
+					break;
+				const int g = 4 * (j + t) + slot;
+				// (scale * x) * w, the reference's order (rmsnorm_quantize_kernel.inc:52-57)
+				float h[8];
 #pragma unroll
-			for (int u = 0; u < 2; ++u) {
-				xv[u] = xn[u];
-				wv[u] = wn[u];
+				for (int u = 0; u < 2; ++u) {
+					const float2 h01 = mul2(mul2(s2, make_float2(xv[t][u].x, xv[t][u].y)), make_float2(wv[t][u].x, wv[t][u].y));
+					const float2 h23 = mul2(mul2(s2, make_float2(xv[t][u].z, xv[t][u].w)), make_float2(wv[t][u].z, wv[t][u].w));
+					h[4 * u] = h01.x;
+					h[4 * u + 1] = h01.y;
+					h[4 * u + 2] = h23.x;
+					h[4 * u + 3] = h23.y;
+				}
+				float gscale, recip;
+				uint32_t maxbits;
+				q8_scale_fast(group_absmax8(h, q, maxbits), gscale, recip);
+				if (g < ngr) {
+					const float4 h0 = make_float4(h[0], h[1], h[2], h[3]), h1 = make_float4(h[4], h[5], h[6], h[7]);
+					// a finite group's products stay within 127.5: the short code path
+					uint2 c = make_uint2(q8_codes4_small(h0, recip), q8_codes4_small(h1, recip));
+					if (maxbits > 0x7f7fffffu)
+						c = codes8_general(h0, h1, recip);
+					__stcs(qr + g * 8 + q, c);
+					if (q == 0)
+						__stcs(sr + g, gscale);
+				}
 			}
 		}
 	}
 }
 
 // slots per lane per pipelined chunk of the sum-of-squares pass
-constexpr int kChunk = 8;
+constexpr int kChunk = 32;
 
 template <typename Kernel, typename... Args>
 int launch_rows(Kernel kernel, const char *what, int64_t rows, void *stream, Args... args)

@@ -58,6 +58,14 @@ __device__ __forceinline__ float4 v7_swiglu4(float4 g, float4 u)
 // exact.  The reciprocal takes the Markstein form.  An inf or a NaN that
 // survived the tree takes the IEEE instructions.  v7g_selftest_arith checks
 // scale and reciprocal against div.rn / rcp.rn for every possible maximum.
+// The IEEE instructions for an inf or NaN maximum, out of line (rare).
+static __device__ __noinline__ float2 q8_scale_ieee(float wmax)
+{
+	float scale, recip;
+	q8_scale(wmax, scale, recip);
+	return make_float2(scale, recip);
+}
+
 __device__ __forceinline__ void q8_scale_fast(float wmax, float &scale, float &recip)
 {
 	wmax = x86_max(wmax, kQ8WmaxFloor);
@@ -65,7 +73,9 @@ __device__ __forceinline__ void q8_scale_fast(float wmax, float &scale, float &r
 		scale = __double2float_rn(__dmul_rn((double)wmax, 1.0 / 127.0));
 		recip = rcp_nr(scale); // scale in [FLT_MIN, FLT_MAX/127]: reciprocal normal
 	} else {
-		q8_scale(wmax, scale, recip);
+		const float2 sr = q8_scale_ieee(wmax);
+		scale = sr.x;
+		recip = sr.y;
 	}
 }
 
