@@ -20,11 +20,11 @@ constexpr int kWarpsPerBlock = kBlock / 32;
 
 // --- A1  RMSNorm rows (rmsnorm_kernel.inc:12-75), caller's MXCSR: no FTZ ---
 // Two passes over the row in chunks of C slots per lane: pass 1 accumulates
-// the chains, pass 2 re-reads the row (from L2) to write the output.  Both
-// passes are software-pipelined: the loads of chunk k0 + C are issued before
-// chunk k0's arithmetic, so a warp keeps C loads in flight through its FMA
-// chain (measured on B200: +17 % over the unpipelined form, and well ahead of
-// holding the whole row in registers, which limits residency).
+// the chains, pass 2 re-reads the row (from L2) to write the output.  A chunk
+// issues its C loads before any arithmetic; full chunks carry no per-slot
+// guards, and the latency between chunks is covered by the four resident CTAs
+// per SM (a register prefetch buffer costs a move per element and registers
+// that would lower residency).
 template <int C, int MINB = kMinBlocks>
 __global__ void __launch_bounds__(kBlock, MINB) k_rmsnorm_rows(float *o, const float *x, const float *__restrict__ w, int64_t rows, int n, float eps)
 {
@@ -37,44 +37,32 @@ __global__ void __launch_bounds__(kBlock, MINB) k_rmsnorm_rows(float *o, const f
 		const float *xr = x + row * n + lane;
 		float *orow = o + row * n + lane;
 		float acc = 0.0f;
-		float v[C];
-#pragma unroll
-		for (int k = 0; k < C; ++k)
-			if (k < vpl)
-				v[k] = xr[32 * k];
-		for (int k0 = 0; k0 < vpl; k0 += C) {
-			float vn[C];
+		int k0 = 0;
+		for (; k0 + C <= vpl; k0 += C) {
+			float v[C];
 #pragma unroll
 			for (int k = 0; k < C; ++k)
-				if (k0 + C + k < vpl)
-					vn[k] = xr[32 * (k0 + C + k)];
+				v[k] = xr[32 * (k0 + k)];
 #pragma unroll
 			for (int k = 0; k < C; ++k)
-				if (k0 + k < vpl)
-					acc = M::fma(v[k], v[k], acc);
-#pragma unroll
-			for (int k = 0; k < C; ++k)
-				v[k] = vn[k];
+				acc = M::fma(v[k], v[k], acc);
+		}
+		for (; k0 < vpl; ++k0) {
+			const float v = xr[32 * k0];
+			acc = M::fma(v, v, acc);
 		}
 		const float scale = rms_scale<false>(reduce_chains_4x8<false>(acc), nf, eps);
-#pragma unroll
-		for (int k = 0; k < C; ++k)
-			if (k < vpl)
-				v[k] = ld_stream(xr + 32 * k);
-		for (int k0 = 0; k0 < vpl; k0 += C) {
-			float vn[C];
+		for (k0 = 0; k0 + C <= vpl; k0 += C) {
+			float v[C];
 #pragma unroll
 			for (int k = 0; k < C; ++k)
-				if (k0 + C + k < vpl)
-					vn[k] = ld_stream(xr + 32 * (k0 + C + k));
+				v[k] = ld_stream(xr + 32 * (k0 + k));
 #pragma unroll
 			for (int k = 0; k < C; ++k)
-				if (k0 + k < vpl)
-					st_stream(orow + 32 * (k0 + k), M::mul(M::mul(v[k], scale), __ldg(w + lane + 32 * (k0 + k))));
-#pragma unroll
-			for (int k = 0; k < C; ++k)
-				v[k] = vn[k];
+				st_stream(orow + 32 * (k0 + k), M::mul(M::mul(v[k], scale), __ldg(w + lane + 32 * (k0 + k))));
 		}
+		for (; k0 < vpl; ++k0)
+			st_stream(orow + 32 * k0, M::mul(M::mul(ld_stream(xr + 32 * k0), scale), __ldg(w + lane + 32 * k0)));
 	}
 }
 
@@ -83,7 +71,7 @@ __global__ void __launch_bounds__(kBlock, MINB) k_rmsnorm_rows(float *o, const f
 // leading blocks into accumulator A (lanes 0..7 here), then runs the 4-way
 // groups from block L on; chain lane l then covers e = 8L + l + 32k.  Pass 1
 // writes the new residual as it goes; pass 2 re-reads it (L2) for the output;
-// both pipelined as in k_rmsnorm_rows.
+// both in unguarded chunks as in k_rmsnorm_rows.
 template <int C, int MINB = kMinBlocks>
 __global__ void __launch_bounds__(kBlock, MINB) k_fused_add_rmsnorm_rows(float *o, float *res, const float *add, const float *__restrict__ w, int64_t rows, int n, float eps)
 {
@@ -108,33 +96,25 @@ __global__ void __launch_bounds__(kBlock, MINB) k_fused_add_rmsnorm_rows(float *
 		}
 		float *rm = rr + off + lane;
 		const float *am = ar + off + lane;
-		float r[C], a[C];
-#pragma unroll
-		for (int k = 0; k < C; ++k)
-			if (k < vpl) {
-				r[k] = ld_stream(rm + 32 * k);
-				a[k] = ld_stream(am + 32 * k);
-			}
-		for (int k0 = 0; k0 < vpl; k0 += C) {
-			float rn[C], an[C];
-#pragma unroll
-			for (int k = 0; k < C; ++k)
-				if (k0 + C + k < vpl) {
-					rn[k] = ld_stream(rm + 32 * (k0 + C + k));
-					an[k] = ld_stream(am + 32 * (k0 + C + k));
-				}
-#pragma unroll
-			for (int k = 0; k < C; ++k)
-				if (k0 + k < vpl) {
-					const float sv = M::add(r[k], a[k]);
-					acc = M::fma(sv, sv, acc);
-					rm[32 * (k0 + k)] = sv;
-				}
+		int k0 = 0;
+		for (; k0 + C <= vpl; k0 += C) {
+			float r[C], a[C];
 #pragma unroll
 			for (int k = 0; k < C; ++k) {
-				r[k] = rn[k];
-				a[k] = an[k];
+				r[k] = ld_stream(rm + 32 * (k0 + k));
+				a[k] = ld_stream(am + 32 * (k0 + k));
 			}
+#pragma unroll
+			for (int k = 0; k < C; ++k) {
+				const float sv = M::add(r[k], a[k]);
+				acc = M::fma(sv, sv, acc);
+				rm[32 * (k0 + k)] = sv;
+			}
+		}
+		for (; k0 < vpl; ++k0) {
+			const float sv = M::add(ld_stream(rm + 32 * k0), ld_stream(am + 32 * k0));
+			acc = M::fma(sv, sv, acc);
+			rm[32 * k0] = sv;
 		}
 		const float scale = rms_scale<false>(reduce_chains_4x8<false>(acc), nf, eps);
 		if (left != 0 && lane < 8) {
@@ -143,38 +123,30 @@ __global__ void __launch_bounds__(kBlock, MINB) k_fused_add_rmsnorm_rows(float *
 		}
 		float *om = orow + off + lane;
 		const float *wm = w + off + lane;
-		float v[C];
-#pragma unroll
-		for (int k = 0; k < C; ++k)
-			if (k < vpl)
-				v[k] = rm[32 * k];
-		for (int k0 = 0; k0 < vpl; k0 += C) {
-			float vn[C];
+		for (k0 = 0; k0 + C <= vpl; k0 += C) {
+			float v[C];
 #pragma unroll
 			for (int k = 0; k < C; ++k)
-				if (k0 + C + k < vpl)
-					vn[k] = rm[32 * (k0 + C + k)];
+				v[k] = rm[32 * (k0 + k)];
 #pragma unroll
 			for (int k = 0; k < C; ++k)
-				if (k0 + k < vpl)
-					st_stream(om + 32 * (k0 + k), M::mul(M::mul(v[k], scale), __ldg(wm + 32 * (k0 + k))));
-#pragma unroll
-			for (int k = 0; k < C; ++k)
-				v[k] = vn[k];
+				st_stream(om + 32 * (k0 + k), M::mul(M::mul(v[k], scale), __ldg(wm + 32 * (k0 + k))));
 		}
+		for (; k0 < vpl; ++k0)
+			st_stream(om + 32 * k0, M::mul(M::mul(rm[32 * k0], scale), __ldg(wm + 32 * k0)));
 	}
 }
 
-// slots per lane per pipelined chunk: as deep as 64 registers allow without spills
-constexpr int kRmsChunk = 12;
-constexpr int kAddChunk = 6;
+// slots per lane per chunk: as deep as 64 registers allow without spills
+constexpr int kRmsChunk = 32;
+constexpr int kAddChunk = 16;
 // Few rows (a decode step, a single vector) leave the GPU mostly idle and
 // the time is the row's own latency: then a deeper chunk without the
 // occupancy cap puts a 2048-wide row's loads in flight at once.  Same
 // arithmetic in the same order, so results are identical.
 constexpr int64_t kFewRows = 1024;
-constexpr int kRmsChunkFew = 32;
-constexpr int kAddChunkFew = 16;
+constexpr int kRmsChunkFew = 64;
+constexpr int kAddChunkFew = 32;
 
 // `oversubscribe` x the resident CTAs, at most one warp per row.
 template <typename Kernel, typename... Args>
