@@ -89,7 +89,8 @@ int v7g_add_inplace(float *x, const float *y, int64_t count, void *stream)
 	if (!x || !y)
 		return set_error(V7G_ERR_ARG, "v7g_add_inplace: NULL pointer");
 	if (aligned16(x) && aligned16(y))
-		return launch_persistent(k_add_inplace<true>, "v7g_add_inplace", ((count >> 2) + kBlock - 1) / kBlock, 4, stream, x, y, count);
+		// a one-shot grid (up to 64 resident waves), as for the elementwise SwiGLU
+		return launch_persistent(k_add_inplace<true>, "v7g_add_inplace", ((count >> 2) + kBlock - 1) / kBlock, 64, stream, x, y, count);
 	return launch_persistent(k_add_inplace<false>, "v7g_add_inplace", (count + kBlock - 1) / kBlock, 1, stream, x, y, count);
 }
 

