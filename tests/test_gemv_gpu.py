@@ -114,33 +114,46 @@ def test_gemv_neg128_weights_and_extreme_scales(cuda, oracle):
         assert_same_f32(host(out2), oracle.swiglu_q8_gemv(xq, xs, wq, ws, wq[::-1], ws[::-1]))
 
 
-@pytest.mark.parametrize("n,d", [(64, 1), (576, 13), (2048, 5000), (8192, 2048)])
-def test_gemv_pipeline_and_direct_kernels_agree(cuda, oracle, n, d):
-    """16-byte aligned weights take the bulk-copy pipeline, 4-byte aligned ones
-    the direct-load kernel: both equal the oracle, and no wait gave up."""
+@pytest.mark.parametrize("n,d", [(64, 1), (576, 13), (1024, 3000), (2048, 5000), (8192, 2048)])
+def test_gemv_stream_pipeline_and_direct_kernels_agree(cuda, oracle, n, d):
+    """16-byte aligned weights and scales take the streaming kernel, aligned
+    weights with 4-byte aligned scales the pipelined kernel, 4-byte aligned
+    weights the direct-load kernel: all equal the oracle, and no wait gave up."""
     import v7multiplikator_b200 as v7g
     rng = np.random.default_rng(n ^ d)
     xq, xs, gq, gs = q8_case(rng, 2, n, d)
     _, _, uq, us = q8_case(rng, 1, n, d)
     want = oracle.swiglu_q8_gemv(xq, xs, gq, gs, uq, us)
+    want0 = oracle.q8_gemv(xq, xs, gq, gs)
+    xf = rng.normal(0, 1, (2, n)).astype(F)
+    want2 = oracle.swiglu_f32q8_gemv(xf, gq, gs, uq, us)
     before = v7g.pipeline_timeouts()
-    for shift in (0, 4):
-        gbuf = torch.zeros(d * n + 16, dtype=torch.int8, device=cuda)
-        ubuf = torch.zeros(d * n + 16, dtype=torch.int8, device=cuda)
-        gt = gbuf[shift:shift + d * n].view(d, n)
-        ut = ubuf[shift:shift + d * n].view(d, n)
-        gt.copy_(dev(gq))
-        ut.copy_(dev(uq))
+
+    def at(a, shift):
+        """a copy of a on the device starting `shift` bytes into a fresh buffer"""
+        t = dev(a)
+        flat = t.reshape(-1).view(torch.int8)
+        buf = torch.zeros(flat.numel() + 16, dtype=torch.int8, device=cuda)
+        buf[shift:shift + flat.numel()].copy_(flat)
+        return buf[shift:shift + flat.numel()].view(t.dtype).view(t.shape)
+
+    for wshift, sshift in ((0, 0), (0, 4), (4, 0)):
+        gt, ut = at(gq, wshift), at(uq, wshift)
+        gst, ust = at(gs, sshift), at(us, sshift)
+        tag = f"weights +{wshift} B, scales +{sshift} B"
         out = torch.empty(2, d, device=cuda)
-        v7g.swiglu_q8_gemv(out, dev(xq), dev(xs), gt, dev(gs), ut, dev(us))
+        v7g.swiglu_q8_gemv(out, dev(xq), dev(xs), gt, gst, ut, ust)
         with np.errstate(all="ignore"):
-            assert_same_f32(host(out), want, f"weights offset {shift}")
-        # the fp32-activation kernel on the same weights
-        xf = rng.normal(0, 1, (2, n)).astype(F)
-        out2 = torch.empty(2, d, device=cuda)
-        v7g.swiglu_f32q8_gemv(out2, dev(xf), gt, dev(gs), ut, dev(us))
-        with np.errstate(all="ignore"):
-            assert_same_f32(host(out2), oracle.swiglu_f32q8_gemv(xf, gq, gs, uq, us), f"fp32 activation, offset {shift}")
+            assert_same_f32(host(out), want, tag)
+        out0 = torch.empty(2, d, device=cuda)
+        v7g.q8_gemv(out0, dev(xq), at(xs, sshift), gt, gst)
+        assert_same_f32(host(out0), want0, "q8, " + tag)
+        # the fp32-activation kernel on the same weights, activation aligned or not
+        for xshift in (0, 4):
+            out2 = torch.empty(2, d, device=cuda)
+            v7g.swiglu_f32q8_gemv(out2, at(xf, xshift), gt, gst, ut, ust)
+            with np.errstate(all="ignore"):
+                assert_same_f32(host(out2), want2, f"fp32 activation +{xshift} B, " + tag)
     assert v7g.pipeline_timeouts() == before == 0
 
 

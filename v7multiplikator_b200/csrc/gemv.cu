@@ -23,10 +23,13 @@
 // and scales are staged once per CTA in shared memory.  Loads for kUnroll
 // groups are issued before their arithmetic.  The weights are read exactly
 // once: HBM-bound at d x n x (1 + 4/64) bytes per matrix.
+#include <algorithm>
+
 #include "arith.cuh"
 #include "internal.h"
 #include "pipeline.cuh"
 #include "q8.cuh"
+#include "q8_fast.cuh"
 
 namespace v7g {
 namespace {
@@ -99,14 +102,16 @@ struct GemvArgs {
 
 // Quantise the CTA's activation row into shared memory with v7d_quantize's
 // rules (quantize_kernel.inc:43-106): half a warp per 64-element group, one
-// float4 per lane; `nthreads` (a multiple of 32) threads take part.
+// float4 per lane; `nthreads` (a multiple of 32) threads take part.  SHARED:
+// x is a 16-byte aligned copy in shared memory (plain loads), else global.
+template <bool SHARED = false>
 __device__ void stage_quantized(const float *x, int n, uint32_t *sq, float *ss, int nthreads = kBlock)
 {
 	constexpr int U = 8; // group pairs per warp loaded before any is processed: one L2 latency per U
 	const int lane = threadIdx.x & 31, half = lane >> 4, hl = lane & 15;
 	const int groups = n / kQ8Group;
 	const int step = (nthreads / 32) * 2;
-	const bool vec = (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
+	const bool vec = SHARED || (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
 	for (int g0 = (threadIdx.x >> 5) * 2; g0 < groups; g0 += U * step) {
 		float4 h[U];
 #pragma unroll
@@ -115,7 +120,10 @@ __device__ void stage_quantized(const float *x, int n, uint32_t *sq, float *ss, 
 			h[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 			if (g < groups) {
 				const float *p = x + (int64_t)g * kQ8Group + 4 * hl;
-				h[u] = vec ? __ldg(reinterpret_cast<const float4 *>(p)) : make_float4(__ldg(p), __ldg(p + 1), __ldg(p + 2), __ldg(p + 3));
+				if (SHARED)
+					h[u] = *reinterpret_cast<const float4 *>(p);
+				else
+					h[u] = vec ? __ldg(reinterpret_cast<const float4 *>(p)) : make_float4(__ldg(p), __ldg(p + 1), __ldg(p + 2), __ldg(p + 3));
 			}
 		}
 #pragma unroll
@@ -124,9 +132,9 @@ __device__ void stage_quantized(const float *x, int n, uint32_t *sq, float *ss, 
 				break;
 			const int g = g0 + u * step + half;
 			float scale, recip;
-			q8_scale(group_absmax_f4(h[u], lane), scale, recip);
+			q8_scale_fast(group_absmax_f4(h[u], lane), scale, recip);
 			if (g < groups) {
-				sq[g * 16 + hl] = q8_codes4(h[u], recip);
+				sq[g * 16 + hl] = q8_codes4_x2(h[u], recip);
 				if (hl == 0)
 					ss[g] = scale;
 			}
@@ -461,6 +469,328 @@ __global__ void __launch_bounds__(R * kLanes + 32, 2) k_q8_gemv_tma(GemvArgs p, 
 		p.out[b * p.d + row0 + r] = MODE == 0 ? res[0] : v7_swiglu(res[0], res[NM - 1]);
 }
 
+// ---- streaming Q8 GEMV -------------------------------------------------------
+// The arithmetic of k_q8_gemv once more, organised for HBM: a CTA (two per
+// SM) walks the row blocks rb = blockIdx.x, + gridDim.x, ... and its producer
+// warp streams, in order and without draining between row blocks:
+//   once      the activation (codes and scales, or the fp32 row) -- ahead of
+//             every weight byte, so the consumers' prologue is one latency;
+//   per block its weight scales, one bulk copy per matrix (the block's rows
+//             are contiguous) into a two-slot ring;
+//   per chunk the block's kChunkGroups groups of every row and matrix into a
+//             ring of up to kMaxStages stages.
+// The consumers form the combined scale (weight scale x activation scale,
+// rounded once as the reference's vmulps) as they go.  Requires every weight
+// and scale pointer 16-byte aligned and groups % 4 == 0 (16-byte scale rows).
+constexpr int kMaxStages = 8;
+
+template <int NM, int R>
+__device__ __forceinline__ void chunk_chains_ws(float (&acc)[NM], const uint32_t *st, const uint32_t *a, const float *wsr, int mstride, const float *xsc, int l, int gk)
+{
+	using M = F<true>;
+	constexpr int SB = 8; // groups per batch (their scale words load as two float4)
+#pragma unroll 1
+	for (int b0 = 0; b0 < kChunkGroups; b0 += SB) {
+		if (b0 >= gk)
+			break;
+		int dots[NM][SB];
+		uint32_t flag = 0;
+#pragma unroll
+		for (int j = 0; j < SB; ++j)
+			if (b0 + j < gk)
+#pragma unroll
+				for (int m = 0; m < NM; ++m) {
+					const uint32_t *wr = st + m * R * (kRowSlot / 4) + (b0 + j) * 16;
+					dots[m][j] = lane_dot(a[(b0 + j) * 16 + l], wr[l], a[(b0 + j) * 16 + 8 + l], wr[8 + l], flag);
+				}
+		if (flag) {
+#pragma unroll
+			for (int j = 0; j < SB; ++j)
+				if (b0 + j < gk)
+#pragma unroll
+					for (int m = 0; m < NM; ++m) {
+						const uint32_t *wr = st + m * R * (kRowSlot / 4) + (b0 + j) * 16;
+						dots[m][j] += lane_dot_correction(a[(b0 + j) * 16 + l], wr[l], a[(b0 + j) * 16 + 8 + l], wr[8 + l]);
+					}
+		}
+		const float4 x0 = *reinterpret_cast<const float4 *>(xsc + b0), x1 = *reinterpret_cast<const float4 *>(xsc + b0 + 4);
+		const float xv[SB] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+		for (int m = 0; m < NM; ++m) {
+			const float4 w0 = *reinterpret_cast<const float4 *>(wsr + m * mstride + b0);
+			const float4 w1 = *reinterpret_cast<const float4 *>(wsr + m * mstride + b0 + 4);
+			const float wv[SB] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+			for (int j = 0; j < SB; ++j)
+				if (b0 + j < gk)
+					acc[m] = M::fma((float)dots[m][j], M::mul(wv[j], xv[j]), acc[m]);
+		}
+	}
+}
+
+// chunk_chains_ws with two threads per row lane (J = 2): thread j computes
+// the dots of groups b0 + 2i + j, the pair exchanges them through shuffles
+// and both run the lane's chain over all groups in order (same operations,
+// same order as one thread would).  Called by every thread of the warp (the
+// shuffles need them all); rows past the matrix compute on stale slots and
+// are not stored.  base: first lane of the row's 16 in the warp.
+template <int NM, int R>
+__device__ __forceinline__ void chunk_chains_ws2(float (&acc)[NM], const uint32_t *st, const uint32_t *a, const float *wsr, int mstride, const float *xsc, int l, int j, int base, int gk)
+{
+	using M = F<true>;
+	constexpr int SB = 8; // groups per batch, SB / 2 per thread
+#pragma unroll 1
+	for (int b0 = 0; b0 < kChunkGroups; b0 += SB) {
+		if (b0 >= gk)
+			break;
+		int dots[NM][SB / 2];
+		uint32_t flag = 0;
+#pragma unroll
+		for (int i = 0; i < SB / 2; ++i) {
+			const int g = b0 + 2 * i + j;
+#pragma unroll
+			for (int m = 0; m < NM; ++m) {
+				const uint32_t *wr = st + m * R * (kRowSlot / 4) + g * 16;
+				dots[m][i] = g < gk ? lane_dot(a[g * 16 + l], wr[l], a[g * 16 + 8 + l], wr[8 + l], flag) : 0;
+			}
+		}
+		if (flag) {
+#pragma unroll
+			for (int i = 0; i < SB / 2; ++i) {
+				const int g = b0 + 2 * i + j;
+				if (g < gk)
+#pragma unroll
+					for (int m = 0; m < NM; ++m) {
+						const uint32_t *wr = st + m * R * (kRowSlot / 4) + g * 16;
+						dots[m][i] += lane_dot_correction(a[g * 16 + l], wr[l], a[g * 16 + 8 + l], wr[8 + l]);
+					}
+			}
+		}
+		const float4 x0 = *reinterpret_cast<const float4 *>(xsc + b0), x1 = *reinterpret_cast<const float4 *>(xsc + b0 + 4);
+		const float xv[SB] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+		for (int m = 0; m < NM; ++m) {
+			const float4 w0 = *reinterpret_cast<const float4 *>(wsr + m * mstride + b0);
+			const float4 w1 = *reinterpret_cast<const float4 *>(wsr + m * mstride + b0 + 4);
+			const float wv[SB] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+			for (int i = 0; i < SB / 2; ++i) {
+				const float mine = (float)dots[m][i];
+				const float de = __shfl_sync(0xffffffffu, mine, base + l);
+				const float dodd = __shfl_sync(0xffffffffu, mine, base + 8 + l);
+				if (b0 + 2 * i < gk)
+					acc[m] = M::fma(de, M::mul(wv[2 * i], xv[2 * i]), acc[m]);
+				if (b0 + 2 * i + 1 < gk)
+					acc[m] = M::fma(dodd, M::mul(wv[2 * i + 1], xv[2 * i + 1]), acc[m]);
+			}
+		}
+	}
+}
+
+struct StreamLayout {
+	int stages;
+	bool xstaged;  // the fp32 activation arrives by bulk copy (FUSED, MODE 2)
+	size_t smem;
+};
+
+// Shared memory: ring [stages][NM][R] row slots | weight-scale slots
+// [2][NM][R * groups] + 16 | activation: codes [n] + scales [groups + 16]
+// (MODE 2: fp32 lane-major [8][xstride]) | fp32 staging [n] when xstaged |
+// barriers full[stages], empty[stages], sfull[2], sempty[2], pro.
+__host__ __device__ inline size_t stream_fixed(int mode, int rows_per_block, int n)
+{
+	const int nm = mode == 0 ? 1 : 2;
+	const size_t groups = (size_t)n / kQ8Group;
+	const size_t slots = 4 * (2 * (size_t)nm * rows_per_block * groups + 16);
+	const size_t act = mode == 2 ? 32 * (groups * 8 + 4) : (size_t)n + 4 * (groups + 16);
+	return slots + act;
+}
+
+template <int MODE, bool FUSED, int R, int J, int P>
+__global__ void __launch_bounds__(R * kLanes * J + 32 * P, 2) k_q8_gemv_stream(GemvArgs p, int stages, int xstaged_arg)
+{
+	static_assert(J == 1 || (J == 2 && MODE != 2), "two threads per row lane only for Q8 x Q8");
+	static_assert(P >= 1 && P <= 4, "one to four producer warps");
+	constexpr int NM = MODE == 0 ? 1 : 2;
+	constexpr int kConsumers = R * kLanes * J;
+	constexpr int kStageBytes = NM * R * kRowSlot;
+	extern __shared__ __align__(128) unsigned char smem[];
+	const int n = p.n, groups = n / kQ8Group;
+	const int nchunks = (groups + kChunkGroups - 1) / kChunkGroups;
+	const int64_t nrb = (p.d + R - 1) / R;
+	const int64_t b = blockIdx.y;
+	// only the fp32-activation forms have a staging area in their layout
+	const bool xstaged = (MODE == 2 || FUSED) && xstaged_arg != 0;
+	const int mstride = R * groups; // floats between a slot's matrices
+	float *sws = reinterpret_cast<float *>(smem + (size_t)stages * kStageBytes);
+	unsigned char *act = reinterpret_cast<unsigned char *>(sws + 2 * NM * mstride + 16);
+	uint32_t *sq = reinterpret_cast<uint32_t *>(act);
+	float *ss = reinterpret_cast<float *>(act + n);
+	float *xt = reinterpret_cast<float *>(act);
+	const int xstride = groups * 8 + 4; // MODE 2: the 8 lanes' rows start 4 banks apart
+	float *xstage = reinterpret_cast<float *>(reinterpret_cast<unsigned char *>(sws) + stream_fixed(MODE, R, n));
+	uint64_t *full = reinterpret_cast<uint64_t *>(reinterpret_cast<unsigned char *>(xstage) + (xstaged ? 4 * (size_t)n : 0));
+	uint64_t *empty = full + stages;
+	uint64_t *sfull = empty + stages;
+	uint64_t *sempty = sfull + 2;
+	uint64_t *pro = sempty + 2;
+	if (threadIdx.x == 0) {
+		for (int s = 0; s < stages; ++s) {
+			mbar_init(full + s, P); // one arrival (with its byte count) per producer warp
+			mbar_init(empty + s, kConsumers / 32);
+		}
+		for (int s = 0; s < 2; ++s) {
+			mbar_init(sfull + s, 1);
+			mbar_init(sempty + s, kConsumers / 32);
+		}
+		mbar_init(pro, 1);
+		mbar_init_fence();
+	}
+	__syncthreads();
+	const bool pro_copy = (MODE != 2 && !FUSED) || xstaged;
+	if (threadIdx.x >= kConsumers) {
+		// P producer warps: warp 0 also copies the activation and the scales;
+		// the copies of a stage are dealt round-robin (a warp issues one copy
+		// per active lane, and issuing costs the warp tens of cycles per copy,
+		// so one warp alone cannot keep HBM busy with 1 KB copies)
+		const int lane = threadIdx.x & 31;
+		const int pw = (threadIdx.x - kConsumers) >> 5;
+		if (pro_copy && pw == 0 && lane == 0) {
+			if (MODE != 2 && !FUSED) {
+				mbar_arrive_expect_tx(pro, (uint32_t)(n + 4 * groups));
+				bulk_copy_g2s(sq, p.xq + b * n, (uint32_t)n, pro);
+				bulk_copy_g2s(ss, p.xs + b * groups, (uint32_t)(4 * groups), pro);
+			} else {
+				mbar_arrive_expect_tx(pro, (uint32_t)(4 * n));
+				bulk_copy_g2s(xstage, p.xf + b * n, (uint32_t)(4 * n), pro);
+			}
+		}
+		uint32_t q = 0;
+		int i = 0;
+		bool ok = true;
+		for (int64_t rb = blockIdx.x; rb < nrb && ok; rb += gridDim.x, ++i) {
+			const int64_t row0 = rb * R;
+			const int rows = (int)min((int64_t)R, p.d - row0);
+			const int slot = i & 1;
+			if (pw == 0) {
+				if (i >= 2 && lane == 0)
+					ok = mbar_wait(sempty + slot, ((i >> 1) - 1) & 1, &g_pipeline_timeouts);
+				if (!__shfl_sync(0xffffffffu, ok, 0))
+					break;
+				if (lane == 0)
+					mbar_arrive_expect_tx(sfull + slot, (uint32_t)(NM * rows * groups * 4));
+				__syncwarp();
+				if (lane < NM)
+					bulk_copy_g2s(sws + (slot * NM + lane) * mstride, (lane == 0 ? p.ws[0] : p.ws[NM - 1]) + row0 * groups,
+					              (uint32_t)(rows * groups * 4), sfull + slot);
+			}
+			const int ncopy = NM * rows;
+			const int mine = ncopy > pw ? (ncopy - pw + P - 1) / P : 0; // copies pw, pw + P, ...
+			for (int k = 0; k < nchunks; ++k, ++q) {
+				const int s = (int)(q % (uint32_t)stages);
+				if (q >= (uint32_t)stages && lane == 0)
+					ok = mbar_wait(empty + s, ((q / stages) - 1) & 1, &g_pipeline_timeouts);
+				if (!__shfl_sync(0xffffffffu, ok, 0))
+					break;
+				const int g0 = k * kChunkGroups;
+				const int gk = min(kChunkGroups, groups - g0);
+				const uint32_t bytes = (uint32_t)(gk * kQ8Group);
+				if (lane == 0)
+					mbar_arrive_expect_tx(full + s, bytes * (uint32_t)mine);
+				__syncwarp();
+				if (lane < mine) {
+					const int c = pw + P * lane;
+					const int m = c / rows, r = c - m * rows;
+					// a select, not p.wq[m]: a runtime index into the parameter
+					// array would copy it to local memory
+					const int8_t *wm = m == 0 ? p.wq[0] : p.wq[NM - 1];
+					bulk_copy_g2s(smem + (size_t)s * kStageBytes + (m * R + r) * kRowSlot, wm + (row0 + r) * n + (int64_t)g0 * kQ8Group, bytes,
+					              full + s);
+				}
+			}
+		}
+		// leave only once every copy issued has landed
+		if (lane == 0) {
+			for (uint32_t k = q > (uint32_t)stages ? q - stages : 0; k < q; ++k)
+				if (!mbar_wait(full + k % stages, (k / stages) & 1, &g_pipeline_timeouts))
+					break;
+			if (pw == 0) {
+				for (int j = i > 2 ? i - 2 : 0; j < i; ++j)
+					if (!mbar_wait(sfull + (j & 1), (j >> 1) & 1, &g_pipeline_timeouts))
+						break;
+				if (pro_copy)
+					mbar_wait(pro, 0, &g_pipeline_timeouts);
+			}
+		}
+		return;
+	}
+	// consumers: the activation first
+	if (pro_copy && !__all_sync(0xffffffffu, mbar_wait(pro, 0, &g_pipeline_timeouts)))
+		return;
+	if (MODE == 2) {
+		const float *xb = p.xf + b * n;
+		for (int e = threadIdx.x; e < n; e += kConsumers)
+			xt[(e & 7) * xstride + (e >> 6) * 8 + ((e >> 3) & 7)] = xstaged ? xstage[e] : __ldg(xb + e);
+		named_sync(1, kConsumers);
+	} else if (FUSED) {
+		if (xstaged)
+			stage_quantized<true>(xstage, n, sq, ss, kConsumers);
+		else
+			stage_quantized<false>(p.xf + b * n, n, sq, ss, kConsumers);
+		named_sync(1, kConsumers);
+	}
+	const int r = threadIdx.x / (kLanes * J), l = threadIdx.x & (kLanes - 1);
+	const int j = J == 1 ? 0 : (threadIdx.x >> 3) & 1;
+	const int base = (threadIdx.x & 31) & ~15;
+	uint32_t q = 0;
+	int i = 0;
+	for (int64_t rb = blockIdx.x; rb < nrb; rb += gridDim.x, ++i) {
+		const int64_t row0 = rb * R;
+		const int rows = (int)min((int64_t)R, p.d - row0);
+		const bool valid = r < rows;
+		const int slot = i & 1;
+		if (!__all_sync(0xffffffffu, mbar_wait(sfull + slot, (i >> 1) & 1, &g_pipeline_timeouts)))
+			return;
+		const float *wsr = sws + slot * NM * mstride + r * groups;
+		float acc[NM];
+#pragma unroll
+		for (int m = 0; m < NM; ++m)
+			acc[m] = 0.0f;
+		for (int k = 0; k < nchunks; ++k, ++q) {
+			const int s = (int)(q % (uint32_t)stages);
+			// the warp leaves together if any lane's wait ran out
+			if (!__all_sync(0xffffffffu, mbar_wait(full + s, (q / stages) & 1, &g_pipeline_timeouts)))
+				return;
+			const int g0 = k * kChunkGroups;
+			const int gk = min(kChunkGroups, groups - g0);
+			if constexpr (J == 2) {
+				const uint32_t *st = reinterpret_cast<const uint32_t *>(smem + (size_t)s * kStageBytes) + r * (kRowSlot / 4);
+				chunk_chains_ws2<NM, R>(acc, st, sq + g0 * 16, wsr + g0, mstride, ss + g0, l, j, base, gk);
+			} else if (valid) {
+				const uint32_t *st = reinterpret_cast<const uint32_t *>(smem + (size_t)s * kStageBytes) + r * (kRowSlot / 4);
+				if constexpr (MODE == 2)
+					chunk_f32<R>(acc, st, xt + l * xstride + g0 * 8, wsr + g0, groups, l, gk);
+				else if (gk == kChunkGroups)
+					chunk_chains_ws<NM, R>(acc, st, sq + g0 * 16, wsr + g0, mstride, ss + g0, l, kChunkGroups);
+				else
+					chunk_chains_ws<NM, R>(acc, st, sq + g0 * 16, wsr + g0, mstride, ss + g0, l, gk);
+			}
+			__syncwarp();
+			if ((threadIdx.x & 31) == 0)
+				mbar_arrive(empty + s);
+		}
+		float res[NM];
+#pragma unroll
+		for (int m = 0; m < NM; ++m)
+			res[m] = hadd_lanes(acc[m]);
+		if (valid && l == 0 && j == 0)
+			p.out[b * p.d + row0 + r] = MODE == 0 ? res[0] : v7_swiglu(res[0], res[NM - 1]);
+		__syncwarp();
+		if ((threadIdx.x & 31) == 0)
+			mbar_arrive(sempty + slot);
+	}
+}
+
 // Shared memory of k_q8_gemv_tma for `stages` stages.
 size_t tma_smem(int mode, int rows, int n, int stages)
 {
@@ -581,11 +911,90 @@ int launch_gemv_tma(const char *what, const GemvArgs &a, int64_t batch, void *st
 	return check_launch(what);
 }
 
-// The pipelined kernel when the weights allow bulk copies (16-byte aligned),
-// else (or when it does not fit) the direct-load kernel.
-template <int MODE, bool FUSED>
-int run_q8_gemv(const char *what, const GemvArgs &a, int64_t batch, void *stream, bool tma)
+// Per-CTA shared memory aimed at two CTAs per SM, or one when two stages do
+// not fit that way.
+constexpr size_t kStreamSmemTwo = 110 * 1024;
+constexpr size_t kStreamSmemOne = 220 * 1024;
+
+StreamLayout stream_layout(int mode, bool fused, int rows_per_block, int n, bool x_aligned)
 {
+	const int nm = mode == 0 ? 1 : 2;
+	const size_t stage = (size_t)nm * rows_per_block * kRowSlot;
+	const size_t bars = 8 * (2 * (size_t)kMaxStages + 5);
+	const size_t fixed = stream_fixed(mode, rows_per_block, n) + bars;
+	const bool want_x = (mode == 2 || fused) && x_aligned;
+	for (size_t budget : {kStreamSmemTwo, kStreamSmemOne})
+		for (int xs = want_x ? 1 : 0; xs >= 0; --xs) {
+			const size_t base = fixed + (xs ? 4 * (size_t)n : 0);
+			if (base + 2 * stage > budget)
+				continue;
+			const int stages = (int)std::min<size_t>(kMaxStages, (budget - base) / stage);
+			return StreamLayout{stages, xs != 0, base + (size_t)stages * stage};
+		}
+	return StreamLayout{0, false, 0};
+}
+
+// Streaming-kernel shapes, measured on B200 at the decode shapes (d = 2048
+// .. 12288): 16 rows per block everywhere (also where that leaves SMs idle:
+// a block's 16 copies per stage keep more bytes in flight per CTA than two
+// blocks of 8); four producer warps for the one-matrix product, two for the
+// two-matrix ones; two threads per row lane for the fused quantise (its
+// in-kernel activation quantisation gets twice the threads).
+template <int MODE, bool FUSED>
+struct StreamShape {
+	static constexpr int R = 16;
+	static constexpr int J = FUSED ? 2 : 1;
+	static constexpr int P = (MODE == 0 && !FUSED) ? 4 : 2;
+};
+
+// grid = the resident CTAs (split over the batch), at most one per row
+// block.  V7G_ERR_UNSUPPORTED when the layout does not fit or groups % 4 != 0,
+// for the caller to fall back.
+template <int MODE, bool FUSED>
+int launch_gemv_stream(const char *what, const GemvArgs &a, int64_t batch, void *stream)
+{
+	using S = StreamShape<MODE, FUSED>;
+	const int groups = a.n / kQ8Group;
+	if (groups % 4 != 0)
+		return V7G_ERR_UNSUPPORTED;
+	DeviceInfo dev;
+	int rc = current_device(&dev);
+	if (rc != V7G_OK)
+		return rc;
+	const StreamLayout lay = stream_layout(MODE, FUSED, S::R, a.n, aligned16(a.xf));
+	if (lay.stages < 2)
+		return V7G_ERR_UNSUPPORTED;
+	const void *kernel = (const void *)k_q8_gemv_stream<MODE, FUSED, S::R, S::J, S::P>;
+	const int threads = S::R * kLanes * S::J + 32 * S::P;
+	// the shared-memory ceiling of the kernel is raised once per device
+	static bool raised[kMaxDevicesTracked];
+	if (dev.device >= kMaxDevicesTracked || !raised[dev.device]) {
+		if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kStreamSmemOne) != cudaSuccess)
+			return check_launch(what);
+		if (dev.device < kMaxDevicesTracked)
+			raised[dev.device] = true;
+	}
+	int per_sm = 0;
+	if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, lay.smem) != cudaSuccess || per_sm < 1)
+		return check_launch(what);
+	const int64_t nrb = (a.d + S::R - 1) / S::R;
+	const int64_t slots = std::max<int64_t>(1, (int64_t)per_sm * dev.sm_count / batch);
+	const dim3 grid((unsigned)std::min(nrb, slots), (unsigned)batch);
+	k_q8_gemv_stream<MODE, FUSED, S::R, S::J, S::P><<<grid, threads, lay.smem, (cudaStream_t)stream>>>(a, lay.stages, lay.xstaged ? 1 : 0);
+	return check_launch(what);
+}
+
+// The streaming kernel when weights and scales allow bulk copies (16-byte
+// aligned), else the pipelined kernel when the weights do, else (or when
+// neither fits) the direct-load kernel.
+template <int MODE, bool FUSED>
+int run_q8_gemv(const char *what, const GemvArgs &a, int64_t batch, void *stream, bool tma, bool scales16)
+{
+	if (tma && scales16) {
+		const int rc = launch_gemv_stream<MODE, FUSED>(what, a, batch, stream);
+		if (rc != V7G_ERR_UNSUPPORTED)
+			return rc;
+	}
 	if (tma) {
 		const int rc = launch_gemv_tma<MODE, FUSED>(what, a, batch, stream);
 		if (rc != V7G_ERR_UNSUPPORTED)
@@ -612,7 +1021,7 @@ int v7g_q8_gemv(float *out, const int8_t *xq, const float *xs, const int8_t *wq,
 	if (!xq || !xs || !aligned16(xq) || !weights_ok(wq, ws))
 		return set_error(V7G_ERR_ARG, "%s: NULL pointer, activation codes not 16-byte or weight codes not 4-byte aligned", what);
 	GemvArgs a{out, xq, xs, nullptr, {wq, wq}, {ws, ws}, n, d};
-	return run_q8_gemv<0, false>(what, a, batch, stream, aligned16(wq));
+	return run_q8_gemv<0, false>(what, a, batch, stream, aligned16(wq), aligned16(ws) && aligned16(xs));
 }
 
 int v7g_q8_fused_gemv(float *out, const float *x, const int8_t *wq, const float *ws, int64_t batch, int n, int d, void *stream)
@@ -626,7 +1035,7 @@ int v7g_q8_fused_gemv(float *out, const float *x, const int8_t *wq, const float 
 	if (!x || !weights_ok(wq, ws))
 		return set_error(V7G_ERR_ARG, "%s: NULL pointer or weight codes not 4-byte aligned", what);
 	GemvArgs a{out, nullptr, nullptr, x, {wq, wq}, {ws, ws}, n, d};
-	return run_q8_gemv<0, true>(what, a, batch, stream, aligned16(wq));
+	return run_q8_gemv<0, true>(what, a, batch, stream, aligned16(wq), aligned16(ws));
 }
 
 int v7g_swiglu_q8_gemv(float *out, const int8_t *xq, const float *xs, const int8_t *gate_q, const float *gate_s, const int8_t *up_q, const float *up_s, int64_t batch, int n, int d, void *stream)
@@ -640,7 +1049,8 @@ int v7g_swiglu_q8_gemv(float *out, const int8_t *xq, const float *xs, const int8
 	if (!xq || !xs || !aligned16(xq) || !weights_ok(gate_q, gate_s) || !weights_ok(up_q, up_s))
 		return set_error(V7G_ERR_ARG, "%s: NULL pointer, activation codes not 16-byte or weight codes not 4-byte aligned", what);
 	GemvArgs a{out, xq, xs, nullptr, {gate_q, up_q}, {gate_s, up_s}, n, d};
-	return run_q8_gemv<1, false>(what, a, batch, stream, aligned16(gate_q) && aligned16(up_q));
+	return run_q8_gemv<1, false>(what, a, batch, stream, aligned16(gate_q) && aligned16(up_q),
+	                             aligned16(gate_s) && aligned16(up_s) && aligned16(xs));
 }
 
 int v7g_swiglu_f32q8_gemv(float *out, const float *x, const int8_t *gate_q, const float *gate_s, const int8_t *up_q, const float *up_s, int64_t batch, int n, int d, void *stream)
@@ -654,6 +1064,11 @@ int v7g_swiglu_f32q8_gemv(float *out, const float *x, const int8_t *gate_q, cons
 	if (!x || !gate_q || !gate_s || !up_q || !up_s)
 		return set_error(V7G_ERR_ARG, "%s: NULL pointer", what);
 	GemvArgs a{out, nullptr, nullptr, x, {gate_q, up_q}, {gate_s, up_s}, n, d};
+	if (aligned16(gate_q) && aligned16(up_q) && aligned16(gate_s) && aligned16(up_s)) {
+		const int rc2 = launch_gemv_stream<2, false>(what, a, batch, stream);
+		if (rc2 != V7G_ERR_UNSUPPORTED)
+			return rc2;
+	}
 	if (aligned16(gate_q) && aligned16(up_q)) {
 		const int rc2 = launch_gemv_tma<2, false>(what, a, batch, stream);
 		if (rc2 != V7G_ERR_UNSUPPORTED)
