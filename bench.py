@@ -598,12 +598,15 @@ def _profile_case(name: str, rows: int, dev):
         if name == "rope_only":
             return lambda: v7g.rope_only_rows(q, k, cos, sin, 0), rows * (24 * 128 * 8 + 64 * 8)
         return lambda: v7g.rmsnorm_rope_rows(q, k, wq, wk, cos, sin, 0, 1e-6), rows * (24 * 128 * 8 + 64 * 8)
-    if name in ("swiglu_q8_gemv", "swiglu_f32q8_gemv", "q8_gemv"):
-        n = 4096 if name != "swiglu_f32q8_gemv" else 2048
+    if name in ("swiglu_q8_gemv", "swiglu_f32q8_gemv", "q8_gemv", "q8_fused_gemv"):
+        n = {"q8_gemv": 8192, "q8_fused_gemv": 8192, "swiglu_q8_gemv": 4096, "swiglu_f32q8_gemv": 2048}[name]  # the kernel-table shapes
         xq, xs, gq, gs, uq, us = gemv_inputs(dev, n, rows)
         y = torch.empty(1, rows, device=dev)
         if name == "q8_gemv":
             return lambda: v7g.q8_gemv(y, xq, xs, gq, gs), rows * (n + n // 16)
+        if name == "q8_fused_gemv":
+            xf = fill((1, n), 15, 0.0, 1.0)
+            return lambda: v7g.q8_fused_gemv(y, xf, gq, gs), rows * (n + n // 16)
         if name == "swiglu_q8_gemv":
             return lambda: v7g.swiglu_q8_gemv(y, xq, xs, gq, gs, uq, us), 2 * rows * (n + n // 16)
         xf = fill((1, n), 14, 0.0, 1.0)
@@ -618,7 +621,7 @@ def _profile_case(name: str, rows: int, dev):
 
 
 PROFILE_CASES = ("swiglu_q8", "swiglu", "rmsnorm", "fused_add_rmsnorm", "add_inplace", "rmsnorm_quantize", "rmsnorm_rope",
-                 "rope_only", "rope_tables", "swiglu_q8_gemv", "swiglu_f32q8_gemv", "q8_gemv")
+                 "rope_only", "rope_tables", "swiglu_q8_gemv", "swiglu_f32q8_gemv", "q8_gemv", "q8_fused_gemv")
 
 
 def run_profile(args) -> None:

@@ -80,6 +80,13 @@ __device__ __forceinline__ int lane_dot_correction(uint32_t a_lo, uint32_t w_lo,
 	return neg128_correction(a_lo, w_lo) + neg128_correction(a_hi, w_hi);
 }
 
+// The same, out of line: for loops where it is cold code that would otherwise
+// crowd the instruction cache.
+static __device__ __noinline__ int lane_dot_correction_call(uint32_t a_lo, uint32_t w_lo, uint32_t a_hi, uint32_t w_hi)
+{
+	return lane_dot_correction(a_lo, w_lo, a_hi, w_hi);
+}
+
 // HADD_YMM over the row's eight lane threads (consecutive lanes of a warp):
 // (l_j + l_{j+4}), then (t0 + t1) + (t2 + t3); the sum lands in lane j = 0.
 __device__ __forceinline__ float hadd_lanes(float v)
@@ -104,15 +111,16 @@ struct GemvArgs {
 // rules (quantize_kernel.inc:43-106): half a warp per 64-element group, one
 // float4 per lane; `nthreads` (a multiple of 32) threads take part.  SHARED:
 // x is a 16-byte aligned copy in shared memory (plain loads), else global.
+// Groups [gbeg, gend) only when gend >= 0 (x, sq, ss still indexed from group 0).
 template <bool SHARED = false>
-__device__ void stage_quantized(const float *x, int n, uint32_t *sq, float *ss, int nthreads = kBlock)
+__device__ __noinline__ void stage_quantized(const float *x, int n, uint32_t *sq, float *ss, int nthreads = kBlock, int gbeg = 0, int gend = -1)
 {
-	constexpr int U = 8; // group pairs per warp loaded before any is processed: one L2 latency per U
+	constexpr int U = 4; // group pairs per warp loaded before any is processed: one latency per U (and compact code)
 	const int lane = threadIdx.x & 31, half = lane >> 4, hl = lane & 15;
-	const int groups = n / kQ8Group;
+	const int groups = gend >= 0 ? gend : n / kQ8Group;
 	const int step = (nthreads / 32) * 2;
 	const bool vec = SHARED || (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
-	for (int g0 = (threadIdx.x >> 5) * 2; g0 < groups; g0 += U * step) {
+	for (int g0 = gbeg + (threadIdx.x >> 5) * 2; g0 < groups; g0 += U * step) {
 		float4 h[U];
 #pragma unroll
 		for (int u = 0; u < U; ++u) {
@@ -126,13 +134,15 @@ __device__ void stage_quantized(const float *x, int n, uint32_t *sq, float *ss, 
 					h[u] = vec ? __ldg(reinterpret_cast<const float4 *>(p)) : make_float4(__ldg(p), __ldg(p + 1), __ldg(p + 2), __ldg(p + 3));
 			}
 		}
+		float amax[U];
+		group_absmax_f4_n<U>(h, lane, amax);
 #pragma unroll
 		for (int u = 0; u < U; ++u) {
 			if (g0 + u * step >= groups) // warp-uniform: both halves stop together
 				break;
 			const int g = g0 + u * step + half;
 			float scale, recip;
-			q8_scale_fast(group_absmax_f4(h[u], lane), scale, recip);
+			q8_scale_fast(amax[u], scale, recip);
 			if (g < groups) {
 				sq[g * 16 + hl] = q8_codes4_x2(h[u], recip);
 				if (hl == 0)
@@ -248,6 +258,8 @@ constexpr int kChunkGroups = 16;
 // A row's slot in a stage: the 1024 bytes of its chunk and 32 bytes of
 // padding, so the four rows a warp reads start 8 banks apart.
 constexpr int kRowSlot = kChunkGroups * kQ8Group + 32;
+// The same padding for a chunk of cg groups (cg even: rows stay 8 banks apart).
+__host__ __device__ constexpr int row_slot(int cg) { return cg * kQ8Group + 32; }
 
 // The chains of one row lane over the gk (<= G) groups of a stage: all dots
 // first (no branch between groups), the rare -128 correction once, then the
@@ -301,7 +313,7 @@ __device__ __forceinline__ void chunk_chains(float (&acc)[NM], const uint32_t *s
 // byte of step k is byte l % 4 of word 2k + l / 4 of the group.  st: the row's
 // gate slot (up at + R slots); xl: the lane's activations from the first
 // group, 8 per group; sw: the row's gate scales (up at + R * sstride).
-template <int R>
+template <int R, int CG = kChunkGroups>
 __device__ __forceinline__ void chunk_f32(float (&acc)[2], const uint32_t *st, const float *xl, const float *sw, int sstride, int l, int gk)
 {
 	const bool odd = (l & 4) != 0;
@@ -311,7 +323,7 @@ __device__ __forceinline__ void chunk_f32(float (&acc)[2], const uint32_t *st, c
 #pragma unroll 2
 	for (int gi = 0; gi < gk; ++gi) {
 		const uint4 *wg = reinterpret_cast<const uint4 *>(st + gi * 16);
-		const uint4 *wu = reinterpret_cast<const uint4 *>(st + R * (kRowSlot / 4) + gi * 16);
+		const uint4 *wu = reinterpret_cast<const uint4 *>(st + R * (row_slot(CG) / 4) + gi * 16);
 		const float4 x0 = *reinterpret_cast<const float4 *>(xl + gi * 8);
 		const float4 x1 = *reinterpret_cast<const float4 *>(xl + gi * 8 + 4);
 		const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
@@ -477,20 +489,21 @@ __global__ void __launch_bounds__(R * kLanes + 32, 2) k_q8_gemv_tma(GemvArgs p, 
 //             every weight byte, so the consumers' prologue is one latency;
 //   per block its weight scales, one bulk copy per matrix (the block's rows
 //             are contiguous) into a two-slot ring;
-//   per chunk the block's kChunkGroups groups of every row and matrix into a
-//             ring of up to kMaxStages stages.
+//   per chunk the block's CG groups of every row and matrix into a ring of
+//             up to kMaxStages stages.
 // The consumers form the combined scale (weight scale x activation scale,
 // rounded once as the reference's vmulps) as they go.  Requires every weight
 // and scale pointer 16-byte aligned and groups % 4 == 0 (16-byte scale rows).
 constexpr int kMaxStages = 8;
 
-template <int NM, int R>
+template <int NM, int R, int SB = 8, int CG = kChunkGroups>
 __device__ __forceinline__ void chunk_chains_ws(float (&acc)[NM], const uint32_t *st, const uint32_t *a, const float *wsr, int mstride, const float *xsc, int l, int gk)
 {
 	using M = F<true>;
-	constexpr int SB = 8; // groups per batch (their scale words load as two float4)
+	static_assert(SB % 4 == 0 && CG % SB == 0, "batches of whole float4 scale words");
+	constexpr int kSlotWords = row_slot(CG) / 4;
 #pragma unroll 1
-	for (int b0 = 0; b0 < kChunkGroups; b0 += SB) {
+	for (int b0 = 0; b0 < CG; b0 += SB) {
 		if (b0 >= gk)
 			break;
 		int dots[NM][SB];
@@ -500,26 +513,33 @@ __device__ __forceinline__ void chunk_chains_ws(float (&acc)[NM], const uint32_t
 			if (b0 + j < gk)
 #pragma unroll
 				for (int m = 0; m < NM; ++m) {
-					const uint32_t *wr = st + m * R * (kRowSlot / 4) + (b0 + j) * 16;
+					const uint32_t *wr = st + m * R * kSlotWords + (b0 + j) * 16;
 					dots[m][j] = lane_dot(a[(b0 + j) * 16 + l], wr[l], a[(b0 + j) * 16 + 8 + l], wr[8 + l], flag);
 				}
-		if (flag) {
+		if (flag) { // cold: the exporter never writes -128
 #pragma unroll
 			for (int j = 0; j < SB; ++j)
 				if (b0 + j < gk)
 #pragma unroll
 					for (int m = 0; m < NM; ++m) {
-						const uint32_t *wr = st + m * R * (kRowSlot / 4) + (b0 + j) * 16;
-						dots[m][j] += lane_dot_correction(a[(b0 + j) * 16 + l], wr[l], a[(b0 + j) * 16 + 8 + l], wr[8 + l]);
+						const uint32_t *wr = st + m * R * kSlotWords + (b0 + j) * 16;
+						dots[m][j] += lane_dot_correction_call(a[(b0 + j) * 16 + l], wr[l], a[(b0 + j) * 16 + 8 + l], wr[8 + l]);
 					}
 		}
-		const float4 x0 = *reinterpret_cast<const float4 *>(xsc + b0), x1 = *reinterpret_cast<const float4 *>(xsc + b0 + 4);
-		const float xv[SB] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+		float xv[SB];
+#pragma unroll
+		for (int q = 0; q < SB / 4; ++q) {
+			const float4 x4 = *reinterpret_cast<const float4 *>(xsc + b0 + 4 * q);
+			xv[4 * q] = x4.x, xv[4 * q + 1] = x4.y, xv[4 * q + 2] = x4.z, xv[4 * q + 3] = x4.w;
+		}
 #pragma unroll
 		for (int m = 0; m < NM; ++m) {
-			const float4 w0 = *reinterpret_cast<const float4 *>(wsr + m * mstride + b0);
-			const float4 w1 = *reinterpret_cast<const float4 *>(wsr + m * mstride + b0 + 4);
-			const float wv[SB] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+			float wv[SB];
+#pragma unroll
+			for (int q = 0; q < SB / 4; ++q) {
+				const float4 w4 = *reinterpret_cast<const float4 *>(wsr + m * mstride + b0 + 4 * q);
+				wv[4 * q] = w4.x, wv[4 * q + 1] = w4.y, wv[4 * q + 2] = w4.z, wv[4 * q + 3] = w4.w;
+			}
 #pragma unroll
 			for (int j = 0; j < SB; ++j)
 				if (b0 + j < gk)
@@ -534,13 +554,14 @@ __device__ __forceinline__ void chunk_chains_ws(float (&acc)[NM], const uint32_t
 // same order as one thread would).  Called by every thread of the warp (the
 // shuffles need them all); rows past the matrix compute on stale slots and
 // are not stored.  base: first lane of the row's 16 in the warp.
-template <int NM, int R>
+template <int NM, int R, int CG = kChunkGroups>
 __device__ __forceinline__ void chunk_chains_ws2(float (&acc)[NM], const uint32_t *st, const uint32_t *a, const float *wsr, int mstride, const float *xsc, int l, int j, int base, int gk)
 {
 	using M = F<true>;
 	constexpr int SB = 8; // groups per batch, SB / 2 per thread
+	constexpr int kSlotWords = row_slot(CG) / 4;
 #pragma unroll 1
-	for (int b0 = 0; b0 < kChunkGroups; b0 += SB) {
+	for (int b0 = 0; b0 < CG; b0 += SB) {
 		if (b0 >= gk)
 			break;
 		int dots[NM][SB / 2];
@@ -550,7 +571,7 @@ __device__ __forceinline__ void chunk_chains_ws2(float (&acc)[NM], const uint32_
 			const int g = b0 + 2 * i + j;
 #pragma unroll
 			for (int m = 0; m < NM; ++m) {
-				const uint32_t *wr = st + m * R * (kRowSlot / 4) + g * 16;
+				const uint32_t *wr = st + m * R * kSlotWords + g * 16;
 				dots[m][i] = g < gk ? lane_dot(a[g * 16 + l], wr[l], a[g * 16 + 8 + l], wr[8 + l], flag) : 0;
 			}
 		}
@@ -561,7 +582,7 @@ __device__ __forceinline__ void chunk_chains_ws2(float (&acc)[NM], const uint32_
 				if (g < gk)
 #pragma unroll
 					for (int m = 0; m < NM; ++m) {
-						const uint32_t *wr = st + m * R * (kRowSlot / 4) + g * 16;
+						const uint32_t *wr = st + m * R * kSlotWords + g * 16;
 						dots[m][i] += lane_dot_correction(a[g * 16 + l], wr[l], a[g * 16 + 8 + l], wr[8 + l]);
 					}
 			}
@@ -606,17 +627,19 @@ __host__ __device__ inline size_t stream_fixed(int mode, int rows_per_block, int
 	return slots + act;
 }
 
-template <int MODE, bool FUSED, int R, int J, int P>
+template <int MODE, bool FUSED, int R, int J, int P, int CG>
 __global__ void __launch_bounds__(R * kLanes * J + 32 * P, 2) k_q8_gemv_stream(GemvArgs p, int stages, int xstaged_arg)
 {
 	static_assert(J == 1 || (J == 2 && MODE != 2), "two threads per row lane only for Q8 x Q8");
 	static_assert(P >= 1 && P <= 4, "one to four producer warps");
 	constexpr int NM = MODE == 0 ? 1 : 2;
 	constexpr int kConsumers = R * kLanes * J;
-	constexpr int kStageBytes = NM * R * kRowSlot;
+	static_assert(CG % 16 == 0, "whole 16-group batches per chunk");
+	constexpr int kSlot = row_slot(CG);
+	constexpr int kStageBytes = NM * R * kSlot;
 	extern __shared__ __align__(128) unsigned char smem[];
 	const int n = p.n, groups = n / kQ8Group;
-	const int nchunks = (groups + kChunkGroups - 1) / kChunkGroups;
+	const int nchunks = (groups + CG - 1) / CG;
 	const int64_t nrb = (p.d + R - 1) / R;
 	const int64_t b = blockIdx.y;
 	// only the fp32-activation forms have a staging area in their layout
@@ -648,6 +671,20 @@ __global__ void __launch_bounds__(R * kLanes * J + 32 * P, 2) k_q8_gemv_stream(G
 	}
 	__syncthreads();
 	const bool pro_copy = (MODE != 2 && !FUSED) || xstaged;
+	// FUSED: every thread of the CTA quantises its share of the activation
+	// (the producer warps once they have issued their first stages, before
+	// which no stage can be freed anyway), then all meet at named barrier 2.
+	// Each thread arrives there exactly once and waits for nothing unbounded
+	// before it.
+	auto quantise_all = [&]() {
+		if (xstaged) {
+			mbar_wait(pro, 0, &g_pipeline_timeouts);
+			stage_quantized<true>(xstage, n, sq, ss, kConsumers + 32 * P);
+		} else {
+			stage_quantized<false>(p.xf + b * n, n, sq, ss, kConsumers + 32 * P);
+		}
+		named_sync(2, kConsumers + 32 * P);
+	};
 	if (threadIdx.x >= kConsumers) {
 		// P producer warps: warp 0 also copies the activation and the scales;
 		// the copies of a stage are dealt round-robin (a warp issues one copy
@@ -668,7 +705,14 @@ __global__ void __launch_bounds__(R * kLanes * J + 32 * P, 2) k_q8_gemv_stream(G
 		uint32_t q = 0;
 		int i = 0;
 		bool ok = true;
+		// FUSED: join the quantisation just before the first wait of any kind
+		// (row block 2's scale slot, or chunk `stages`), or at the end
+		bool joined = !FUSED;
 		for (int64_t rb = blockIdx.x; rb < nrb && ok; rb += gridDim.x, ++i) {
+			if (!joined && i >= 2) {
+				quantise_all();
+				joined = true;
+			}
 			const int64_t row0 = rb * R;
 			const int rows = (int)min((int64_t)R, p.d - row0);
 			const int slot = i & 1;
@@ -688,12 +732,16 @@ __global__ void __launch_bounds__(R * kLanes * J + 32 * P, 2) k_q8_gemv_stream(G
 			const int mine = ncopy > pw ? (ncopy - pw + P - 1) / P : 0; // copies pw, pw + P, ...
 			for (int k = 0; k < nchunks; ++k, ++q) {
 				const int s = (int)(q % (uint32_t)stages);
+				if (!joined && q >= (uint32_t)stages) {
+					quantise_all();
+					joined = true;
+				}
 				if (q >= (uint32_t)stages && lane == 0)
 					ok = mbar_wait(empty + s, ((q / stages) - 1) & 1, &g_pipeline_timeouts);
 				if (!__shfl_sync(0xffffffffu, ok, 0))
 					break;
-				const int g0 = k * kChunkGroups;
-				const int gk = min(kChunkGroups, groups - g0);
+				const int g0 = k * CG;
+				const int gk = min(CG, groups - g0);
 				const uint32_t bytes = (uint32_t)(gk * kQ8Group);
 				if (lane == 0)
 					mbar_arrive_expect_tx(full + s, bytes * (uint32_t)mine);
@@ -704,11 +752,13 @@ __global__ void __launch_bounds__(R * kLanes * J + 32 * P, 2) k_q8_gemv_stream(G
 					// a select, not p.wq[m]: a runtime index into the parameter
 					// array would copy it to local memory
 					const int8_t *wm = m == 0 ? p.wq[0] : p.wq[NM - 1];
-					bulk_copy_g2s(smem + (size_t)s * kStageBytes + (m * R + r) * kRowSlot, wm + (row0 + r) * n + (int64_t)g0 * kQ8Group, bytes,
+					bulk_copy_g2s(smem + (size_t)s * kStageBytes + (m * R + r) * kSlot, wm + (row0 + r) * n + (int64_t)g0 * kQ8Group, bytes,
 					              full + s);
 				}
 			}
 		}
+		if (!joined)
+			quantise_all();
 		// leave only once every copy issued has landed
 		if (lane == 0) {
 			for (uint32_t k = q > (uint32_t)stages ? q - stages : 0; k < q; ++k)
@@ -724,21 +774,18 @@ __global__ void __launch_bounds__(R * kLanes * J + 32 * P, 2) k_q8_gemv_stream(G
 		}
 		return;
 	}
-	// consumers: the activation first
-	if (pro_copy && !__all_sync(0xffffffffu, mbar_wait(pro, 0, &g_pipeline_timeouts)))
-		return;
+	// consumers.  A wait that runs out clears the warp's `live` flag: the warp
+	// skips its remaining waits and arithmetic but still reaches every named
+	// barrier below, so the other warps' barriers complete; nothing is stored.
+	bool live = !pro_copy || __all_sync(0xffffffffu, mbar_wait(pro, 0, &g_pipeline_timeouts));
 	if (MODE == 2) {
 		const float *xb = p.xf + b * n;
 		for (int e = threadIdx.x; e < n; e += kConsumers)
 			xt[(e & 7) * xstride + (e >> 6) * 8 + ((e >> 3) & 7)] = xstaged ? xstage[e] : __ldg(xb + e);
 		named_sync(1, kConsumers);
-	} else if (FUSED) {
-		if (xstaged)
-			stage_quantized<true>(xstage, n, sq, ss, kConsumers);
-		else
-			stage_quantized<false>(p.xf + b * n, n, sq, ss, kConsumers);
-		named_sync(1, kConsumers);
 	}
+	if (FUSED)
+		quantise_all();
 	const int r = threadIdx.x / (kLanes * J), l = threadIdx.x & (kLanes - 1);
 	const int j = J == 1 ? 0 : (threadIdx.x >> 3) & 1;
 	const int base = (threadIdx.x & 31) & ~15;
@@ -749,8 +796,7 @@ __global__ void __launch_bounds__(R * kLanes * J + 32 * P, 2) k_q8_gemv_stream(G
 		const int rows = (int)min((int64_t)R, p.d - row0);
 		const bool valid = r < rows;
 		const int slot = i & 1;
-		if (!__all_sync(0xffffffffu, mbar_wait(sfull + slot, (i >> 1) & 1, &g_pipeline_timeouts)))
-			return;
+		live = live && __all_sync(0xffffffffu, mbar_wait(sfull + slot, (i >> 1) & 1, &g_pipeline_timeouts));
 		const float *wsr = sws + slot * NM * mstride + r * groups;
 		float acc[NM];
 #pragma unroll
@@ -758,22 +804,22 @@ __global__ void __launch_bounds__(R * kLanes * J + 32 * P, 2) k_q8_gemv_stream(G
 			acc[m] = 0.0f;
 		for (int k = 0; k < nchunks; ++k, ++q) {
 			const int s = (int)(q % (uint32_t)stages);
-			// the warp leaves together if any lane's wait ran out
-			if (!__all_sync(0xffffffffu, mbar_wait(full + s, (q / stages) & 1, &g_pipeline_timeouts)))
-				return;
-			const int g0 = k * kChunkGroups;
-			const int gk = min(kChunkGroups, groups - g0);
-			if constexpr (J == 2) {
-				const uint32_t *st = reinterpret_cast<const uint32_t *>(smem + (size_t)s * kStageBytes) + r * (kRowSlot / 4);
-				chunk_chains_ws2<NM, R>(acc, st, sq + g0 * 16, wsr + g0, mstride, ss + g0, l, j, base, gk);
+			const int g0 = k * CG;
+			const int gk = min(CG, groups - g0);
+			// warp-uniform: the warp waits, and computes, together
+			live = live && __all_sync(0xffffffffu, mbar_wait(full + s, (q / stages) & 1, &g_pipeline_timeouts));
+			if (!live) {
+			} else if constexpr (J == 2) {
+				const uint32_t *st = reinterpret_cast<const uint32_t *>(smem + (size_t)s * kStageBytes) + r * (kSlot / 4);
+				chunk_chains_ws2<NM, R, CG>(acc, st, sq + g0 * 16, wsr + g0, mstride, ss + g0, l, j, base, gk);
 			} else if (valid) {
-				const uint32_t *st = reinterpret_cast<const uint32_t *>(smem + (size_t)s * kStageBytes) + r * (kRowSlot / 4);
+				const uint32_t *st = reinterpret_cast<const uint32_t *>(smem + (size_t)s * kStageBytes) + r * (kSlot / 4);
 				if constexpr (MODE == 2)
-					chunk_f32<R>(acc, st, xt + l * xstride + g0 * 8, wsr + g0, groups, l, gk);
-				else if (gk == kChunkGroups)
-					chunk_chains_ws<NM, R>(acc, st, sq + g0 * 16, wsr + g0, mstride, ss + g0, l, kChunkGroups);
+					chunk_f32<R, CG>(acc, st, xt + l * xstride + g0 * 8, wsr + g0, groups, l, gk);
+				else if (gk == CG) // one matrix: 16-group batches, the most independent work per wait
+					chunk_chains_ws<NM, R, NM == 1 ? 16 : 8, CG>(acc, st, sq + g0 * 16, wsr + g0, mstride, ss + g0, l, CG);
 				else
-					chunk_chains_ws<NM, R>(acc, st, sq + g0 * 16, wsr + g0, mstride, ss + g0, l, gk);
+					chunk_chains_ws<NM, R, 8, CG>(acc, st, sq + g0 * 16, wsr + g0, mstride, ss + g0, l, gk);
 			}
 			__syncwarp();
 			if ((threadIdx.x & 31) == 0)
@@ -783,7 +829,7 @@ __global__ void __launch_bounds__(R * kLanes * J + 32 * P, 2) k_q8_gemv_stream(G
 #pragma unroll
 		for (int m = 0; m < NM; ++m)
 			res[m] = hadd_lanes(acc[m]);
-		if (valid && l == 0 && j == 0)
+		if (live && valid && l == 0 && j == 0)
 			p.out[b * p.d + row0 + r] = MODE == 0 ? res[0] : v7_swiglu(res[0], res[NM - 1]);
 		__syncwarp();
 		if ((threadIdx.x & 31) == 0)
@@ -912,18 +958,19 @@ int launch_gemv_tma(const char *what, const GemvArgs &a, int64_t batch, void *st
 }
 
 // Per-CTA shared memory aimed at two CTAs per SM, or one when two stages do
-// not fit that way.
+// not fit that way or when there are no more row blocks than SMs (one CTA
+// per SM then in any case, so it may as well take the whole SM).
 constexpr size_t kStreamSmemTwo = 110 * 1024;
 constexpr size_t kStreamSmemOne = 220 * 1024;
 
-StreamLayout stream_layout(int mode, bool fused, int rows_per_block, int n, bool x_aligned)
+StreamLayout stream_layout(int mode, bool fused, int rows_per_block, int n, bool x_aligned, int cg, bool one_per_sm = false)
 {
 	const int nm = mode == 0 ? 1 : 2;
-	const size_t stage = (size_t)nm * rows_per_block * kRowSlot;
+	const size_t stage = (size_t)nm * rows_per_block * row_slot(cg);
 	const size_t bars = 8 * (2 * (size_t)kMaxStages + 5);
 	const size_t fixed = stream_fixed(mode, rows_per_block, n) + bars;
 	const bool want_x = (mode == 2 || fused) && x_aligned;
-	for (size_t budget : {kStreamSmemTwo, kStreamSmemOne})
+	for (size_t budget : {one_per_sm ? kStreamSmemOne : kStreamSmemTwo, kStreamSmemOne})
 		for (int xs = want_x ? 1 : 0; xs >= 0; --xs) {
 			const size_t base = fixed + (xs ? 4 * (size_t)n : 0);
 			if (base + 2 * stage > budget)
@@ -937,14 +984,15 @@ StreamLayout stream_layout(int mode, bool fused, int rows_per_block, int n, bool
 // Streaming-kernel shapes, measured on B200 at the decode shapes (d = 2048
 // .. 12288): 16 rows per block everywhere (also where that leaves SMs idle:
 // a block's 16 copies per stage keep more bytes in flight per CTA than two
-// blocks of 8); four producer warps for the one-matrix product, two for the
-// two-matrix ones; two threads per row lane for the fused quantise (its
-// in-kernel activation quantisation gets twice the threads).
+// blocks of 8); four producer warps and 2 KB row copies for the one-matrix
+// product (it is paced by how fast copies are issued), two producer warps
+// and 1 KB copies for the two-matrix ones (their stages are twice as big).
 template <int MODE, bool FUSED>
 struct StreamShape {
 	static constexpr int R = 16;
-	static constexpr int J = FUSED ? 2 : 1;
-	static constexpr int P = (MODE == 0 && !FUSED) ? 4 : 2;
+	static constexpr int J = 1;
+	static constexpr int P = MODE == 0 ? 4 : 2;
+	static constexpr int CG = MODE == 0 ? 32 : kChunkGroups;
 };
 
 // grid = the resident CTAs (split over the batch), at most one per row
@@ -961,10 +1009,11 @@ int launch_gemv_stream(const char *what, const GemvArgs &a, int64_t batch, void 
 	int rc = current_device(&dev);
 	if (rc != V7G_OK)
 		return rc;
-	const StreamLayout lay = stream_layout(MODE, FUSED, S::R, a.n, aligned16(a.xf));
+	const int64_t nrb = (a.d + S::R - 1) / S::R;
+	const StreamLayout lay = stream_layout(MODE, FUSED, S::R, a.n, aligned16(a.xf), S::CG, nrb * batch <= dev.sm_count);
 	if (lay.stages < 2)
 		return V7G_ERR_UNSUPPORTED;
-	const void *kernel = (const void *)k_q8_gemv_stream<MODE, FUSED, S::R, S::J, S::P>;
+	const void *kernel = (const void *)k_q8_gemv_stream<MODE, FUSED, S::R, S::J, S::P, S::CG>;
 	const int threads = S::R * kLanes * S::J + 32 * S::P;
 	// the shared-memory ceiling of the kernel is raised once per device
 	static bool raised[kMaxDevicesTracked];
@@ -977,10 +1026,9 @@ int launch_gemv_stream(const char *what, const GemvArgs &a, int64_t batch, void 
 	int per_sm = 0;
 	if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, lay.smem) != cudaSuccess || per_sm < 1)
 		return check_launch(what);
-	const int64_t nrb = (a.d + S::R - 1) / S::R;
 	const int64_t slots = std::max<int64_t>(1, (int64_t)per_sm * dev.sm_count / batch);
 	const dim3 grid((unsigned)std::min(nrb, slots), (unsigned)batch);
-	k_q8_gemv_stream<MODE, FUSED, S::R, S::J, S::P><<<grid, threads, lay.smem, (cudaStream_t)stream>>>(a, lay.stages, lay.xstaged ? 1 : 0);
+	k_q8_gemv_stream<MODE, FUSED, S::R, S::J, S::P, S::CG><<<grid, threads, lay.smem, (cudaStream_t)stream>>>(a, lay.stages, lay.xstaged ? 1 : 0);
 	return check_launch(what);
 }
 

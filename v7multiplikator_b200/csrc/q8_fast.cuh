@@ -48,16 +48,23 @@ __device__ __forceinline__ float4 v7_swiglu4(float4 g, float4 u)
 	return make_float4(a.x, a.y, b.x, b.y);
 }
 
-// q8_scale for a finite maximum without the general divide: wmax / 127 as a
-// double product rounded once to float.  That is the correctly rounded
-// quotient for every wmax here: the product carries a relative error below
-// 2.2 * 2^-53, so a wrong float rounding would need the exact quotient within
-// that distance of a float rounding boundary, i.e. 27 equal bits after its
-// 25th significant bit; the expansion of an integer over 127 repeats with
-// period 7 (2^7 = 1 mod 127), so such a run only occurs when the quotient is
-// exact.  The reciprocal takes the Markstein form.  An inf or a NaN that
-// survived the tree takes the IEEE instructions.  v7g_selftest_arith checks
-// scale and reciprocal against div.rn / rcp.rn for every possible maximum.
+// q8_scale for a finite maximum without the general divide, in single
+// precision: wmax / 127 as a product by the constant 1/127 held as two floats,
+// Ch + Cl (Ch = RN(1/127), Cl = RN(1/127 - Ch)), evaluated the way Brisebarre
+// and Muller give for correctly rounded multiplication by an arbitrary
+// precision constant ("Correctly rounded multiplication by arbitrary precision
+// constants", IEEE Trans. Computers 57(2), 2008): u = RN(w * Cl), then
+// RN(w * Ch + u) in one fused multiply-add.  For this constant that is the
+// correctly rounded quotient for every w in the floored range; below 2^-60
+// the maximum is first scaled by 2^64 (exactly) so that w * Cl stays a normal
+// float under FTZ, and the quotient (at least FLT_MIN, so normal) scaled back
+// exactly.  No double-precision instruction: those are a scarce pipe here.
+// The reciprocal takes the Markstein form.  An inf or a NaN that survived the
+// tree takes the IEEE instructions.  v7g_selftest_arith checks scale and
+// reciprocal against div.rn / rcp.rn for every possible maximum.
+constexpr float kInv127Hi = 7.87401572e-03f; // 0x3C010204
+constexpr float kInv127Lo = 2.93329942e-11f; // 0x2E010204
+
 // The IEEE instructions for an inf or NaN maximum, out of line (rare).
 static __device__ __noinline__ float2 q8_scale_ieee(float wmax)
 {
@@ -70,7 +77,11 @@ __device__ __forceinline__ void q8_scale_fast(float wmax, float &scale, float &r
 {
 	wmax = x86_max(wmax, kQ8WmaxFloor);
 	if (wmax <= 3.402823466e38f) {
-		scale = __double2float_rn(__dmul_rn((double)wmax, 1.0 / 127.0));
+		using M = F<true>;
+		const bool tiny = wmax < 8.67361738e-19f; // 2^-60
+		const float w = tiny ? M::mul(wmax, 1.84467441e19f) : wmax; // * 2^64
+		const float q = M::fma(w, kInv127Hi, M::mul(w, kInv127Lo));
+		scale = tiny ? M::mul(q, 5.42101086e-20f) : q; // * 2^-64
 		recip = rcp_nr(scale); // scale in [FLT_MIN, FLT_MAX/127]: reciprocal normal
 	} else {
 		const float2 sr = q8_scale_ieee(wmax);
