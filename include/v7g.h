@@ -154,7 +154,8 @@ int v7g_swiglu_f32q8_gemv(float *out, const float *x, const int8_t *gate_q, cons
 
 /* Number of bounded waits in the pipelined GEMV kernels that gave up since
    the library was loaded (a kernel that gives up writes no result for the
-   rows it was computing).  0 in every correct run. */
+   rows it was computing).  0 in every correct run; 0xffffffff when the
+   counter cannot be read. */
 unsigned int v7g_pipeline_timeouts(void);
 
 /* RMSNorm rows on HOST buffers with no device allocation.  No counterpart in
@@ -194,8 +195,10 @@ uint64_t v7g_launch_count(void);
 /* Exhaustive device self-check of the library's fast arithmetic (the
    Markstein-corrected reciprocal, the fast Q8 scale, the packed-pair SiLU and
    Q8 code paths) against the plain IEEE instructions, over every input each can
-   receive.  dev_counts: 6 zeroed device counters, incremented by the number of
-   mismatches of each test (all must stay 0).  Asynchronous on `stream`. */
+   receive, plus 2^31 Q8 products next to a rounding tie (where fusing the
+   product into the rounding step would show).  dev_counts: 7 zeroed device
+   counters, incremented by the number of mismatches of each test (all must
+   stay 0).  Asynchronous on `stream`. */
 int v7g_selftest_arith(unsigned long long *dev_counts, void *stream);
 
 /* Library version string. */

@@ -29,7 +29,10 @@ LIB = LIBDIR / "libv7_threading.so"
 CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 NVCC = str(CUDA_HOME / "bin" / "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xptxas", "-warn-spills"] + ARCH
+# --fmad=false: the reference rounds every product that it does not fuse
+# explicitly, and the kernels spell each intended fused multiply-add as one
+# (fp.cuh, arith.cuh); the compiler must not contract anything else.
+NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "--fmad=false", "-Xcompiler", "-fPIC", "-Xptxas", "-warn-spills"] + ARCH
 CXX_FLAGS = ["-O2", "-std=c++17", "-fPIC", "-Wall", "-Wno-unused-parameter", f"-I{CUDA_HOME / 'include'}"]
 
 KERNEL_SOURCES = ["runtime.cu", "norm.cu", "norm_q8.cu", "rope.cu", "rope_only.cu", "rope_tables.cu", "swiglu.cu", "add.cu",

@@ -9,6 +9,16 @@
 // compilation unit's -ftz setting, so this header may only be used from units
 // built with -ftz=true (build.py defines V7G_FTZ_TU for them).
 //
+// A pair product that feeds a pair sum directly can come out fused into one
+// multiply-add in some kernels (seen with a product added to a rounding
+// constant), losing the product's rounding.  Code that relies on that
+// rounding must not have that shape: q8_codes4_small converts the product
+// with cvt.rni instead; the other kernels put a separate step between
+// (q8_codes4_x2 its clamp) or use the product more than once (v7_sigmoid_x2),
+// and v7g_selftest_arith checks each over its inputs.  (Inline-PTX pair
+// operations would rule it out but cost a third of the SwiGLU throughput in
+// register-pair moves.)
+//
 // rcp.rn expands to a general sequence with special-case branches.  For the
 // arguments these kernels have (finite, normal, normal reciprocal) the
 // correctly rounded 1/d comes from the hardware reciprocal seed (rcp.approx,

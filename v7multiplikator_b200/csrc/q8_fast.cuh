@@ -92,18 +92,21 @@ __device__ __forceinline__ void q8_scale_fast(float wmax, float &scale, float &r
 
 // Codes of four values whose products p = h * recip satisfy |p| < 127.5 (a
 // group with neither NaN nor infinity, quantised with its own scale: |p| is
-// at most 127 (1 + 3 * 2^-24)): round to nearest even through the 1.5 * 2^23
-// addition and keep the low byte.  For such p the reference's conversion,
-// saturating packs and -127 floor change nothing, so no clamp or range test
-// is needed.  Checked against q8_code_bits over every such p by
-// v7g_selftest_arith.
+// at most 127 (1 + 3 * 2^-24)): the rounded product converted to the nearest
+// integer, ties to even (cvt.rni, CVTPS2DQ's rounding), keeping the low byte.
+// For such p the reference's saturating packs and -127 floor change nothing,
+// so no clamp or range test is needed.  The conversion takes the product as
+// rounded by its own multiply: no fused multiply-add can skip that rounding
+// (a product added straight to a 1.5 * 2^23 rounding constant was fused by
+// the compiler in some kernels, which moved exact ties).  Checked against
+// q8_code_bits over every such p, and on products next to a tie under
+// non-trivial reciprocals, by v7g_selftest_arith.
 __device__ __forceinline__ uint32_t q8_codes4_small(float4 h, float recip)
 {
 	const float2 p01 = mul2(make_float2(h.x, h.y), splat2(recip));
 	const float2 p23 = mul2(make_float2(h.z, h.w), splat2(recip));
-	const float2 b01 = add2(p01, splat2(kRoundMagic));
-	const float2 b23 = add2(p23, splat2(kRoundMagic));
-	return pack4_low_bytes(__float_as_uint(b01.x), __float_as_uint(b01.y), __float_as_uint(b23.x), __float_as_uint(b23.y));
+	return pack4_low_bytes((uint32_t)__float2int_rn(p01.x), (uint32_t)__float2int_rn(p01.y), (uint32_t)__float2int_rn(p23.x),
+	                       (uint32_t)__float2int_rn(p23.y));
 }
 
 // q8_codes4 with pair arithmetic.

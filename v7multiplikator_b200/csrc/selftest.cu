@@ -11,6 +11,11 @@
 //           absmax in [2^-127, 2^128) plus inf and NaN
 //   test 5  q8_codes4_small code == q8_code_bits code for every p with
 //           |p| < 127.5 (recip = 1, so p = h)
+//   test 6  q8_codes4_small and q8_codes4_x2 == q8_code_bits of the rounded
+//           product h * recip, for 2^31 products within a few ulps of a
+//           rounding tie m + 1/2 under 2^16 reciprocals: where the product's
+//           own rounding decides the code (a fused multiply-add would not
+//           round it)
 // The counts of mismatches are the kernel's output (all zero when the fast
 // forms are exact over their whole input range).
 #include "internal.h"
@@ -27,7 +32,7 @@ __global__ void __launch_bounds__(kBlock) k_selftest(unsigned long long *counts)
 {
 	const uint64_t stride = (uint64_t)gridDim.x * kBlock;
 	const uint64_t tid = (uint64_t)blockIdx.x * kBlock + threadIdx.x;
-	unsigned long long bad[6] = {0, 0, 0, 0, 0, 0};
+	unsigned long long bad[7] = {0, 0, 0, 0, 0, 0, 0};
 	// test 0: exponents -126 .. 125
 	for (uint64_t i = tid; i < (252ull << 23); i += stride) {
 		const float d = from_exp_mant((int)(i >> 23) - 126, (uint32_t)(i & 0x7fffff));
@@ -71,7 +76,24 @@ __global__ void __launch_bounds__(kBlock) k_selftest(unsigned long long *counts)
 		const uint32_t want = pack4_low_bytes(q8_code_bits(p0), q8_code_bits(p1), q8_code_bits(p1), q8_code_bits(p0));
 		bad[5] += packed != want;
 	}
-	for (int t = 0; t < 6; ++t)
+	// test 6: i = [recip 16 bits | tie 8 bits | offset 7 bits]; recip in
+	// [2^-7, 2^9) spread over mantissas and exponents, h = RN(t / recip)
+	// nudged by -3..+3 ulps, t = m + 1/2 for m in [-128, 127]
+	for (uint64_t i = tid; i < (1ull << 31); i += stride) {
+		const uint32_t ri = (uint32_t)(i >> 15);
+		const float recip = from_exp_mant((int)(ri >> 12) - 7, (ri * 2654435761u) & 0x7fffffu);
+		const float t = (float)((int)((i >> 7) & 0xff) - 128) + 0.5f;
+		const int nudge = (int)(i & 7) - 3;
+		const float h0 = F<true>::div(t, recip);
+		const float h = __uint_as_float(__float_as_uint(h0) + nudge);
+		const float p = F<true>::mul(h, recip);
+		const uint32_t want = q8_code_bits(p) & 0xffu;
+		const float4 h4 = make_float4(h, h, h, h);
+		const uint32_t small = fabsf(p) < 127.5f ? q8_codes4_small(h4, recip) : want * 0x01010101u;
+		const uint32_t x2 = q8_codes4_x2(h4, recip);
+		bad[6] += (small != want * 0x01010101u) + (x2 != want * 0x01010101u);
+	}
+	for (int t = 0; t < 7; ++t)
 		if (bad[t])
 			atomicAdd(counts + t, bad[t]);
 }

@@ -496,9 +496,9 @@ def v7s_rmsnorm_quantize(out_q: torch.Tensor, in_x: torch.Tensor, out_s: torch.T
 
 def selftest_arith(device: Optional[torch.device] = None) -> list[int]:
     """Runs the library's exhaustive device check of its fast arithmetic and
-    returns the mismatch count of each of its six tests (all 0 when exact)."""
+    returns the mismatch count of each of its seven tests (all 0 when exact)."""
     device = device or torch.device("cuda", torch.cuda.current_device())
-    counts = torch.zeros(6, dtype=torch.int64, device=device)
+    counts = torch.zeros(7, dtype=torch.int64, device=device)
     _check(lib().v7g_selftest_arith(counts.data_ptr(), _stream(counts, None)))
     return [int(c) for c in counts.cpu().tolist()]
 
