@@ -548,66 +548,6 @@ __device__ __forceinline__ void chunk_chains_ws(float (&acc)[NM], const uint32_t
 	}
 }
 
-// chunk_chains_ws with two threads per row lane (J = 2): thread j computes
-// the dots of groups b0 + 2i + j, the pair exchanges them through shuffles
-// and both run the lane's chain over all groups in order (same operations,
-// same order as one thread would).  Called by every thread of the warp (the
-// shuffles need them all); rows past the matrix compute on stale slots and
-// are not stored.  base: first lane of the row's 16 in the warp.
-template <int NM, int R, int CG = kChunkGroups>
-__device__ __forceinline__ void chunk_chains_ws2(float (&acc)[NM], const uint32_t *st, const uint32_t *a, const float *wsr, int mstride, const float *xsc, int l, int j, int base, int gk)
-{
-	using M = F<true>;
-	constexpr int SB = 8; // groups per batch, SB / 2 per thread
-	constexpr int kSlotWords = row_slot(CG) / 4;
-#pragma unroll 1
-	for (int b0 = 0; b0 < CG; b0 += SB) {
-		if (b0 >= gk)
-			break;
-		int dots[NM][SB / 2];
-		uint32_t flag = 0;
-#pragma unroll
-		for (int i = 0; i < SB / 2; ++i) {
-			const int g = b0 + 2 * i + j;
-#pragma unroll
-			for (int m = 0; m < NM; ++m) {
-				const uint32_t *wr = st + m * R * kSlotWords + g * 16;
-				dots[m][i] = g < gk ? lane_dot(a[g * 16 + l], wr[l], a[g * 16 + 8 + l], wr[8 + l], flag) : 0;
-			}
-		}
-		if (flag) {
-#pragma unroll
-			for (int i = 0; i < SB / 2; ++i) {
-				const int g = b0 + 2 * i + j;
-				if (g < gk)
-#pragma unroll
-					for (int m = 0; m < NM; ++m) {
-						const uint32_t *wr = st + m * R * kSlotWords + g * 16;
-						dots[m][i] += lane_dot_correction(a[g * 16 + l], wr[l], a[g * 16 + 8 + l], wr[8 + l]);
-					}
-			}
-		}
-		const float4 x0 = *reinterpret_cast<const float4 *>(xsc + b0), x1 = *reinterpret_cast<const float4 *>(xsc + b0 + 4);
-		const float xv[SB] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-#pragma unroll
-		for (int m = 0; m < NM; ++m) {
-			const float4 w0 = *reinterpret_cast<const float4 *>(wsr + m * mstride + b0);
-			const float4 w1 = *reinterpret_cast<const float4 *>(wsr + m * mstride + b0 + 4);
-			const float wv[SB] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-#pragma unroll
-			for (int i = 0; i < SB / 2; ++i) {
-				const float mine = (float)dots[m][i];
-				const float de = __shfl_sync(0xffffffffu, mine, base + l);
-				const float dodd = __shfl_sync(0xffffffffu, mine, base + 8 + l);
-				if (b0 + 2 * i < gk)
-					acc[m] = M::fma(de, M::mul(wv[2 * i], xv[2 * i]), acc[m]);
-				if (b0 + 2 * i + 1 < gk)
-					acc[m] = M::fma(dodd, M::mul(wv[2 * i + 1], xv[2 * i + 1]), acc[m]);
-			}
-		}
-	}
-}
-
 struct StreamLayout {
 	int stages;
 	bool xstaged;  // the fp32 activation arrives by bulk copy (FUSED, MODE 2)
@@ -627,13 +567,12 @@ __host__ __device__ inline size_t stream_fixed(int mode, int rows_per_block, int
 	return slots + act;
 }
 
-template <int MODE, bool FUSED, int R, int J, int P, int CG>
-__global__ void __launch_bounds__(R * kLanes * J + 32 * P, 2) k_q8_gemv_stream(GemvArgs p, int stages, int xstaged_arg)
+template <int MODE, bool FUSED, int R, int P, int CG>
+__global__ void __launch_bounds__(R * kLanes + 32 * P, 2) k_q8_gemv_stream(GemvArgs p, int stages, int xstaged_arg)
 {
-	static_assert(J == 1 || (J == 2 && MODE != 2), "two threads per row lane only for Q8 x Q8");
 	static_assert(P >= 1 && P <= 4, "one to four producer warps");
 	constexpr int NM = MODE == 0 ? 1 : 2;
-	constexpr int kConsumers = R * kLanes * J;
+	constexpr int kConsumers = R * kLanes;
 	static_assert(CG % 16 == 0, "whole 16-group batches per chunk");
 	constexpr int kSlot = row_slot(CG);
 	constexpr int kStageBytes = NM * R * kSlot;
@@ -786,9 +725,7 @@ __global__ void __launch_bounds__(R * kLanes * J + 32 * P, 2) k_q8_gemv_stream(G
 	}
 	if (FUSED)
 		quantise_all();
-	const int r = threadIdx.x / (kLanes * J), l = threadIdx.x & (kLanes - 1);
-	const int j = J == 1 ? 0 : (threadIdx.x >> 3) & 1;
-	const int base = (threadIdx.x & 31) & ~15;
+	const int r = threadIdx.x / kLanes, l = threadIdx.x & (kLanes - 1);
 	uint32_t q = 0;
 	int i = 0;
 	for (int64_t rb = blockIdx.x; rb < nrb; rb += gridDim.x, ++i) {
@@ -808,11 +745,7 @@ __global__ void __launch_bounds__(R * kLanes * J + 32 * P, 2) k_q8_gemv_stream(G
 			const int gk = min(CG, groups - g0);
 			// warp-uniform: the warp waits, and computes, together
 			live = live && __all_sync(0xffffffffu, mbar_wait(full + s, (q / stages) & 1, &g_pipeline_timeouts));
-			if (!live) {
-			} else if constexpr (J == 2) {
-				const uint32_t *st = reinterpret_cast<const uint32_t *>(smem + (size_t)s * kStageBytes) + r * (kSlot / 4);
-				chunk_chains_ws2<NM, R, CG>(acc, st, sq + g0 * 16, wsr + g0, mstride, ss + g0, l, j, base, gk);
-			} else if (valid) {
+			if (live && valid) {
 				const uint32_t *st = reinterpret_cast<const uint32_t *>(smem + (size_t)s * kStageBytes) + r * (kSlot / 4);
 				if constexpr (MODE == 2)
 					chunk_f32<R, CG>(acc, st, xt + l * xstride + g0 * 8, wsr + g0, groups, l, gk);
@@ -829,7 +762,7 @@ __global__ void __launch_bounds__(R * kLanes * J + 32 * P, 2) k_q8_gemv_stream(G
 #pragma unroll
 		for (int m = 0; m < NM; ++m)
 			res[m] = hadd_lanes(acc[m]);
-		if (live && valid && l == 0 && j == 0)
+		if (live && valid && l == 0)
 			p.out[b * p.d + row0 + r] = MODE == 0 ? res[0] : v7_swiglu(res[0], res[NM - 1]);
 		__syncwarp();
 		if ((threadIdx.x & 31) == 0)
@@ -990,7 +923,6 @@ StreamLayout stream_layout(int mode, bool fused, int rows_per_block, int n, bool
 template <int MODE, bool FUSED>
 struct StreamShape {
 	static constexpr int R = 16;
-	static constexpr int J = 1;
 	static constexpr int P = MODE == 0 ? 4 : 2;
 	static constexpr int CG = MODE == 0 ? 32 : kChunkGroups;
 };
@@ -1013,8 +945,8 @@ int launch_gemv_stream(const char *what, const GemvArgs &a, int64_t batch, void 
 	const StreamLayout lay = stream_layout(MODE, FUSED, S::R, a.n, aligned16(a.xf), S::CG, nrb * batch <= dev.sm_count);
 	if (lay.stages < 2)
 		return V7G_ERR_UNSUPPORTED;
-	const void *kernel = (const void *)k_q8_gemv_stream<MODE, FUSED, S::R, S::J, S::P, S::CG>;
-	const int threads = S::R * kLanes * S::J + 32 * S::P;
+	const void *kernel = (const void *)k_q8_gemv_stream<MODE, FUSED, S::R, S::P, S::CG>;
+	const int threads = S::R * kLanes + 32 * S::P;
 	// the shared-memory ceiling of the kernel is raised once per device
 	static bool raised[kMaxDevicesTracked];
 	if (dev.device >= kMaxDevicesTracked || !raised[dev.device]) {
@@ -1028,7 +960,7 @@ int launch_gemv_stream(const char *what, const GemvArgs &a, int64_t batch, void 
 		return check_launch(what);
 	const int64_t slots = std::max<int64_t>(1, (int64_t)per_sm * dev.sm_count / batch);
 	const dim3 grid((unsigned)std::min(nrb, slots), (unsigned)batch);
-	k_q8_gemv_stream<MODE, FUSED, S::R, S::J, S::P, S::CG><<<grid, threads, lay.smem, (cudaStream_t)stream>>>(a, lay.stages, lay.xstaged ? 1 : 0);
+	k_q8_gemv_stream<MODE, FUSED, S::R, S::P, S::CG><<<grid, threads, lay.smem, (cudaStream_t)stream>>>(a, lay.stages, lay.xstaged ? 1 : 0);
 	return check_launch(what);
 }
 
