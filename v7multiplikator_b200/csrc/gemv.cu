@@ -316,23 +316,21 @@ __device__ __forceinline__ void chunk_chains(float (&acc)[NM], const uint32_t *s
 template <int R, int CG = kChunkGroups>
 __device__ __forceinline__ void chunk_f32(float (&acc)[2], const uint32_t *st, const float *xl, const float *sw, int sstride, int l, int gk)
 {
-	const bool odd = (l & 4) != 0;
 	const uint32_t sel = 0x7540u | (uint32_t)(l & 3); // byte l % 4, then 0, 0, 0x4B
 	const float2 bias = splat2(-8388736.0f);            // -(2^23 + 128)
 	float2 a = make_float2(acc[0], acc[1]);
+	// the lane's words of step k: 2k + l / 4, loaded one by one (no selects)
+	const uint32_t *stg = st + (l >> 2), *stu = st + R * (row_slot(CG) / 4) + (l >> 2);
 #pragma unroll 2
 	for (int gi = 0; gi < gk; ++gi) {
-		const uint4 *wg = reinterpret_cast<const uint4 *>(st + gi * 16);
-		const uint4 *wu = reinterpret_cast<const uint4 *>(st + R * (row_slot(CG) / 4) + gi * 16);
 		const float4 x0 = *reinterpret_cast<const float4 *>(xl + gi * 8);
 		const float4 x1 = *reinterpret_cast<const float4 *>(xl + gi * 8 + 4);
 		const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
 		const float2 sc = make_float2(sw[gi], sw[R * sstride + gi]);
 #pragma unroll
 		for (int j = 0; j < 4; ++j) {
-			const uint4 g4 = wg[j], u4 = wu[j];
-			const uint32_t gw[2] = {odd ? g4.y : g4.x, odd ? g4.w : g4.z};
-			const uint32_t uw[2] = {odd ? u4.y : u4.x, odd ? u4.w : u4.z};
+			const uint32_t gw[2] = {stg[gi * 16 + 4 * j], stg[gi * 16 + 4 * j + 2]};
+			const uint32_t uw[2] = {stu[gi * 16 + 4 * j], stu[gi * 16 + 4 * j + 2]};
 #pragma unroll
 			for (int h = 0; h < 2; ++h) {
 				const float2 raw = make_float2(__uint_as_float(__byte_perm(gw[h] ^ 0x80808080u, 0x4B000000u, sel)),
