@@ -34,6 +34,31 @@ __device__ __forceinline__ float head_rms_scale(float ss, float eps)
 	return (r >= 1.17549435e-38f && r < 8.50705917e37f) ? rcp_nr_ftz(r) : M::rcp(r);
 }
 
+// reduce_chains_4x8 of four heads at once.  The butterfly pairs lanes at
+// distance 8, 16, 4, 1, 2 as reduce_chains_4x8 does, but after the first
+// step a lane keeps the partial sums of only two heads (bit 3 of the lane
+// picks which two) and after the second of one (bit 4), so one shuffle moves
+// what the partner needs instead of four.  Each head's total is the same
+// pairwise tree of the same values as reduce_chains_4x8 gives (fp32 addition
+// is commutative), so it is bit-identical; head h's total lands in the lanes
+// with bit 3 = h >> 1 and bit 4 = h & 1.
+__device__ __forceinline__ float reduce_chains_4x8_quad(const float (&a)[4], int lane)
+{
+	using M = F<true>;
+	const bool b3 = (lane & 8) != 0, b4 = (lane & 16) != 0;
+	// distance 8: keep heads {0, 1} (bit 3 clear) or {2, 3}, send the other pair
+	const float r0 = __shfl_xor_sync(kFullMask, b3 ? a[0] : a[2], 8);
+	const float r1 = __shfl_xor_sync(kFullMask, b3 ? a[1] : a[3], 8);
+	const float s0 = M::add(b3 ? a[2] : a[0], r0);
+	const float s1 = M::add(b3 ? a[3] : a[1], r1);
+	// distance 16: keep the first (bit 4 clear) or the second of the pair
+	const float r = __shfl_xor_sync(kFullMask, b4 ? s0 : s1, 16);
+	float t = M::add(b4 ? s1 : s0, r);
+	t = M::add(t, __shfl_xor_sync(kFullMask, t, 4));
+	t = M::add(t, __shfl_xor_sync(kFullMask, t, 1));
+	return M::add(t, __shfl_xor_sync(kFullMask, t, 2));
+}
+
 struct RopeArgs {
 	float *q;
 	float *k;
@@ -93,14 +118,38 @@ __global__ void __launch_bounds__(kBlock) k_rope_rows(RopeArgs p)
 				for (int k = 0; k < V; ++k)
 					x[h][k] = ld_stream(base + h * D + 32 * k);
 			}
+		// per-head scales: four full heads share one butterfly and one scale
+		// computation per lane (the lanes of class h hold head h's), else
+		// one butterfly per head
+		float hs[CH];
+		if (CH == 4 && nh == 4) {
+			float acc[4];
+#pragma unroll
+			for (int h = 0; h < 4; ++h) {
+				acc[h] = 0.0f;
+#pragma unroll
+				for (int k = 0; k < V; ++k)
+					acc[h] = M::fma(x[h][k], x[h][k], acc[h]);
+			}
+			const float mine = head_rms_scale<D>(reduce_chains_4x8_quad(acc, lane), p.eps);
+#pragma unroll
+			for (int h = 0; h < 4; ++h) // head h's lanes: 8 * (h >> 1) + 16 * (h & 1)
+				hs[h] = __shfl_sync(kFullMask, mine, ((h >> 1) << 3) | ((h & 1) << 4));
+		} else {
+#pragma unroll
+			for (int h = 0; h < CH; ++h)
+				if (h < nh) {
+					float acc = 0.0f;
+#pragma unroll
+					for (int k = 0; k < V; ++k)
+						acc = M::fma(x[h][k], x[h][k], acc);
+					hs[h] = head_rms_scale<D>(reduce_chains_4x8<true>(acc), p.eps);
+				}
+		}
 #pragma unroll
 		for (int h = 0; h < CH; ++h)
 			if (h < nh) {
-				float acc = 0.0f;
-#pragma unroll
-				for (int k = 0; k < V; ++k)
-					acc = M::fma(x[h][k], x[h][k], acc);
-				const float scale = head_rms_scale<D>(reduce_chains_4x8<true>(acc), p.eps);
+				const float scale = hs[h];
 				float *hb = base + h * D;
 				if (pos == 0) {
 #pragma unroll
