@@ -16,7 +16,6 @@ constexpr int kBlock = 256;
 // four CTAs per SM (at most 64 registers a thread): 4096 rows of one warp each
 // fit in one wave on 148 SMs, with no half-empty second wave
 constexpr int kMinBlocks = 4;
-constexpr int kWarpsPerBlock = kBlock / 32;
 
 // --- A1  RMSNorm rows (rmsnorm_kernel.inc:12-75), caller's MXCSR: no FTZ ---
 // Two passes over the row in chunks of C slots per lane: pass 1 accumulates
@@ -25,15 +24,15 @@ constexpr int kWarpsPerBlock = kBlock / 32;
 // guards, and the latency between chunks is covered by the four resident CTAs
 // per SM (a register prefetch buffer costs a move per element and registers
 // that would lower residency).
-template <int C, int MINB = kMinBlocks>
-__global__ void __launch_bounds__(kBlock, MINB) k_rmsnorm_rows(float *o, const float *x, const float *__restrict__ w, int64_t rows, int n, float eps)
+template <int C, int MINB = kMinBlocks, int BLOCK = kBlock>
+__global__ void __launch_bounds__(BLOCK, MINB) k_rmsnorm_rows(float *o, const float *x, const float *__restrict__ w, int64_t rows, int n, float eps)
 {
 	using M = F<false>;
 	const int lane = threadIdx.x & 31;
-	const int64_t nwarps = ((int64_t)gridDim.x * kBlock) >> 5;
+	const int64_t nwarps = ((int64_t)gridDim.x * BLOCK) >> 5;
 	const int vpl = n >> 5;
 	const float nf = (float)n;
-	for (int64_t row = ((int64_t)blockIdx.x * kBlock + threadIdx.x) >> 5; row < rows; row += nwarps) {
+	for (int64_t row = ((int64_t)blockIdx.x * BLOCK + threadIdx.x) >> 5; row < rows; row += nwarps) {
 		const float *xr = x + row * n + lane;
 		float *orow = o + row * n + lane;
 		float acc = 0.0f;
@@ -72,17 +71,17 @@ __global__ void __launch_bounds__(kBlock, MINB) k_rmsnorm_rows(float *o, const f
 // groups from block L on; chain lane l then covers e = 8L + l + 32k.  Pass 1
 // writes the new residual as it goes; pass 2 re-reads it (L2) for the output;
 // both in unguarded chunks as in k_rmsnorm_rows.
-template <int C, int MINB = kMinBlocks>
-__global__ void __launch_bounds__(kBlock, MINB) k_fused_add_rmsnorm_rows(float *o, float *res, const float *add, const float *__restrict__ w, int64_t rows, int n, float eps)
+template <int C, int MINB = kMinBlocks, int BLOCK = kBlock>
+__global__ void __launch_bounds__(BLOCK, MINB) k_fused_add_rmsnorm_rows(float *o, float *res, const float *add, const float *__restrict__ w, int64_t rows, int n, float eps)
 {
 	using M = F<false>;
 	const int lane = threadIdx.x & 31;
-	const int64_t nwarps = ((int64_t)gridDim.x * kBlock) >> 5;
+	const int64_t nwarps = ((int64_t)gridDim.x * BLOCK) >> 5;
 	const int left = (n >> 3) & 3;
 	const int off = 8 * left;
 	const int vpl = (n - off) >> 5;
 	const float nf = (float)n;
-	for (int64_t row = ((int64_t)blockIdx.x * kBlock + threadIdx.x) >> 5; row < rows; row += nwarps) {
+	for (int64_t row = ((int64_t)blockIdx.x * BLOCK + threadIdx.x) >> 5; row < rows; row += nwarps) {
 		float *rr = res + row * n;
 		const float *ar = add + row * n;
 		float *orow = o + row * n;
@@ -145,21 +144,27 @@ constexpr int kAddChunk = 16;
 // occupancy cap puts a 2048-wide row's loads in flight at once.  Same
 // arithmetic in the same order, so results are identical.
 constexpr int64_t kFewRows = 1024;
+// Up to about one row per SM, a CTA of one warp per row: the rows spread over
+// as many SMs (each SM's load pipeline serves one row) instead of eight to
+// a CTA on a few SMs.
+constexpr int64_t kSpreadRows = 256;
 constexpr int kRmsChunkFew = 64;
 constexpr int kAddChunkFew = 32;
 
-// `oversubscribe` x the resident CTAs, at most one warp per row.
+// `oversubscribe` x the resident CTAs of `block` threads, at most one warp
+// per row.
 template <typename Kernel, typename... Args>
-int launch_rows(Kernel kernel, const char *what, int64_t rows, int oversubscribe, void *stream, Args... args)
+int launch_rows(Kernel kernel, const char *what, int64_t rows, int oversubscribe, int block, void *stream, Args... args)
 {
 	DeviceInfo dev;
 	int rc = current_device(&dev);
 	if (rc != V7G_OK)
 		return rc;
-	const int64_t want = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;
-	const int resident = resident_grid((const void *)kernel, kBlock, 0, want, dev);
+	const int warps = block / 32;
+	const int64_t want = (rows + warps - 1) / warps;
+	const int resident = resident_grid((const void *)kernel, block, 0, want, dev);
 	const int grid = (int)(want < (int64_t)oversubscribe * resident ? want : (int64_t)oversubscribe * resident);
-	kernel<<<grid, kBlock, 0, (cudaStream_t)stream>>>(args...);
+	kernel<<<grid, block, 0, (cudaStream_t)stream>>>(args...);
 	return check_launch(what);
 }
 
@@ -182,9 +187,11 @@ int v7g_rmsnorm_rows(float *o, const float *x, const float *w, int64_t rows, int
 		return clear_error();
 	if (!o || !x || !w)
 		return set_error(V7G_ERR_ARG, "v7g_rmsnorm_rows: NULL pointer");
+	if (rows <= kSpreadRows)
+		return launch_rows(k_rmsnorm_rows<kRmsChunkFew, 1, 32>, "v7g_rmsnorm_rows", rows, 1, 32, stream, o, x, w, rows, n, eps);
 	if (rows <= kFewRows)
-		return launch_rows(k_rmsnorm_rows<kRmsChunkFew, 1>, "v7g_rmsnorm_rows", rows, 1, stream, o, x, w, rows, n, eps);
-	return launch_rows(k_rmsnorm_rows<kRmsChunk>, "v7g_rmsnorm_rows", rows, 1, stream, o, x, w, rows, n, eps);
+		return launch_rows(k_rmsnorm_rows<kRmsChunkFew, 1>, "v7g_rmsnorm_rows", rows, 1, kBlock, stream, o, x, w, rows, n, eps);
+	return launch_rows(k_rmsnorm_rows<kRmsChunk>, "v7g_rmsnorm_rows", rows, 1, kBlock, stream, o, x, w, rows, n, eps);
 }
 
 int v7g_fused_add_rmsnorm_rows(float *o, float *residual, const float *add, const float *w, int64_t rows, int n, float eps, void *stream)
@@ -197,9 +204,13 @@ int v7g_fused_add_rmsnorm_rows(float *o, float *residual, const float *add, cons
 		return clear_error();
 	if (!o || !residual || !add || !w)
 		return set_error(V7G_ERR_ARG, "v7g_fused_add_rmsnorm_rows: NULL pointer");
+	if (rows <= kSpreadRows)
+		return launch_rows(k_fused_add_rmsnorm_rows<kAddChunkFew, 1, 32>, "v7g_fused_add_rmsnorm_rows", rows, 4, 32, stream, o, residual, add, w, rows, n,
+		                   eps);
 	if (rows <= kFewRows)
-		return launch_rows(k_fused_add_rmsnorm_rows<kAddChunkFew, 1>, "v7g_fused_add_rmsnorm_rows", rows, 4, stream, o, residual, add, w, rows, n, eps);
-	return launch_rows(k_fused_add_rmsnorm_rows<kAddChunk>, "v7g_fused_add_rmsnorm_rows", rows, 4, stream, o, residual, add, w, rows, n, eps);
+		return launch_rows(k_fused_add_rmsnorm_rows<kAddChunkFew, 1>, "v7g_fused_add_rmsnorm_rows", rows, 4, kBlock, stream, o, residual, add, w, rows,
+		                   n, eps);
+	return launch_rows(k_fused_add_rmsnorm_rows<kAddChunk>, "v7g_fused_add_rmsnorm_rows", rows, 4, kBlock, stream, o, residual, add, w, rows, n, eps);
 }
 
 } // extern "C"
