@@ -36,6 +36,21 @@ __global__ void __launch_bounds__(BLOCK, MINB) k_rmsnorm_rows(float *o, const fl
 		const float *xr = x + row * n + lane;
 		float *orow = o + row * n + lane;
 		float acc = 0.0f;
+		if (vpl == C) {
+			// the whole row is one chunk: keep it in registers for the output
+			float v[C];
+#pragma unroll
+			for (int k = 0; k < C; ++k)
+				v[k] = ld_stream(xr + 32 * k);
+#pragma unroll
+			for (int k = 0; k < C; ++k)
+				acc = M::fma(v[k], v[k], acc);
+			const float scale = rms_scale<false>(reduce_chains_4x8<false>(acc), nf, eps);
+#pragma unroll
+			for (int k = 0; k < C; ++k)
+				st_stream(orow + 32 * k, M::mul(M::mul(v[k], scale), __ldg(w + lane + 32 * k)));
+			continue;
+		}
 		int k0 = 0;
 		for (; k0 + C <= vpl; k0 += C) {
 			float v[C];
