@@ -17,12 +17,18 @@
 //
 // The lane accumulators are eight independent fp32 chains per output row, so
 // the GPU runs one chain per thread: eight threads per row, four rows per
-// warp.  A thread streams its row's bytes 4l..4l+3 and 32+4l..32+4l+3 of every
-// group (two 4-byte loads per matrix; the row's eight threads read both
-// 32-byte sectors of the group whole) and its dp4a dot; the activation codes
-// and scales are staged once per CTA in shared memory.  Loads for kUnroll
-// groups are issued before their arithmetic.  The weights are read exactly
-// once: HBM-bound at d x n x (1 + 4/64) bytes per matrix.
+// warp; lane l's dot uses the row's bytes 4l..4l+3 and 32+4l..32+4l+3 of
+// every group (dp4a).  The weights are read exactly once: HBM-bound at
+// d x n x (1 + 4/64) bytes per matrix.  Three kernels share this arithmetic:
+//   k_q8_gemv_stream  weights and scales 16-byte aligned, groups % 4 == 0:
+//                     persistent CTAs, producer warps stream activation,
+//                     scales and weight chunks by bulk copy into shared
+//                     memory rings (the decode-size fast path);
+//   k_q8_gemv_tma     weights aligned but scales not: one producer warp, a
+//                     per-CTA ring, the scales read by the consumers;
+//   k_q8_gemv         anything else: direct 4-byte loads, kUnroll groups
+//                     issued before their arithmetic.
+// The entry points pick the first that applies.
 #include <algorithm>
 
 #include "arith.cuh"
