@@ -487,8 +487,9 @@ __global__ void __launch_bounds__(R * kLanes + 32, 2) k_q8_gemv_tma(GemvArgs p, 
 
 // ---- streaming Q8 GEMV -------------------------------------------------------
 // The arithmetic of k_q8_gemv once more, organised for HBM: a CTA (two per
-// SM) walks the row blocks rb = blockIdx.x, + gridDim.x, ... and its producer
-// warp streams, in order and without draining between row blocks:
+// SM, or one with twice the ring when there are no more row blocks than SMs)
+// walks the row blocks rb = blockIdx.x, + gridDim.x, ... and its P producer
+// warps stream, in order and without draining between row blocks:
 //   once      the activation (codes and scales, or the fp32 row) -- ahead of
 //             every weight byte, so the consumers' prologue is one latency;
 //   per block its weight scales, one bulk copy per matrix (the block's rows
