@@ -14,7 +14,9 @@ Reported (one JSON line from rank 0):
              once) / max-over-ranks device time, inputs resident in HBM
   e2e        the same metric through the public API with host buffers: every
              step copies the shard's gate/up from pinned host memory and reads
-             codes/scales back (pipelined in row chunks over three streams)
+             codes/scales back (pipelined in row chunks over three streams);
+             e2e.link times the same copies alone, the step's floor on the
+             host link
   roofline   the kernel's achieved GB/s against the measured HBM copy peak
   cpu_baseline  the oracle port on the host cores, bounded sample (N=1 only)
   kernels    the other BASELINE configs (C1-C4) and the next rows (add_inplace,
@@ -351,10 +353,45 @@ def run_e2e(args, v7g, dev, g, u, codes, scales, rows, world):
     wall = (time.perf_counter() - t0) * 1e3
     t_max = max_over_ranks(ms, world)
     value = c5_bytes(C5_ROWS) * steps / (t_max * 1e-3) / 1e9
+    link = host_link(dev, (hg, hu), (g, u), (hc, hs), (codes, scales), world)
+    floor_ms = max(link["h2d_ms"], link["d2h_ms"])
+    link["floor_ms_per_step"] = round(floor_ms, 4)
+    link["frac"] = round(floor_ms / (t_max / steps), 4)
     return {"value": round(value, 2), "unit": "GB/s", "steps": steps,
             "h2d_bytes_per_step": int(C5_ROWS * C5_N * 8), "d2h_bytes_per_step": int(C5_ROWS * (C5_N + C5_N // GROUP * 4)),
             "ms_per_step": round(t_max / steps, 4), "wall_ms_per_step_rank0": round(wall / steps, 4),
-            "path": f"pinned host -> v7g_swiglu_q8_rows -> pinned host, {nchunks} row chunks on 3 streams"}
+            "path": f"pinned host -> v7g_swiglu_q8_rows -> pinned host, {nchunks} row chunks on 3 streams",
+            "link": link}
+
+
+def host_link(dev, h_in, d_in, h_out, d_out, world, reps: int = 3) -> dict:
+    """The host link alone: one step's input copies (pinned host -> device)
+    and, separately, its output copies (device -> pinned host), each timed
+    with CUDA events on one stream, max over ranks.  The slower direction is
+    the floor of the end-to-end step, whose copies overlap each other and
+    the kernel."""
+    s = torch.cuda.Stream(device=dev)
+    out = {}
+    for name, src, dst in (("h2d", h_in, d_in), ("d2h", d_out, h_out)):
+        nbytes = sum(t.numel() * t.element_size() for t in src)
+        with torch.cuda.stream(s):
+            for a, b in zip(src, dst):
+                b.copy_(a, non_blocking=True)
+        s.synchronize()
+        barrier(world)
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(s)
+        with torch.cuda.stream(s):
+            for _ in range(reps):
+                for a, b in zip(src, dst):
+                    b.copy_(a, non_blocking=True)
+        end.record(s)
+        s.synchronize()
+        ms = max_over_ranks(start.elapsed_time(end), world) / reps
+        out[f"{name}_ms"] = round(ms, 4)
+        out[f"{name}_gbs"] = round(nbytes / (ms * 1e-3) / 1e9, 2)
+    return out
 
 
 def kernel_table(v7g, dev, stream, peak) -> dict:
