@@ -395,26 +395,59 @@ def host_link(dev, h_in, d_in, h_out, d_out, world, reps: int = 3) -> dict:
 
 
 def kernel_table(v7g, dev, stream, peak) -> dict:
-    """Device-timed GB/s of the other BASELINE configs on one GPU, median of 50
-    launches.  Configs whose inputs fit in L2 (C1, C2, C3 and the add,
-    RMSNorm->Q8 and RoPE-only rows) flush L2 before every launch."""
+    """Device-timed GB/s of the other BASELINE configs on one GPU.
+
+    us        mean of 50 single launches, each behind an L2 flush for the
+              configs whose inputs fit in L2 (C1, C2, C3 and the add,
+              RMSNorm->Q8, RoPE-only and GEMV rows).  The event clock ticks
+              in steps of about 2 us on this part, so the mean (the launch
+              starts at a random phase of the tick) is the estimate;
+              us_median is kept beside it.
+    us_b2b    launches back to back, cycling over `b2b_sets` copies of the
+              inputs whose total is over twice L2, so that no launch finds
+              its inputs in L2: the per-launch cost in a stream of launches,
+              as an inference engine issues them.  C1 (1 MB) has one set: L2
+              resident, labelled as such."""
     out = {}
     # 512 MB written + 512 MB read (each > 4x L2) before every flushed launch
     flush = (torch.zeros(128 * 2**20, device=dev), torch.zeros(1024, 128 * 1024, device=dev),
              torch.empty(128 * 1024, device=dev))
     K = 50
 
-    def rec(name, fn, nbytes, rows, flushed, note=""):
+    def sets_for(set_bytes: int) -> int:
+        return max(2, -(-2 * L2_BYTES // set_bytes) + 1)
+
+    def b2b(fns) -> float:
+        n = max(30, 3 * len(fns))
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            for f in fns:
+                f()
+            torch.cuda._sleep(4_000_000)  # every launch queued before the first runs
+            start.record(stream)
+            for i in range(n):
+                fns[i % len(fns)]()
+            end.record(stream)
+        stream.synchronize()
+        return start.elapsed_time(end) / n
+
+    def rec(name, fns, nbytes, rows, flushed, note=""):
+        fns = fns if isinstance(fns, list) else [fns]
         torch.cuda.synchronize()  # inputs were written on the default stream
         with torch.cuda.stream(stream):
             for _ in range(3):
-                fn()
+                fns[0]()
         stream.synchronize()
-        _, per = time_launches(fn, K, stream, flush if flushed else None)
-        ms = statistics.median(per)
+        _, per = time_launches(fns[0], K, stream, flush if flushed else None)
+        ms = statistics.mean(per)
         gbs = nbytes / (ms * 1e-3) / 1e9
+        ms_b = b2b(fns)
+        gbs_b = nbytes / (ms_b * 1e-3) / 1e9
         out[name] = {"gbs": round(gbs, 1), "frac": round(gbs / peak, 4), "us": round(ms * 1e3, 2),
-                     "rows_per_s": round(rows / (ms * 1e-3), 1), "bytes": nbytes, "l2_flushed": flushed}
+                     "us_median": round(statistics.median(per) * 1e3, 2),
+                     "rows_per_s": round(rows / (ms * 1e-3), 1), "bytes": nbytes, "l2_flushed": flushed,
+                     "us_b2b": round(ms_b * 1e3, 2), "gbs_b2b": round(gbs_b, 1), "frac_b2b": round(gbs_b / peak, 4),
+                     "b2b_sets": len(fns)}
         if note:
             out[name]["note"] = note
 
@@ -422,32 +455,42 @@ def kernel_table(v7g, dev, stream, peak) -> dict:
         t = torch.empty(*shape, device=dev)
         return v7g.fill_normal(t.view(-1, shape[-1]), seed=seed, mean=mean, std=std)
 
+    def copies(n, *ts):
+        return [tuple(ts)] + [tuple(t.clone() for t in ts) for _ in range(n - 1)]
+
     # C1 RMSNorm x[64, 2048]
     x = fill((64, 2048), 1, 0.0, 1.0)
     w = fill((1, 2048), 2, 1.0, 0.1)[0]
     o = torch.empty_like(x)
     rec("c1_rmsnorm_64x2048", lambda: v7g.rmsnorm_rows(o, x, w, 1e-6, stream=stream), 64 * 2048 * 8 + 2048 * 4, 64, True,
-        "launch/latency-bound: 1 MiB of traffic")
+        "launch/latency-bound: 1 MiB of traffic; us_b2b is L2-resident")
     # C2 fused add + RMSNorm [4096, 2048]
     r = fill((4096, 2048), 3, 0.0, 1.0)
     d = fill((4096, 2048), 4, 0.0, 0.5)
-    o2 = torch.empty_like(r)
-    rec("c2_fused_add_rmsnorm_4096x2048", lambda: v7g.fused_add_rmsnorm_rows(o2, r, d, w, 1e-6, stream=stream),
-        4096 * 2048 * 16 + 2048 * 4, 4096, True)
-    rec("add_inplace_4096x2048", lambda: v7g.add_inplace(r, d, stream=stream), 4096 * 2048 * 12, 4096, True)
+    c2b = 4096 * 2048 * 16 + 2048 * 4
+    sets = copies(sets_for(c2b), r, d, torch.empty_like(r))
+    rec("c2_fused_add_rmsnorm_4096x2048",
+        [lambda t=t: v7g.fused_add_rmsnorm_rows(t[2], t[0], t[1], w, 1e-6, stream=stream) for t in sets],
+        c2b, 4096, True)
+    rec("add_inplace_4096x2048", [lambda t=t: v7g.add_inplace(t[0], t[1], stream=stream) for t in sets],
+        4096 * 2048 * 12, 4096, True)
+    del sets
     # C3 RMSNorm + RoPE Q[8192,16,128] K[8192,8,128]
     q = fill((8192, 16 * 128), 6, 0.0, 1.0).view(8192, 16, 128)
     k = fill((8192, 8 * 128), 7, 0.0, 1.0).view(8192, 8, 128)
     wq = fill((1, 128), 8, 1.0, 0.1)[0]
     wk = fill((1, 128), 9, 1.0, 0.1)[0]
     cos, sin = v7g.rope_tables(8192, 64, 1e6, device=dev)
+    c3b = 8192 * 24 * 128 * 8 + 8192 * 64 * 8
+    sets = copies(sets_for(c3b), q, k, cos, sin)
     # Q + K are 100.7 MB, under the 126 MB L2: flushed
-    rec("c3_rmsnorm_rope_8192x(16+8)x128", lambda: v7g.rmsnorm_rope_rows(q, k, wq, wk, cos, sin, 0, 1e-6, stream=stream),
-        8192 * 24 * 128 * 8 + 8192 * 64 * 8 + 2 * 128 * 4, 8192, True)
+    rec("c3_rmsnorm_rope_8192x(16+8)x128",
+        [lambda t=t: v7g.rmsnorm_rope_rows(t[0], t[1], wq, wk, t[2], t[3], 0, 1e-6, stream=stream) for t in sets],
+        c3b + 2 * 128 * 4, 8192, True)
     # RoPE without the norm at the C3 geometry
-    rec("rope_only_8192x(16+8)x128", lambda: v7g.rope_only_rows(q, k, cos, sin, 0, stream=stream),
-        8192 * 24 * 128 * 8 + 8192 * 64 * 8, 8192, True)
-    del q, k
+    rec("rope_only_8192x(16+8)x128", [lambda t=t: v7g.rope_only_rows(t[0], t[1], t[2], t[3], 0, stream=stream) for t in sets],
+        c3b, 8192, True)
+    del q, k, sets
     # the reference's internal tables: 131072 positions x 64 pairs, cos + sin written
     tc = torch.empty(131072, 64, device=dev)
     ts = torch.empty_like(tc)
@@ -460,31 +503,38 @@ def kernel_table(v7g, dev, stream, peak) -> dict:
     gg = fill((4096, 8192), 10, 0.0, 2.0)
     uu = fill((4096, 8192), 11, 0.0, 2.0)
     oo = torch.empty_like(gg)
-    rec("c4_swiglu_4096x8192", lambda: v7g.swiglu(oo, gg, uu, stream=stream), 4096 * 8192 * 12, 4096, False)
+    sets = copies(2, gg, uu, oo)  # 403 MB per set: no launch finds its inputs in L2
+    rec("c4_swiglu_4096x8192", [lambda t=t: v7g.swiglu(t[2], t[0], t[1], stream=stream) for t in sets],
+        4096 * 8192 * 12, 4096, False)
+    del gg, uu, oo, sets
     # Q8-weight GEMVs (decode, batch 1) at model shapes; weights under L2 size: flushed
     for n, d in ((2048, 8192), (4096, 12288)):
         xq, xs, gq, gs, uq, us = gemv_inputs(dev, n, d)
         y = torch.empty(1, d, device=dev)
-        rec(f"swiglu_q8_gemv_{n}x{d}", lambda: v7g.swiglu_q8_gemv(y, xq, xs, gq, gs, uq, us, stream=stream),
-            2 * d * (n + n // 16) + n + n // 16 + 4 * d, d, True)
+        nb = 2 * d * (n + n // 16) + n + n // 16 + 4 * d
+        sets = copies(sets_for(nb), gq, gs, uq, us)
+        rec(f"swiglu_q8_gemv_{n}x{d}",
+            [lambda t=t: v7g.swiglu_q8_gemv(y, xq, xs, t[0], t[1], t[2], t[3], stream=stream) for t in sets], nb, d, True)
         if n == 2048:
             xf = fill((1, n), 14, 0.0, 1.0)
-            rec(f"swiglu_f32q8_gemv_{n}x{d}", lambda: v7g.swiglu_f32q8_gemv(y, xf, gq, gs, uq, us, stream=stream),
+            rec(f"swiglu_f32q8_gemv_{n}x{d}",
+                [lambda t=t: v7g.swiglu_f32q8_gemv(y, xf, t[0], t[1], t[2], t[3], stream=stream) for t in sets],
                 2 * d * (n + n // 16) + 4 * n + 4 * d, d, True)
-        del gq, gs, uq, us
+        del gq, gs, uq, us, sets
     xq, xs, wq, ws, _, _ = gemv_inputs(dev, 8192, 2048, both=False)
     y = torch.empty(1, 2048, device=dev)
-    rec("q8_gemv_8192x2048", lambda: v7g.q8_gemv(y, xq, xs, wq, ws, stream=stream),
-        2048 * (8192 + 8192 // 16) + 8192 + 8192 // 16 + 4 * 2048, 2048, True)
+    nb = 2048 * (8192 + 8192 // 16) + 8192 + 8192 // 16 + 4 * 2048
+    sets = copies(sets_for(nb), wq, ws)
+    rec("q8_gemv_8192x2048", [lambda t=t: v7g.q8_gemv(y, xq, xs, t[0], t[1], stream=stream) for t in sets], nb, 2048, True)
     xf = fill((1, 8192), 15, 0.0, 1.0)
-    rec("q8_fused_gemv_8192x2048", lambda: v7g.q8_fused_gemv(y, xf, wq, ws, stream=stream),
+    rec("q8_fused_gemv_8192x2048", [lambda t=t: v7g.q8_fused_gemv(y, xf, t[0], t[1], stream=stream) for t in sets],
         2048 * (8192 + 8192 // 16) + 4 * 8192 + 4 * 2048, 2048, True)
-    del wq, ws
+    del wq, ws, sets
     # RMSNorm -> Q8 at the C2 shape
-    codes = torch.empty(4096, 2048, dtype=torch.int8, device=dev)
-    sc = torch.empty(4096, 32, device=dev)
-    rec("rmsnorm_quantize_4096x2048", lambda: v7g.rmsnorm_quantize_rows(codes, sc, r, w, 1e-6, stream=stream),
-        4096 * (2048 * 5 + 32 * 4) + 2048 * 4, 4096, True)
+    nb = 4096 * (2048 * 5 + 32 * 4) + 2048 * 4
+    sets = copies(sets_for(nb), r, torch.empty(4096, 2048, dtype=torch.int8, device=dev), torch.empty(4096, 32, device=dev))
+    rec("rmsnorm_quantize_4096x2048",
+        [lambda t=t: v7g.rmsnorm_quantize_rows(t[1], t[2], t[0], w, 1e-6, stream=stream) for t in sets], nb, 4096, True)
     return out
 
 

@@ -92,21 +92,27 @@ __device__ __forceinline__ void q8_scale_fast(float wmax, float &scale, float &r
 
 // Codes of four values whose products p = h * recip satisfy |p| < 127.5 (a
 // group with neither NaN nor infinity, quantised with its own scale: |p| is
-// at most 127 (1 + 3 * 2^-24)): the rounded product converted to the nearest
-// integer, ties to even (cvt.rni, CVTPS2DQ's rounding), keeping the low byte.
-// For such p the reference's saturating packs and -127 floor change nothing,
-// so no clamp or range test is needed.  The conversion takes the product as
-// rounded by its own multiply: no fused multiply-add can skip that rounding
-// (a product added straight to a 1.5 * 2^23 rounding constant was fused by
-// the compiler in some kernels, which moved exact ties).  Checked against
-// q8_code_bits over every such p, and on products next to a tie under
-// non-trivial reciprocals, by v7g_selftest_arith.
+// at most 127 (1 + 3 * 2^-24)): the rounded product plus 1.5 * 2^23, whose
+// low byte is then the product rounded to the nearest integer, ties to even
+// (CVTPS2DQ's rounding; the constant is even, so the adder's tie rule is the
+// conversion's).  For such p the reference's saturating packs and -127 floor
+// change nothing, so no clamp or range test is needed.  The product and the
+// sum are single mul.rn / add.rn instructions: PTX does not contract an
+// instruction with an explicit rounding modifier into a fused multiply-add,
+// which would skip the product's rounding and move exact ties (the packed
+// intrinsics were fused that way in some kernels).  Two full-rate
+// instructions per code instead of a multiply and a float-to-int conversion
+// (16 results per clock per SM in CUDA's throughput table, against 128 for
+// a multiply or an add).
+// Checked against q8_code_bits over every such p, and on products next to a
+// tie under non-trivial reciprocals, by v7g_selftest_arith.
 __device__ __forceinline__ uint32_t q8_codes4_small(float4 h, float recip)
 {
-	const float2 p01 = mul2(make_float2(h.x, h.y), splat2(recip));
-	const float2 p23 = mul2(make_float2(h.z, h.w), splat2(recip));
-	return pack4_low_bytes((uint32_t)__float2int_rn(p01.x), (uint32_t)__float2int_rn(p01.y), (uint32_t)__float2int_rn(p23.x),
-	                       (uint32_t)__float2int_rn(p23.y));
+	using M = F<true>;
+	return pack4_low_bytes(__float_as_uint(M::add(M::mul(h.x, recip), kRoundMagic)),
+	                       __float_as_uint(M::add(M::mul(h.y, recip), kRoundMagic)),
+	                       __float_as_uint(M::add(M::mul(h.z, recip), kRoundMagic)),
+	                       __float_as_uint(M::add(M::mul(h.w, recip), kRoundMagic)));
 }
 
 // q8_codes4 with pair arithmetic.
