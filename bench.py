@@ -75,7 +75,7 @@ class ClockSampler:
                "hw_power_brake_slowdown": 0x80}
 
     def __init__(self, device_index: int, period_s: float = 0.005):
-        self.samples: list[tuple[int, int, int]] = []
+        self.samples: list[tuple] = []  # (sm MHz, reasons, util %, memory MHz, board W, GPU C)
         self.period = period_s
         self.ok = False
         try:
@@ -86,6 +86,7 @@ class ClockSampler:
             self.h = pynvml.nvmlDeviceGetHandleByUUID(uuid.encode())
             self.nvml = pynvml
             self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.mem_max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_MEM)
             self.ok = True
         except Exception as e:  # pragma: no cover - reported in the JSON line
             self.err = repr(e)
@@ -99,7 +100,10 @@ class ClockSampler:
                 sm = n.nvmlDeviceGetClockInfo(self.h, n.NVML_CLOCK_SM)
                 reasons = n.nvmlDeviceGetCurrentClocksEventReasons(self.h)
                 util = n.nvmlDeviceGetUtilizationRates(self.h).gpu
-                self.samples.append((sm, reasons, util))
+                mem = n.nvmlDeviceGetClockInfo(self.h, n.NVML_CLOCK_MEM)
+                power = n.nvmlDeviceGetPowerUsage(self.h) / 1000.0
+                temp = n.nvmlDeviceGetTemperature(self.h, n.NVML_TEMPERATURE_GPU)
+                self.samples.append((sm, reasons, util, mem, power, temp))
             except Exception:
                 pass
             if self._stop.wait(self.period):
@@ -120,9 +124,12 @@ class ClockSampler:
         if not self.ok:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": getattr(self, "err", "nvml unavailable")}
         loaded = [s for s in self.samples if s[2] > 0] or self.samples
-        reasons = sorted({name for _, r, _ in loaded for name, bit in self.REASONS.items() if r & bit})
-        return {"sm_mhz": statistics.median(s[0] for s in loaded) if loaded else None, "sm_max_mhz": self.max_mhz,
-                "reasons": reasons, "samples": len(loaded), "source": "NVML, sampled every 5 ms in the timed region"}
+        reasons = sorted({name for _, r, *_ in loaded for name, bit in self.REASONS.items() if r & bit})
+        med = (lambda i: statistics.median(s[i] for s in loaded) if loaded else None)
+        return {"sm_mhz": med(0), "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(loaded),
+                "mem_mhz": med(3), "mem_max_mhz": self.mem_max_mhz, "power_w": med(4),
+                "temp_c_max": max((s[5] for s in loaded), default=None),
+                "source": "NVML, sampled every 5 ms in the timed region"}
 
 
 # ------------------------------------------------------------ distributed
@@ -284,6 +291,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
                         "+ fp32 scales [16384, 192] (one per 64-element group)",
             "rows": C5_ROWS, "n": C5_N, "rows_per_gpu": rows, "parallelism": f"row-shard x{world}, no collective",
             "bytes_per_row": c5_bytes(1), "l2": "inputs 1.61 GB > 126 MB L2: no flush needed",
+            "launch_overlap": v7g.launch_overlap(),
         },
         "roofline": {
             "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
@@ -407,7 +415,9 @@ def kernel_table(v7g, dev, stream, peak) -> dict:
               inputs whose total is over twice L2, so that no launch finds
               its inputs in L2: the per-launch cost in a stream of launches,
               as an inference engine issues them.  C1 (1 MB) has one set: L2
-              resident, labelled as such."""
+              resident, labelled as such.  Launch overlap (programmatic
+              dependent launch) is on, the library's default;
+              us_b2b_no_overlap repeats the figure with plain launches."""
     out = {}
     # 512 MB written + 512 MB read (each > 4x L2) before every flushed launch
     flush = (torch.zeros(128 * 2**20, device=dev), torch.zeros(1024, 128 * 1024, device=dev),
@@ -443,11 +453,16 @@ def kernel_table(v7g, dev, stream, peak) -> dict:
         gbs = nbytes / (ms * 1e-3) / 1e9
         ms_b = b2b(fns)
         gbs_b = nbytes / (ms_b * 1e-3) / 1e9
+        v7g.set_launch_overlap(False)
+        try:
+            ms_p = b2b(fns)
+        finally:
+            v7g.set_launch_overlap(True)
         out[name] = {"gbs": round(gbs, 1), "frac": round(gbs / peak, 4), "us": round(ms * 1e3, 2),
                      "us_median": round(statistics.median(per) * 1e3, 2),
                      "rows_per_s": round(rows / (ms * 1e-3), 1), "bytes": nbytes, "l2_flushed": flushed,
                      "us_b2b": round(ms_b * 1e3, 2), "gbs_b2b": round(gbs_b, 1), "frac_b2b": round(gbs_b / peak, 4),
-                     "b2b_sets": len(fns)}
+                     "b2b_sets": len(fns), "us_b2b_no_overlap": round(ms_p * 1e3, 2)}
         if note:
             out[name]["note"] = note
 

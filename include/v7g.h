@@ -192,6 +192,15 @@ const char *v7g_last_error(void);
 /* Number of kernels this library has launched in this process. */
 uint64_t v7g_launch_count(void);
 
+/* Launch overlap (programmatic dependent launch), on by default: each kernel
+   is launched so that it may be scheduled while the kernel ahead of it in the
+   stream drains, and waits on the device for that kernel's completion before
+   its first memory access.  Stream order is kept either way; off gives plain
+   launches.  Process-wide; takes effect at the next launch.  No reference
+   counterpart (the reference's kernels are CPU calls). */
+void v7g_set_launch_overlap(int on);
+int v7g_get_launch_overlap(void);
+
 /* Exhaustive device self-check of the library's fast arithmetic (the
    Markstein-corrected reciprocal, the fast Q8 scale, the packed-pair SiLU and
    Q8 code paths) against the plain IEEE instructions, over every input each can

@@ -90,6 +90,18 @@ def test_rms_eps_global(native_lib_path):
     v7g.set_rms_eps(old)
 
 
+def test_launch_overlap_switch(native_lib_path):
+    import v7multiplikator_b200 as v7g
+    assert v7g.launch_overlap()  # on by default
+    try:
+        v7g.set_launch_overlap(False)
+        assert not v7g.launch_overlap()
+        assert v7g.lib().v7g_get_launch_overlap() == 0
+    finally:
+        v7g.set_launch_overlap(True)
+    assert v7g.launch_overlap()
+
+
 @pytest.fixture(scope="module")
 def abi_probe(tmp_path_factory):
     exe = tmp_path_factory.mktemp("probe") / "abi_probe"

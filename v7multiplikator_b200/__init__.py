@@ -23,6 +23,7 @@ from .ops import (  # noqa: F401
     fused_add_rmsnorm_rows,
     get_rms_eps,
     launch_count,
+    launch_overlap,
     lib,
     pipeline_timeouts,
     q8_fused_gemv,
@@ -37,6 +38,7 @@ from .ops import (  # noqa: F401
     rope_only_rows,
     rope_tables,
     selftest_arith,
+    set_launch_overlap,
     set_rms_eps,
     swiglu,
     swiglu_f32q8_gemv,

@@ -1,6 +1,7 @@
 // add.cu -- x += y (v7s_add_inplace, add_kernel.inc:26-49) and the
 // deterministic synthetic-input generator.
 #include "internal.h"
+#include "launch.cuh"
 #include "reduce.cuh"
 
 namespace v7g {
@@ -11,6 +12,7 @@ constexpr int kBlock = 256;
 template <bool VEC>
 __global__ void __launch_bounds__(kBlock) k_add_inplace(float *x, const float *y, int64_t count)
 {
+	kernel_entry();
 	using M = F<false>;
 	const int64_t tid = (int64_t)blockIdx.x * kBlock + threadIdx.x;
 	const int64_t nthreads = (int64_t)gridDim.x * kBlock;
@@ -43,6 +45,7 @@ __device__ __forceinline__ uint64_t mix64(uint64_t z)
 // N(mean, std) from the counter (seed, row, col) by the Box-Muller transform.
 __global__ void __launch_bounds__(kBlock) k_fill_normal(float *dst, int64_t rows, int64_t n, int64_t row0, uint64_t seed, float mean, float std)
 {
+	kernel_entry();
 	const int64_t total = rows * n;
 	const int64_t stride = (int64_t)gridDim.x * kBlock;
 	const uint64_t key = mix64(seed ^ 0x9e3779b97f4a7c15ull);
@@ -69,8 +72,8 @@ int launch_persistent(Kernel kernel, const char *what, int64_t work_blocks, int 
 	work_blocks = work_blocks < 1 ? 1 : work_blocks;
 	const int resident = resident_grid((const void *)kernel, kBlock, 0, work_blocks, dev);
 	const int grid = (int)(work_blocks < (int64_t)resident * oversubscribe ? work_blocks : (int64_t)resident * oversubscribe);
-	kernel<<<grid, kBlock, 0, (cudaStream_t)stream>>>(args...);
-	return check_launch(what);
+	const cudaError_t launched = launch_kernel(kernel, grid, kBlock, 0, stream, args...);
+	return check_launch(what, launched);
 }
 
 } // namespace

@@ -33,6 +33,7 @@
 
 #include "arith.cuh"
 #include "internal.h"
+#include "launch.cuh"
 #include "pipeline.cuh"
 #include "q8.cuh"
 #include "q8_fast.cuh"
@@ -163,6 +164,7 @@ __device__ __noinline__ void stage_quantized(const float *x, int n, uint32_t *sq
 template <int MODE, bool FUSED>
 __global__ void __launch_bounds__(kBlock) k_q8_gemv(GemvArgs p)
 {
+	kernel_entry();
 	using M = F<true>;
 	constexpr int NM = MODE == 1 ? 2 : 1;
 	extern __shared__ __align__(128) unsigned char smem[];
@@ -354,6 +356,7 @@ __device__ __forceinline__ void chunk_f32(float (&acc)[2], const uint32_t *st, c
 template <int MODE, bool FUSED, int R>
 __global__ void __launch_bounds__(R * kLanes + 32, 2) k_q8_gemv_tma(GemvArgs p, int stages)
 {
+	kernel_entry();
 	using M = F<true>;
 	constexpr int NM = MODE == 0 ? 1 : 2;
 	constexpr int kConsumers = R * kLanes;
@@ -575,6 +578,7 @@ __host__ __device__ inline size_t stream_fixed(int mode, int rows_per_block, int
 template <int MODE, bool FUSED, int R, int P, int CG>
 __global__ void __launch_bounds__(R * kLanes + 32 * P, 2) k_q8_gemv_stream(GemvArgs p, int stages, int xstaged_arg)
 {
+	kernel_entry();
 	static_assert(P >= 1 && P <= 4, "one to four producer warps");
 	constexpr int NM = MODE == 0 ? 1 : 2;
 	constexpr int kConsumers = R * kLanes;
@@ -789,6 +793,7 @@ size_t tma_smem(int mode, int rows, int n, int stages)
 // thread l of a row owns lane l, i.e. elements e = l (mod 8).
 __global__ void __launch_bounds__(kBlock) k_f32q8_swiglu_gemv(GemvArgs p)
 {
+	kernel_entry();
 	using M = F<true>;
 	const int n = p.n, groups = n / kQ8Group;
 	const int64_t b = blockIdx.y;
@@ -845,8 +850,8 @@ int launch_gemv(Kernel kernel, const char *what, const GemvArgs &a, int64_t batc
 	if (smem > 48 * 1024 && cudaFuncSetAttribute((const void *)kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
 		return check_launch(what);
 	const dim3 grid((unsigned)((a.d + kRowsPerBlock - 1) / kRowsPerBlock), (unsigned)batch);
-	kernel<<<grid, kBlock, smem, (cudaStream_t)stream>>>(a);
-	return check_launch(what);
+	const cudaError_t launched = launch_kernel(kernel, grid, kBlock, smem, stream, a);
+	return check_launch(what, launched);
 }
 
 bool weights_ok(const int8_t *q, const float *s) { return q && s && (reinterpret_cast<uintptr_t>(q) & 3) == 0; }
@@ -888,11 +893,12 @@ int launch_gemv_tma(const char *what, const GemvArgs &a, int64_t batch, void *st
 		return check_launch(what);
 	}
 	const dim3 grid((unsigned)((a.d + R - 1) / R), (unsigned)batch);
+	cudaError_t launched;
 	if (wide)
-		k_q8_gemv_tma<MODE, FUSED, 16><<<grid, 16 * kLanes + 32, smem, (cudaStream_t)stream>>>(a, stages);
+		launched = launch_kernel((k_q8_gemv_tma<MODE, FUSED, 16>), grid, 16 * kLanes + 32, smem, stream, a, stages);
 	else
-		k_q8_gemv_tma<MODE, FUSED, 8><<<grid, 8 * kLanes + 32, smem, (cudaStream_t)stream>>>(a, stages);
-	return check_launch(what);
+		launched = launch_kernel((k_q8_gemv_tma<MODE, FUSED, 8>), grid, 8 * kLanes + 32, smem, stream, a, stages);
+	return check_launch(what, launched);
 }
 
 // Per-CTA shared memory aimed at two CTAs per SM, or one when two stages do
@@ -965,8 +971,8 @@ int launch_gemv_stream(const char *what, const GemvArgs &a, int64_t batch, void 
 		return check_launch(what);
 	const int64_t slots = std::max<int64_t>(1, (int64_t)per_sm * dev.sm_count / batch);
 	const dim3 grid((unsigned)std::min(nrb, slots), (unsigned)batch);
-	k_q8_gemv_stream<MODE, FUSED, S::R, S::P, S::CG><<<grid, threads, lay.smem, (cudaStream_t)stream>>>(a, lay.stages, lay.xstaged ? 1 : 0);
-	return check_launch(what);
+	const cudaError_t launched = launch_kernel((k_q8_gemv_stream<MODE, FUSED, S::R, S::P, S::CG>), grid, threads, lay.smem, stream, a, lay.stages, lay.xstaged ? 1 : 0);
+	return check_launch(what, launched);
 }
 
 // The streaming kernel when weights and scales allow bulk copies (16-byte

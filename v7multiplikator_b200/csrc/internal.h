@@ -31,6 +31,12 @@ int current_device(DeviceInfo *out);
 
 // Checks the launch just issued; on failure records the CUDA error.
 int check_launch(const char *what);
+// The same for a launch that returned its own status (cudaLaunchKernelEx).
+int check_launch(const char *what, cudaError_t launched);
+
+// Whether kernels are launched to overlap the drain of the kernel ahead of
+// them in the stream (v7g_set_launch_overlap; on by default).
+bool launch_overlap();
 
 // Persistent-grid size: at most `work_blocks` blocks, at most what fits
 // resident on the device at once (occupancy of `kernel` at `block` threads).

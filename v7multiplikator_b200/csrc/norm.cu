@@ -7,6 +7,7 @@
 // = 4n read + 4n written (+ 4n each for the residual of the fused add); the
 // second pass's re-read of the row is served by L2, gamma by L1/L2.
 #include "internal.h"
+#include "launch.cuh"
 #include "reduce.cuh"
 
 namespace v7g {
@@ -27,6 +28,7 @@ constexpr int kMinBlocks = 4;
 template <int C, int MINB = kMinBlocks, int BLOCK = kBlock>
 __global__ void __launch_bounds__(BLOCK, MINB) k_rmsnorm_rows(float *o, const float *x, const float *__restrict__ w, int64_t rows, int n, float eps)
 {
+	kernel_entry();
 	using M = F<false>;
 	const int lane = threadIdx.x & 31;
 	const int64_t nwarps = ((int64_t)gridDim.x * BLOCK) >> 5;
@@ -89,6 +91,7 @@ __global__ void __launch_bounds__(BLOCK, MINB) k_rmsnorm_rows(float *o, const fl
 template <int C, int MINB = kMinBlocks, int BLOCK = kBlock>
 __global__ void __launch_bounds__(BLOCK, MINB) k_fused_add_rmsnorm_rows(float *o, float *res, const float *add, const float *__restrict__ w, int64_t rows, int n, float eps)
 {
+	kernel_entry();
 	using M = F<false>;
 	const int lane = threadIdx.x & 31;
 	const int64_t nwarps = ((int64_t)gridDim.x * BLOCK) >> 5;
@@ -179,8 +182,8 @@ int launch_rows(Kernel kernel, const char *what, int64_t rows, int oversubscribe
 	const int64_t want = (rows + warps - 1) / warps;
 	const int resident = resident_grid((const void *)kernel, block, 0, want, dev);
 	const int grid = (int)(want < (int64_t)oversubscribe * resident ? want : (int64_t)oversubscribe * resident);
-	kernel<<<grid, block, 0, (cudaStream_t)stream>>>(args...);
-	return check_launch(what);
+	const cudaError_t launched = launch_kernel(kernel, grid, block, 0, stream, args...);
+	return check_launch(what, launched);
 }
 
 bool row_len_ok(int n) { return n > 0 && n < (1 << 24); }

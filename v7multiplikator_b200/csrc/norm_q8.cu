@@ -2,6 +2,7 @@
 // (v7s_rmsnorm_quantize, rmsnorm_quantize_kernel.inc:60-218).  An FTZ
 // compilation unit: the reference runs the Q8 path with FTZ+DAZ.
 #include "internal.h"
+#include "launch.cuh"
 #include "q8_fast.cuh"
 #include "reduce.cuh"
 
@@ -81,6 +82,7 @@ __device__ __noinline__ uint2 codes8_general(float4 h0, float4 h1, float recip)
 template <int C>
 __global__ void __launch_bounds__(kBlock, kMinBlocks) k_rmsnorm_quantize_rows(uint2 *codes, float *scales, const float *x, const float *__restrict__ w, int64_t rows, int n, float eps)
 {
+	kernel_entry();
 	using M = F<true>;
 	const int lane = threadIdx.x & 31;
 	const int slot = lane >> 3; // group of the four the warp holds
@@ -177,8 +179,8 @@ int launch_rows(Kernel kernel, const char *what, int64_t rows, void *stream, Arg
 	const int64_t want = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;
 	const int resident = resident_grid((const void *)kernel, kBlock, 0, want, dev);
 	const int grid = (int)(want < 2ll * resident ? want : 2ll * resident);
-	kernel<<<grid, kBlock, 0, (cudaStream_t)stream>>>(args...);
-	return check_launch(what);
+	const cudaError_t launched = launch_kernel(kernel, grid, kBlock, 0, stream, args...);
+	return check_launch(what, launched);
 }
 
 bool row_len_ok(int n) { return n > 0 && n < (1 << 24); }

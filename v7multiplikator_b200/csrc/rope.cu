@@ -10,6 +10,7 @@
 // kernel that re-reads the head (from L1) in the rotation pass.
 // The reference runs this kernel on its dispatched workers: FTZ+DAZ.
 #include "internal.h"
+#include "launch.cuh"
 #include "reduce.cuh"
 
 namespace v7g {
@@ -76,6 +77,7 @@ struct RopeArgs {
 template <int V, int CH = kChunk>
 __global__ void __launch_bounds__(kBlock) k_rope_rows(RopeArgs p)
 {
+	kernel_entry();
 	using M = F<true>;
 	constexpr int D = 32 * V;
 	constexpr int P = V / 2;
@@ -171,6 +173,7 @@ __global__ void __launch_bounds__(kBlock) k_rope_rows(RopeArgs p)
 // General head size (D % 32 == 0, D <= 1024): one warp per (token, head).
 __global__ void __launch_bounds__(kBlock) k_rope_rows_general(RopeArgs p, int D)
 {
+	kernel_entry();
 	using M = F<true>;
 	const int lane = threadIdx.x & 31;
 	const int64_t nwarps = ((int64_t)gridDim.x * kBlock) >> 5;
@@ -223,8 +226,8 @@ int launch_persistent(Kernel kernel, const char *what, int64_t work_blocks, void
 		return rc;
 	const int resident = resident_grid((const void *)kernel, kBlock, 0, work_blocks, dev);
 	const int grid = (int)(work_blocks < 4ll * resident ? work_blocks : 4ll * resident);
-	kernel<<<grid, kBlock, 0, (cudaStream_t)stream>>>(args...);
-	return check_launch(what);
+	const cudaError_t launched = launch_kernel(kernel, grid, kBlock, 0, stream, args...);
+	return check_launch(what, launched);
 }
 
 } // namespace

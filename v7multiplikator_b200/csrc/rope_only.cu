@@ -15,6 +15,7 @@
 // four consecutive pairs of one head (float4 of lo, of hi, of cos, of sin);
 // the token's cos/sin row is shared by all its heads and stays in L1/L2.
 #include "internal.h"
+#include "launch.cuh"
 #include "reduce.cuh"
 
 namespace v7g {
@@ -46,6 +47,7 @@ __device__ __forceinline__ void rotate(float lo, float hi, float c, float s, flo
 template <bool VEC>
 __global__ void __launch_bounds__(kBlock) k_rope_only_rows(RopeOnlyArgs p)
 {
+	kernel_entry();
 	constexpr int P = VEC ? 4 : 1;
 	const int per_head = p.half / P;
 	const int per_token = (p.hq + p.hk) * per_head;
@@ -95,8 +97,8 @@ int launch_persistent(Kernel kernel, const char *what, int64_t work_blocks, int 
 	work_blocks = work_blocks < 1 ? 1 : work_blocks;
 	const int resident = resident_grid((const void *)kernel, kBlock, 0, work_blocks, dev);
 	const int grid = (int)(work_blocks < (int64_t)resident * oversubscribe ? work_blocks : (int64_t)resident * oversubscribe);
-	kernel<<<grid, kBlock, 0, (cudaStream_t)stream>>>(args...);
-	return check_launch(what);
+	const cudaError_t launched = launch_kernel(kernel, grid, kBlock, 0, stream, args...);
+	return check_launch(what, launched);
 }
 
 } // namespace

@@ -24,6 +24,7 @@
 // by one fp32 ulp on such entries (one entry in 16.8 million for the
 // 131072 x 64 table with base 1e6).
 #include "internal.h"
+#include "launch.cuh"
 
 namespace v7g {
 namespace {
@@ -37,6 +38,7 @@ struct Freqs {
 
 __global__ void __launch_bounds__(kBlock) k_rope_tables(float *cos_t, float *sin_t, int64_t pos0, int64_t positions, int half, int stride, Freqs fr)
 {
+	kernel_entry();
 	const int64_t total = positions * stride;
 	const int64_t step = (int64_t)gridDim.x * kBlock;
 	for (int64_t i = (int64_t)blockIdx.x * kBlock + threadIdx.x; i < total; i += step) {
@@ -97,6 +99,6 @@ extern "C" int v7g_rope_tables(float *cos_table, float *sin_table, int64_t pos0,
 	const int64_t work_blocks = (positions * stride + kBlock - 1) / kBlock;
 	const int resident = resident_grid((const void *)k_rope_tables, kBlock, 0, work_blocks, dev);
 	const int grid = (int)(work_blocks < 4ll * resident ? work_blocks : 4ll * resident);
-	k_rope_tables<<<grid, kBlock, 0, (cudaStream_t)stream>>>(cos_table, sin_table, pos0, positions, half, stride, fr);
-	return check_launch(what);
+	const cudaError_t launched = launch_kernel(k_rope_tables, grid, kBlock, 0, stream, cos_table, sin_table, pos0, positions, half, stride, fr);
+	return check_launch(what, launched);
 }

@@ -12,6 +12,7 @@ namespace v7g {
 namespace {
 thread_local char t_error[512] = "";
 std::atomic<uint64_t> g_launches{0};
+std::atomic<int> g_launch_overlap{1};
 
 constexpr int kMaxDevices = 64;
 struct CachedDevice {
@@ -75,6 +76,19 @@ int check_launch(const char *what)
 	return clear_error();
 }
 
+int check_launch(const char *what, cudaError_t launched)
+{
+	cudaError_t e = cudaGetLastError(); // clears a sticky error the launch left as well
+	if (launched != cudaSuccess)
+		e = launched;
+	if (e != cudaSuccess)
+		return set_error(V7G_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
+	count_launch();
+	return clear_error();
+}
+
+bool launch_overlap() { return g_launch_overlap.load(std::memory_order_relaxed) != 0; }
+
 int resident_grid(const void *kernel, int block, size_t smem, int64_t work_blocks, const DeviceInfo &dev)
 {
 	int per_sm = 0;
@@ -98,6 +112,8 @@ float v7g_get_rms_eps(void) { return g_rms_eps; }
 float *v7g_rms_eps_slot(void) { return &g_rms_eps; }
 const char *v7g_last_error(void) { return v7g::t_error; }
 uint64_t v7g_launch_count(void) { return v7g::g_launches.load(std::memory_order_relaxed); }
+void v7g_set_launch_overlap(int on) { v7g::g_launch_overlap.store(on ? 1 : 0, std::memory_order_relaxed); }
+int v7g_get_launch_overlap(void) { return v7g::g_launch_overlap.load(std::memory_order_relaxed); }
 const char *v7g_version(void) { return "v7g 0.1.0 (sm_100a; reference ABI cpki-gmbh/v7multiplikator v2.36.8)"; }
 
 } // extern "C"

@@ -19,6 +19,7 @@
 // The counts of mismatches are the kernel's output (all zero when the fast
 // forms are exact over their whole input range).
 #include "internal.h"
+#include "launch.cuh"
 #include "q8_fast.cuh"
 
 namespace v7g {
@@ -30,6 +31,7 @@ __device__ __forceinline__ float from_exp_mant(int e, uint32_t m) { return __uin
 
 __global__ void __launch_bounds__(kBlock) k_selftest(unsigned long long *counts)
 {
+	kernel_entry();
 	const uint64_t stride = (uint64_t)gridDim.x * kBlock;
 	const uint64_t tid = (uint64_t)blockIdx.x * kBlock + threadIdx.x;
 	unsigned long long bad[7] = {0, 0, 0, 0, 0, 0, 0};
@@ -112,6 +114,6 @@ extern "C" int v7g_selftest_arith(unsigned long long *dev_counts, void *stream)
 	if (rc != V7G_OK)
 		return rc;
 	const int grid = resident_grid((const void *)k_selftest, kBlock, 0, 1 << 20, dev);
-	k_selftest<<<grid, kBlock, 0, (cudaStream_t)stream>>>(dev_counts);
-	return check_launch("v7g_selftest_arith");
+	const cudaError_t launched = launch_kernel(k_selftest, grid, kBlock, 0, stream, dev_counts);
+	return check_launch("v7g_selftest_arith", launched);
 }

@@ -12,6 +12,7 @@
 #include <algorithm>
 
 #include "internal.h"
+#include "launch.cuh"
 #include "q8_fast.cuh"
 
 namespace v7g {
@@ -27,6 +28,7 @@ constexpr int kQ8Unroll = 2;
 template <bool VEC>
 __global__ void __launch_bounds__(kBlock) k_swiglu(float *out, const float *gate, const float *up, int64_t count)
 {
+	kernel_entry();
 	const int64_t tid = (int64_t)blockIdx.x * kBlock + threadIdx.x;
 	const int64_t nthreads = (int64_t)gridDim.x * kBlock;
 	if (VEC) {
@@ -54,6 +56,7 @@ __global__ void __launch_bounds__(kBlock) k_swiglu(float *out, const float *gate
 template <bool SWIGLU, int U>
 __global__ void __launch_bounds__(kBlock) k_q8_groups(uint32_t *codes, float *scales, const float4 *a, const float4 *b, int64_t ngroups)
 {
+	kernel_entry();
 	const int lane = threadIdx.x & 31;
 	const int half = lane >> 4;
 	const int hl = lane & 15;
@@ -104,6 +107,7 @@ __global__ void __launch_bounds__(kBlock) k_q8_groups(uint32_t *codes, float *sc
 template <bool SWIGLU>
 __global__ void __launch_bounds__(kBlock) k_q8_general(int8_t *codes, float *scales, const float *a, const float *b, int64_t rows, int n)
 {
+	kernel_entry();
 	using M = F<true>;
 	const int lane = threadIdx.x & 31;
 	const int64_t nwarps = ((int64_t)gridDim.x * kBlock) >> 5;
@@ -149,8 +153,8 @@ int launch_persistent(Kernel kernel, const char *what, int64_t work_blocks, int 
 		return rc;
 	const int resident = resident_grid((const void *)kernel, kBlock, 0, work_blocks, dev);
 	const int grid = (int)std::min<int64_t>(work_blocks, (int64_t)resident * oversubscribe);
-	kernel<<<grid, kBlock, 0, (cudaStream_t)stream>>>(args...);
-	return check_launch(what);
+	const cudaError_t launched = launch_kernel(kernel, grid, kBlock, 0, stream, args...);
+	return check_launch(what, launched);
 }
 
 int q8_rows(const char *what, int8_t *codes, float *scales, const float *a, const float *b, int64_t rows, int n, void *stream, bool swiglu)

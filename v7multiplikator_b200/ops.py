@@ -98,6 +98,10 @@ def lib() -> ctypes.CDLL:
         L.v7g_get_rms_eps.restype = c_float
         L.v7g_last_error.restype = c_char_p
         L.v7g_launch_count.restype = c_uint64
+        L.v7g_set_launch_overlap.argtypes = [c_int]
+        L.v7g_set_launch_overlap.restype = None
+        L.v7g_get_launch_overlap.argtypes = []
+        L.v7g_get_launch_overlap.restype = c_int
         L.v7g_version.restype = c_char_p
         L.v7g_pipeline_timeouts.restype = ctypes.c_uint
         _lib = L
@@ -511,6 +515,18 @@ def pipeline_timeouts() -> int:
 def launch_count() -> int:
     """Kernels launched by the library so far in this process."""
     return int(lib().v7g_launch_count())
+
+
+def set_launch_overlap(on: bool) -> None:
+    """Launch overlap (programmatic dependent launch; on by default): each
+    kernel may be scheduled while the kernel ahead of it in the stream drains
+    and waits on the device for it before touching memory.  Off: plain
+    launches.  Results are the same either way."""
+    lib().v7g_set_launch_overlap(1 if on else 0)
+
+
+def launch_overlap() -> bool:
+    return bool(lib().v7g_get_launch_overlap())
 
 
 def version() -> str:
