@@ -69,7 +69,8 @@ def ncu_traffic() -> dict:
 
 
 class ClockSampler:
-    """Samples SM clock and clock-event reasons through NVML while running."""
+    """Samples SM clock and clock-event reasons through NVML while running,
+    with the memory clock, board power and GPU temperature beside them."""
 
     REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4,
                "hw_power_brake_slowdown": 0x80}
@@ -86,7 +87,7 @@ class ClockSampler:
             self.h = pynvml.nvmlDeviceGetHandleByUUID(uuid.encode())
             self.nvml = pynvml
             self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
-            self.mem_max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_MEM)
+            self.mem_max_mhz = self._extra(lambda: pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_MEM))
             self.ok = True
         except Exception as e:  # pragma: no cover - reported in the JSON line
             self.err = repr(e)
@@ -100,14 +101,22 @@ class ClockSampler:
                 sm = n.nvmlDeviceGetClockInfo(self.h, n.NVML_CLOCK_SM)
                 reasons = n.nvmlDeviceGetCurrentClocksEventReasons(self.h)
                 util = n.nvmlDeviceGetUtilizationRates(self.h).gpu
-                mem = n.nvmlDeviceGetClockInfo(self.h, n.NVML_CLOCK_MEM)
-                power = n.nvmlDeviceGetPowerUsage(self.h) / 1000.0
-                temp = n.nvmlDeviceGetTemperature(self.h, n.NVML_TEMPERATURE_GPU)
-                self.samples.append((sm, reasons, util, mem, power, temp))
+                self.samples.append((sm, reasons, util, self._extra(lambda: n.nvmlDeviceGetClockInfo(self.h, n.NVML_CLOCK_MEM)),
+                                     self._extra(lambda: n.nvmlDeviceGetPowerUsage(self.h) / 1000.0),
+                                     self._extra(lambda: n.nvmlDeviceGetTemperature(self.h, n.NVML_TEMPERATURE_GPU))))
             except Exception:
                 pass
             if self._stop.wait(self.period):
                 break
+
+    @staticmethod
+    def _extra(read):
+        """A reading that only explains the clocks (memory clock, power,
+        temperature): None where this driver does not give it."""
+        try:
+            return read()
+        except Exception:
+            return None
 
     def __enter__(self):
         if self.ok:
@@ -125,10 +134,12 @@ class ClockSampler:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": getattr(self, "err", "nvml unavailable")}
         loaded = [s for s in self.samples if s[2] > 0] or self.samples
         reasons = sorted({name for _, r, *_ in loaded for name, bit in self.REASONS.items() if r & bit})
-        med = (lambda i: statistics.median(s[i] for s in loaded) if loaded else None)
+        def med(i):
+            v = [s[i] for s in loaded if s[i] is not None]
+            return statistics.median(v) if v else None
         return {"sm_mhz": med(0), "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(loaded),
                 "mem_mhz": med(3), "mem_max_mhz": self.mem_max_mhz, "power_w": med(4),
-                "temp_c_max": max((s[5] for s in loaded), default=None),
+                "temp_c_max": max((s[5] for s in loaded if s[5] is not None), default=None),
                 "source": "NVML, sampled every 5 ms in the timed region"}
 
 
