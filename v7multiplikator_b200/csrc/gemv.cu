@@ -318,17 +318,17 @@ __device__ __forceinline__ void chunk_chains(float (&acc)[NM], const uint32_t *s
 // weight byte to float by placing it in the mantissa of 2^23 + 128 and
 // subtracting (exact), times its group scale (rounded), fused multiply-add
 // with x_e -- the dual-row arithmetic of swiglu_kernel.inc:30-47.  The lane's
-// byte of step k is byte l % 4 of word 2k + l / 4 of the group.  st: the row's
+// byte of step k is byte 8k + l of the group, read on its own (one shared
+// load and one logic op per byte: (u ^ 0x80) | 0x4B000000).  st: the row's
 // gate slot (up at + R slots); xl: the lane's activations from the first
 // group, 8 per group; sw: the row's gate scales (up at + R * sstride).
 template <int R, int CG = kChunkGroups>
 __device__ __forceinline__ void chunk_f32(float (&acc)[2], const uint32_t *st, const float *xl, const float *sw, int sstride, int l, int gk)
 {
-	const uint32_t sel = 0x7540u | (uint32_t)(l & 3); // byte l % 4, then 0, 0, 0x4B
-	const float2 bias = splat2(-8388736.0f);            // -(2^23 + 128)
+	const float2 bias = splat2(-8388736.0f); // -(2^23 + 128)
 	float2 a = make_float2(acc[0], acc[1]);
-	// the lane's words of step k: 2k + l / 4, loaded one by one (no selects)
-	const uint32_t *stg = st + (l >> 2), *stu = st + R * (row_slot(CG) / 4) + (l >> 2);
+	const unsigned char *stg = reinterpret_cast<const unsigned char *>(st) + l;
+	const unsigned char *stu = stg + R * row_slot(CG);
 #pragma unroll 2
 	for (int gi = 0; gi < gk; ++gi) {
 		const float4 x0 = *reinterpret_cast<const float4 *>(xl + gi * 8);
@@ -336,15 +336,10 @@ __device__ __forceinline__ void chunk_f32(float (&acc)[2], const uint32_t *st, c
 		const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
 		const float2 sc = make_float2(sw[gi], sw[R * sstride + gi]);
 #pragma unroll
-		for (int j = 0; j < 4; ++j) {
-			const uint32_t gw[2] = {stg[gi * 16 + 4 * j], stg[gi * 16 + 4 * j + 2]};
-			const uint32_t uw[2] = {stu[gi * 16 + 4 * j], stu[gi * 16 + 4 * j + 2]};
-#pragma unroll
-			for (int h = 0; h < 2; ++h) {
-				const float2 raw = make_float2(__uint_as_float(__byte_perm(gw[h] ^ 0x80808080u, 0x4B000000u, sel)),
-				                               __uint_as_float(__byte_perm(uw[h] ^ 0x80808080u, 0x4B000000u, sel)));
-				a = fma2(splat2(xv[2 * j + h]), mul2(add2(raw, bias), sc), a);
-			}
+		for (int k = 0; k < 8; ++k) {
+			const uint32_t gb = stg[gi * kQ8Group + 8 * k], ub = stu[gi * kQ8Group + 8 * k];
+			const float2 raw = make_float2(__uint_as_float((gb ^ 0x80u) | 0x4B000000u), __uint_as_float((ub ^ 0x80u) | 0x4B000000u));
+			a = fma2(splat2(xv[k]), mul2(add2(raw, bias), sc), a);
 		}
 	}
 	acc[0] = a.x;
