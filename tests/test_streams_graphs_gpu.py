@@ -101,3 +101,51 @@ def test_chunked_streams_match_single_launch(cuda):
         assert torch.equal(hs.view(torch.int32), want_s.view(torch.int32))
         hc.zero_()
         hs.zero_()
+
+
+def test_host_threads_on_own_streams(cuda):
+    """Batched entries called from several host threads at once, each on its
+    own stream (ctypes releases the interpreter lock during the call), give the
+    results of one thread: the per-device one-time set-up and the launch path
+    are safe to enter concurrently."""
+    import threading
+
+    import v7multiplikator_b200 as v7g
+    rng = np.random.default_rng(9)
+    n, dout, rows = 4096, 2048, 256
+    wq = torch.from_numpy(rng.integers(-127, 128, (dout, n), dtype=np.int8)).cuda()
+    ws = torch.from_numpy((0.001 + 0.01 * rng.random((dout, n // 64))).astype(np.float32)).cuda()
+    w = torch.from_numpy((1 + 0.1 * rng.standard_normal(n)).astype(np.float32)).cuda()
+    xs = [torch.from_numpy(rng.standard_normal((rows, n), dtype=np.float32)).cuda() for _ in range(4)]
+
+    def work(x, stream):
+        codes = torch.empty(rows, n, dtype=torch.int8, device="cuda")
+        scales = torch.empty(rows, n // 64, device="cuda")
+        y = torch.empty(2, dout, device="cuda")
+        for _ in range(10):
+            v7g.rmsnorm_quantize_rows(codes, scales, x, w, 1e-6, stream=stream)
+            v7g.q8_gemv(y, codes[:2], scales[:2], wq, ws, stream=stream)
+            v7g.q8_fused_gemv(y[1:], x[:1], wq, ws, stream=stream)
+        stream.synchronize()
+        return codes.cpu(), scales.cpu(), y.cpu()
+
+    torch.cuda.synchronize()
+    want = [work(x, torch.cuda.current_stream()) for x in xs]
+    got = [None] * len(xs)
+    errors = []
+
+    def run(i):
+        try:
+            got[i] = work(xs[i], torch.cuda.Stream())
+        except Exception as e:  # reported below
+            errors.append(e)
+
+    threads = [threading.Thread(target=run, args=(i,)) for i in range(len(xs))]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    assert not errors, errors
+    for a, b in zip(want, got):
+        for ta, tb in zip(a, b):
+            assert torch.equal(ta.view(torch.uint8), tb.view(torch.uint8))

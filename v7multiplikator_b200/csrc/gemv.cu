@@ -30,6 +30,7 @@
 //                     issued before their arithmetic.
 // The entry points pick the first that applies.
 #include <algorithm>
+#include <atomic>
 
 #include "arith.cuh"
 #include "internal.h"
@@ -877,12 +878,13 @@ int launch_gemv_tma(const char *what, const GemvArgs &a, int64_t batch, void *st
 	if (smem > kTmaSmemBudget)
 		return V7G_ERR_UNSUPPORTED;
 	const void *kernel = wide ? (const void *)k_q8_gemv_tma<MODE, FUSED, 16> : (const void *)k_q8_gemv_tma<MODE, FUSED, 8>;
-	// the shared-memory ceiling of each kernel is raised once per device
-	static bool raised[2][kMaxDevicesTracked];
-	if (dev.device < kMaxDevicesTracked && !raised[wide][dev.device]) {
+	// the shared-memory ceiling of each kernel is raised once per device (the
+	// call is idempotent, so threads racing to the first launch may both make it)
+	static std::atomic<bool> raised[2][kMaxDevicesTracked];
+	if (dev.device < kMaxDevicesTracked && !raised[wide][dev.device].load(std::memory_order_relaxed)) {
 		if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTmaSmemBudget) != cudaSuccess)
 			return check_launch(what);
-		raised[wide][dev.device] = true;
+		raised[wide][dev.device].store(true, std::memory_order_relaxed);
 	} else if (dev.device >= kMaxDevicesTracked &&
 	           cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTmaSmemBudget) != cudaSuccess) {
 		return check_launch(what);
@@ -954,12 +956,12 @@ int launch_gemv_stream(const char *what, const GemvArgs &a, int64_t batch, void 
 	const void *kernel = (const void *)k_q8_gemv_stream<MODE, FUSED, S::R, S::P, S::CG>;
 	const int threads = S::R * kLanes + 32 * S::P;
 	// the shared-memory ceiling of the kernel is raised once per device
-	static bool raised[kMaxDevicesTracked];
-	if (dev.device >= kMaxDevicesTracked || !raised[dev.device]) {
+	static std::atomic<bool> raised[kMaxDevicesTracked];
+	if (dev.device >= kMaxDevicesTracked || !raised[dev.device].load(std::memory_order_relaxed)) {
 		if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kStreamSmemOne) != cudaSuccess)
 			return check_launch(what);
 		if (dev.device < kMaxDevicesTracked)
-			raised[dev.device] = true;
+			raised[dev.device].store(true, std::memory_order_relaxed);
 	}
 	int per_sm = 0;
 	if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, lay.smem) != cudaSuccess || per_sm < 1)
