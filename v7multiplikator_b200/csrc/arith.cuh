@@ -12,8 +12,8 @@
 // A pair product that feeds a pair sum directly can come out fused into one
 // multiply-add in some kernels (seen with a product added to a rounding
 // constant), losing the product's rounding.  Code that relies on that
-// rounding must not have that shape: q8_codes4_small converts the product
-// with cvt.rni instead; the other kernels put a separate step between
+// rounding must not have that shape: q8_codes4_small uses scalar mul.rn and
+// add.rn in inline PTX, which PTX never contracts; the other kernels put a separate step between
 // (q8_codes4_x2 its clamp) or use the product more than once (v7_sigmoid_x2),
 // and v7g_selftest_arith checks each over its inputs.  (Inline-PTX pair
 // operations would rule it out but cost a third of the SwiGLU throughput in
