@@ -70,3 +70,18 @@ def test_our_arm_line():
     assert line["gpu_launches"] == 5
     clk = line["clocks"]
     assert "sm_mhz" in clk and "reasons" in clk
+
+
+def test_clock_summary_tolerates_missing_readings():
+    """The clock record keeps the SM clock and throttle reasons when the
+    driver does not give the memory clock, power or temperature."""
+    import bench
+    c = bench.ClockSampler.__new__(bench.ClockSampler)
+    c.ok, c.max_mhz, c.mem_max_mhz = True, 1965, None
+    # (sm MHz, reasons, util %, memory MHz, board W, GPU C); the idle sample is left out
+    c.samples = [(1965, 0x0, 80, None, 700.0, None), (1950, 0x4, 90, 3996, None, 55), (300, 0x0, 0, 3996, 90.0, 40)]
+    s = c.summary()
+    assert s["sm_mhz"] == 1957.5 and s["sm_max_mhz"] == 1965
+    assert s["reasons"] == ["sw_power_cap"]
+    assert s["mem_mhz"] == 3996 and s["power_w"] == 700.0 and s["temp_c_max"] == 55
+    assert s["samples"] == 2
