@@ -132,7 +132,10 @@ class ClockSampler:
     def summary(self) -> dict:
         if not self.ok:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": getattr(self, "err", "nvml unavailable")}
-        loaded = [s for s in self.samples if s[2] > 0] or self.samples
+        # every sample falls inside the timed region (the sampler runs only
+        # there); NVML's utilisation reading averages over a window longer
+        # than the region, so it is not used to pick samples
+        loaded = self.samples
         reasons = sorted({name for _, r, *_ in loaded for name, bit in self.REASONS.items() if r & bit})
         def med(i):
             v = [s[i] for s in loaded if s[i] is not None]

@@ -78,10 +78,11 @@ def test_clock_summary_tolerates_missing_readings():
     import bench
     c = bench.ClockSampler.__new__(bench.ClockSampler)
     c.ok, c.max_mhz, c.mem_max_mhz = True, 1965, None
-    # (sm MHz, reasons, util %, memory MHz, board W, GPU C); the idle sample is left out
-    c.samples = [(1965, 0x0, 80, None, 700.0, None), (1950, 0x4, 90, 3996, None, 55), (300, 0x0, 0, 3996, 90.0, 40)]
+    # (sm MHz, reasons, util %, memory MHz, board W, GPU C); a utilisation of 0
+    # (NVML's window is longer than the timed region) does not drop a sample
+    c.samples = [(1965, 0x0, 80, None, 700.0, None), (1950, 0x4, 0, 3996, None, 55), (1965, 0x0, 0, 3996, 690.0, 40)]
     s = c.summary()
-    assert s["sm_mhz"] == 1957.5 and s["sm_max_mhz"] == 1965
+    assert s["sm_mhz"] == 1965 and s["sm_max_mhz"] == 1965
     assert s["reasons"] == ["sw_power_cap"]
-    assert s["mem_mhz"] == 3996 and s["power_w"] == 700.0 and s["temp_c_max"] == 55
-    assert s["samples"] == 2
+    assert s["mem_mhz"] == 3996 and s["power_w"] == 695.0 and s["temp_c_max"] == 55
+    assert s["samples"] == 3
