@@ -164,3 +164,36 @@ def test_gemv_rejects_bad_shapes(cuda):
     s = torch.zeros(4, 1, device=cuda)
     with pytest.raises(v7g.V7GError, match="multiple of 64"):
         v7g.q8_gemv(torch.empty(1, 4, device=cuda), x, torch.zeros(1, 1, device=cuda), w, s)
+
+
+def test_gemv_longest_rows(cuda, oracle):
+    """The longest activation the entries accept (n = 65536, whose staged
+    activation no longer fits the streaming kernel's layout, so the fallback
+    paths run), a ragged d and two batch rows, all four products against the
+    oracle; one group more is refused with the limit named."""
+    import v7multiplikator_b200 as v7g
+    n, d = 65536, 40
+    rng = np.random.default_rng(65536)
+    xq, xs, wq, ws = q8_case(rng, 2, n, d)
+    out = torch.empty(2, d, device=cuda)
+    v7g.q8_gemv(out, dev(xq), dev(xs), dev(wq), dev(ws))
+    assert_same_f32(host(out), oracle.q8_gemv(xq, xs, wq, ws), "v7d_q8 n = 65536")
+    x = rng.normal(0, 2, (2, n)).astype(F)
+    v7g.q8_fused_gemv(out, dev(x), dev(wq), dev(ws))
+    with np.errstate(all="ignore"):
+        assert_same_f32(host(out), oracle.q8_fused_gemv(x, wq, ws), "v7d_q8_fused n = 65536")
+    gq, gs = ref_fill(rng, (d, n), np.int8), ref_fill(rng, (d, n // 64), F)
+    uq, us = ref_fill(rng, (d, n), np.int8), ref_fill(rng, (d, n // 64), F)
+    xq1, xs1 = ref_fill(rng, (2, n), np.int8), ref_fill(rng, (2, n // 64), F)
+    v7g.swiglu_q8_gemv(out, dev(xq1), dev(xs1), dev(gq), dev(gs), dev(uq), dev(us))
+    with np.errstate(all="ignore"):
+        assert_same_f32(host(out), oracle.swiglu_q8_gemv(xq1, xs1, gq, gs, uq, us), "v7d_swiglu_q8 n = 65536")
+    xf = ref_fill(rng, (2, n), F)
+    v7g.swiglu_f32q8_gemv(out, dev(xf), dev(gq), dev(gs), dev(uq), dev(us))
+    with np.errstate(all="ignore"):
+        assert_same_f32(host(out), oracle.swiglu_f32q8_gemv(xf, gq, gs, uq, us), "v7d_swiglu n = 65536")
+    m = n + 64
+    with pytest.raises(v7g.V7GError, match="at most 65536"):
+        v7g.q8_gemv(torch.empty(1, 4, device=cuda), torch.zeros(1, m, dtype=torch.int8, device=cuda),
+                    torch.zeros(1, m // 64, device=cuda), torch.zeros(4, m, dtype=torch.int8, device=cuda),
+                    torch.zeros(4, m // 64, device=cuda))
