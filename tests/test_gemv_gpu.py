@@ -197,3 +197,18 @@ def test_gemv_longest_rows(cuda, oracle):
         v7g.q8_gemv(torch.empty(1, 4, device=cuda), torch.zeros(1, m, dtype=torch.int8, device=cuda),
                     torch.zeros(1, m // 64, device=cuda), torch.zeros(4, m, dtype=torch.int8, device=cuda),
                     torch.zeros(4, m // 64, device=cuda))
+
+
+def test_gemv_largest_batch(cuda, oracle):
+    """The largest batch (65535 activation rows: the grid's second dimension)
+    against the oracle; one row more is refused."""
+    import v7multiplikator_b200 as v7g
+    batch, n, d = 65535, 64, 8
+    rng = np.random.default_rng(7)
+    xq, xs, wq, ws = q8_case(rng, batch, n, d)
+    out = torch.empty(batch, d, device=cuda)
+    v7g.q8_gemv(out, dev(xq), dev(xs), dev(wq), dev(ws))
+    assert_same_f32(host(out), oracle.q8_gemv(xq, xs, wq, ws), "v7d_q8 batch 65535")
+    with pytest.raises(v7g.V7GError, match="above 65535"):
+        v7g.q8_gemv(torch.empty(batch + 1, d, device=cuda), torch.zeros(batch + 1, n, dtype=torch.int8, device=cuda),
+                    torch.zeros(batch + 1, 1, device=cuda), dev(wq), dev(ws))
