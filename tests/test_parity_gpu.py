@@ -62,6 +62,16 @@ def test_selftest_arith_exhaustive(cuda):
 # --------------------------------------------------------------- RMSNorm rows
 
 
+
+def rope_tables_for(oracle, rng, rows, half, rmd, base):
+    """cos/sin tables [rows, rmd]: the reference's own builder (x87, through the
+    oracle) up to the 256 frequency pairs it makes; beyond that -- head_dim up to
+    1024, which the kernels take with caller tables -- seeded unit-circle values."""
+    if half <= 256:
+        return oracle.rope_tables(rows, half, rmd, base)
+    th = rng.uniform(-np.pi, np.pi, (rows, rmd))
+    return np.cos(th).astype(np.float32), np.sin(th).astype(np.float32)
+
 @pytest.mark.parametrize("rows,n", [(1, 32), (3, 64), (17, 96), (64, 2048), (5, 3072), (2, 8192), (7, 4096), (300, 256),
                                     (1025, 96), (2000, 2048)])
 @pytest.mark.parametrize("eps", [0.0, 1e-6])
@@ -143,7 +153,7 @@ def test_fused_add_rmsnorm_reference_validator_cases(cuda, oracle, golden, dim):
 # ------------------------------------------------------------ RMSNorm + RoPE
 
 
-@pytest.mark.parametrize("head_dim", [32, 64, 96, 128, 192, 256, 512])
+@pytest.mark.parametrize("head_dim", [32, 64, 96, 128, 192, 256, 512, 1024])
 @pytest.mark.parametrize("heads", [(16, 8), (5, 3), (0, 2), (4, 0)])
 @pytest.mark.parametrize("tokens,pos0", [(1, 0), (7, 0), (130, 5)])
 def test_rmsnorm_rope_rows(cuda, oracle, head_dim, heads, tokens, pos0):
@@ -155,7 +165,7 @@ def test_rmsnorm_rope_rows(cuda, oracle, head_dim, heads, tokens, pos0):
     wq = normal(rng, head_dim, 1, 0.1)
     wk = normal(rng, head_dim, 1, 0.1)
     rmd = head_dim  # validator layout: rows of head_dim, first half used
-    cos, sin = oracle.rope_tables(pos0 + tokens, head_dim // 2, rmd, 1e6)
+    cos, sin = rope_tables_for(oracle, rng, pos0 + tokens, head_dim // 2, rmd, 1e6)
     qt, kt = dev(q), dev(k)
     v7g.rmsnorm_rope_rows(qt if hq else None, kt if hk else None, dev(wq) if hq else None, dev(wk) if hk else None,
                           dev(cos), dev(sin), pos0, 1e-6)

@@ -24,7 +24,17 @@ def ulp_distance(a: np.ndarray, b: np.ndarray) -> np.ndarray:
     return np.abs(key(a) - key(b))
 
 
-@pytest.mark.parametrize("head_dim", [32, 64, 96, 128, 256, 512])
+
+def rope_tables_for(oracle, rng, rows, half, rmd, base):
+    """cos/sin tables [rows, rmd]: the reference's own builder (x87, through the
+    oracle) up to the 256 frequency pairs it makes; beyond that -- head_dim up to
+    1024, which the kernels take with caller tables -- seeded unit-circle values."""
+    if half <= 256:
+        return oracle.rope_tables(rows, half, rmd, base)
+    th = rng.uniform(-np.pi, np.pi, (rows, rmd))
+    return np.cos(th).astype(np.float32), np.sin(th).astype(np.float32)
+
+@pytest.mark.parametrize("head_dim", [32, 64, 96, 128, 256, 512, 1024])
 @pytest.mark.parametrize("heads", [(16, 8), (5, 3), (0, 2), (4, 0)])
 @pytest.mark.parametrize("tokens,pos0", [(1, 0), (1, 9), (7, 0), (130, 5)])
 def test_rope_only_rows(cuda, oracle, head_dim, heads, tokens, pos0):
@@ -33,7 +43,7 @@ def test_rope_only_rows(cuda, oracle, head_dim, heads, tokens, pos0):
     rng = np.random.default_rng(head_dim * 1000 + hq * 10 + hk + tokens + pos0)
     q = normal(rng, (tokens, hq, head_dim))
     k = normal(rng, (tokens, hk, head_dim))
-    cos, sin = oracle.rope_tables(pos0 + tokens, head_dim // 2, head_dim, 1e6)
+    cos, sin = rope_tables_for(oracle, rng, pos0 + tokens, head_dim // 2, head_dim, 1e6)
     qt, kt = dev(q), dev(k)
     v7g.rope_only_rows(qt if hq else None, kt if hk else None, dev(cos), dev(sin), pos0)
     if hq:
@@ -150,6 +160,19 @@ def test_rope_only_rejects_bad_head_dim(cuda):
     t = torch.zeros(4, 24, device=cuda)
     with pytest.raises(v7g.V7GError, match="multiple of 32"):
         v7g.rope_only_rows(q, None, t, t, 1)
+
+
+def test_rope_entries_reject_head_dim_above_1024(cuda):
+    """One 32-block past the largest head the kernels take (1024) is refused
+    by both entries, with the range named, before anything is launched."""
+    import v7multiplikator_b200 as v7g
+    q = torch.zeros(2, 1, 1056, device=cuda)
+    t = torch.zeros(4, 528, device=cuda)
+    w = torch.ones(1056, device=cuda)
+    with pytest.raises(v7g.V7GError, match=r"\[32, 1024\]"):
+        v7g.rope_only_rows(q, None, t, t, 1)
+    with pytest.raises(v7g.V7GError, match=r"\[32, 1024\]"):
+        v7g.rmsnorm_rope_rows(q, None, w, None, t, t, 1, 1e-6)
 
 
 def test_reference_abi_rope_entries(cuda, oracle, tmp_path):
