@@ -467,3 +467,34 @@ def test_nonzero_stream(cuda, oracle):
     s.synchronize()
     wq, ws = oracle.swiglu_q8(g, u)
     np.testing.assert_array_equal(codes.cpu().numpy(), wq)
+
+
+@pytest.mark.parametrize("rows,n", [(2, 1 << 20), (1, (1 << 24) - 64)])
+def test_row_kernels_longest_rows(cuda, oracle, rows, n):
+    """The longest rows the row kernels take (n below 2^24: a 64 MB row, one
+    warp streaming it in chunks) for RMSNorm, fused add + RMSNorm and
+    RMSNorm -> Q8, against the oracle; n = 2^24 is refused."""
+    import v7multiplikator_b200 as v7g
+    rng = np.random.default_rng(n + rows)
+    x = normal(rng, (rows, n))
+    a = normal(rng, (rows, n), 0, 0.5)
+    w = normal(rng, n, 1.0, 0.1)
+    out = torch.empty(rows, n, device=cuda)
+    v7g.rmsnorm_rows(out, dev(x), dev(w), 1e-6)
+    assert_same_f32(host(out), oracle.rmsnorm(x, w, 1e-6), "rmsnorm")
+    rt = dev(x)
+    v7g.fused_add_rmsnorm_rows(out, rt, dev(a), dev(w), 1e-6)
+    want_o, want_r = oracle.fused_add_rmsnorm(x, a, w, 1e-6)
+    assert_same_f32(host(rt), want_r, "residual")
+    assert_same_f32(host(out), want_o, "fused out")
+    del rt, out
+    codes = torch.empty(rows, n, dtype=torch.int8, device=cuda)
+    scales = torch.empty(rows, n // 64, device=cuda)
+    v7g.rmsnorm_quantize_rows(codes, scales, dev(x), dev(w), 1e-6)
+    wq, ws = oracle.rmsnorm_quantize(x, w, 1e-6)
+    np.testing.assert_array_equal(host(codes), wq)
+    assert_same_f32(host(scales), ws)
+    if rows == 1:
+        m = 1 << 24
+        with pytest.raises(v7g.V7GError, match="2\\^24"):
+            v7g.rmsnorm_rows(torch.empty(1, m, device=cuda), torch.zeros(1, m, device=cuda), torch.ones(m, device=cuda), 1e-6)
