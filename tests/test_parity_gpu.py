@@ -249,7 +249,7 @@ def plant(x: np.ndarray, rng, count: int) -> np.ndarray:
     return x
 
 
-@pytest.mark.parametrize("rows,n", [(1, 64), (3, 128), (5, 192), (33, 12288), (2, 448), (1, 64 * 1001)])
+@pytest.mark.parametrize("rows,n", [(1, 64), (3, 128), (5, 192), (33, 12288), (2, 448), (1, 64 * 1001), (1, 1 << 22)])
 @pytest.mark.parametrize("specials", [False, True])
 def test_swiglu_q8_rows(cuda, oracle, rows, n, specials):
     import v7multiplikator_b200 as v7g
