@@ -196,8 +196,9 @@ uint64_t v7g_launch_count(void);
    is launched so that it may be scheduled while the kernel ahead of it in the
    stream drains, and waits on the device for that kernel's completion before
    its first memory access.  Stream order is kept either way; off gives plain
-   launches.  Process-wide; takes effect at the next launch.  No reference
-   counterpart (the reference's kernels are CPU calls). */
+   launches.  Process-wide; takes effect at the next launch.  The environment
+   variable V7G_LAUNCH_OVERLAP=0, read when the library is loaded, starts it
+   off.  No reference counterpart (the reference's kernels are CPU calls). */
 void v7g_set_launch_overlap(int on);
 int v7g_get_launch_overlap(void);
 

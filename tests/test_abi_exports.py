@@ -7,6 +7,7 @@ from __future__ import annotations
 
 import ctypes
 import subprocess
+import sys
 from pathlib import Path
 
 import pytest
@@ -100,6 +101,18 @@ def test_launch_overlap_switch(native_lib_path):
     finally:
         v7g.set_launch_overlap(True)
     assert v7g.launch_overlap()
+
+
+def test_launch_overlap_environment_switch(native_lib_path):
+    """V7G_LAUNCH_OVERLAP=0 starts the library with plain launches."""
+    import os
+    env = dict(os.environ, V7G_LAUNCH_OVERLAP="0")
+    code = "import v7multiplikator_b200 as v; print(v.launch_overlap())"
+    out = subprocess.run([sys.executable, "-c", code], cwd=ROOT, env=env, capture_output=True, text=True, check=True)
+    assert out.stdout.strip() == "False"
+    env["V7G_LAUNCH_OVERLAP"] = "1"
+    out = subprocess.run([sys.executable, "-c", code], cwd=ROOT, env=env, capture_output=True, text=True, check=True)
+    assert out.stdout.strip() == "True"
 
 
 @pytest.fixture(scope="module")

@@ -3,6 +3,7 @@
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 #include "internal.h"
@@ -12,7 +13,14 @@ namespace v7g {
 namespace {
 thread_local char t_error[512] = "";
 std::atomic<uint64_t> g_launches{0};
-std::atomic<int> g_launch_overlap{1};
+// launch overlap: on unless the environment says V7G_LAUNCH_OVERLAP=0 (read
+// once, when the library is loaded); v7g_set_launch_overlap changes it later
+int overlap_from_env()
+{
+	const char *v = std::getenv("V7G_LAUNCH_OVERLAP");
+	return (v && v[0] == '0' && v[1] == 0) ? 0 : 1;
+}
+std::atomic<int> g_launch_overlap{overlap_from_env()};
 
 constexpr int kMaxDevices = 64;
 struct CachedDevice {
