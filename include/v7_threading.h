@@ -12,7 +12,11 @@
  * GPU: each entry accepts HOST or DEVICE pointers (decided per pointer with
  * cudaPointerGetAttributes).  Device pointers are used in place; host buffers
  * are staged through a device workspace.  Every call returns with its results
- * written, as the reference's do.
+ * written, as the reference's do.  The calls take no stream, so a call given
+ * any device pointer first waits for all work already queued on that device
+ * (cudaDeviceSynchronize): inputs a caller's kernel is still writing, on any
+ * stream, are complete before they are read.  A call leaves the calling
+ * thread's current CUDA device as it found it.
  *
  * Everything outside that path (models, chat, tokenizer, attention, matmul,
  * vision, SectorLogo, ...) is exported as a stub: it returns 0/NULL and marks

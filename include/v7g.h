@@ -169,12 +169,15 @@ unsigned int v7g_pipeline_timeouts(void);
    V7G_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds until the
    process exits.  Work beyond that (gamma plus x and o, each rounded up to 256
    bytes) is rejected with V7G_ERR_ARG.  The first call on a device looks up
-   the array's device address (cudaGetSymbolAddress), so make it before any
-   stream capture.  Synchronous: returns when o is written.  Calls share the
-   array; they are serialised and each waits for `stream`, so they never
-   overlap on the GPU -- calls that did overlap would race.  Nothing needs
-   clearing between calls: each copies its whole input in and output out.
-   Results equal v7g_rmsnorm_rows bit for bit.  Contract: n % 32 == 0. */
+   the array's device address (cudaGetSymbolAddress) and keeps it until the
+   process exits, so make that call before any stream capture, and do not
+   call cudaDeviceReset in between.  `stream` must belong to the current
+   device (V7G_ERR_ARG otherwise).  Synchronous: returns when o is written,
+   and on a failure only once nothing it queued is still running.  Calls
+   share the array; they are serialised and each waits for `stream`, so they
+   never overlap on the GPU -- calls that did overlap would race.  Nothing
+   needs clearing between calls: each copies its whole input in and output
+   out.  Results equal v7g_rmsnorm_rows bit for bit.  Contract: n % 32 == 0. */
 #define V7G_NOALLOC_SCRATCH_BYTES (4u << 20)
 int v7g_rmsnorm_rows_noalloc(float *o, const float *x, const float *w, int64_t rows, int n, float eps, void *stream);
 

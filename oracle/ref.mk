@@ -6,7 +6,9 @@
 # Include set and flags follow the reference Makefile (Makefile:6-9, :60, :67-68);
 # v_rmsnorm_validate is built at -O0 as the reference builds it (Makefile:60).
 # The reference's engine itself is NASM and cannot be assembled here (no nasm).
-REF ?= /root/reference
+# The reference tree: REF=... on the command line, else $V7_REFERENCE_DIR, else
+# a `reference` checkout beside this repository (this file runs from oracle/).
+REF ?= $(or $(V7_REFERENCE_DIR),$(abspath ../../reference))
 OUT := _ref
 CXX ?= g++
 CPPFLAGS_REF := -D_GNU_SOURCE -I$(REF)/src/linux/compat -I$(REF)/src/linux -I$(REF)/src -I$(REF)/tools -I$(REF)/tools/zydis_stub

@@ -11,13 +11,16 @@
 * ``v7_load_names.txt`` -- the 99 symbol names the reference's loader
   resolves (src/v7_lib.h:613-735).
 
-Usage: python tests/golden/make_golden.py [--ref /root/reference]
-Needs g++ and the reference source tree; the outputs are committed.
+Usage: python tests/golden/make_golden.py [--ref <reference tree>]
+The tree defaults to $V7_REFERENCE_DIR, else a `reference` checkout beside
+this repository.  Needs g++ and the reference source tree; the outputs are
+committed.
 """
 from __future__ import annotations
 
 import argparse
 import hashlib
+import os
 import re
 import struct
 import subprocess
@@ -31,7 +34,7 @@ HERE = Path(__file__).resolve().parent
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("V7_REFERENCE_DIR") or str(HERE.parents[2] / "reference"))
     args = ap.parse_args()
     ref = Path(args.ref)
 

@@ -9,7 +9,12 @@
 //   - a host pointer is staged through a per-device workspace: inputs copied
 //     in, outputs copied back before the call returns.
 // Each call runs on a library-owned stream and returns with its results in
-// place (the reference's calls are synchronous).  A contract violation or a
+// place (the reference's calls are synchronous).  The reference's calls take
+// no stream, so when any pointer is device memory the call first waits for
+// all work already queued on that device (cudaDeviceSynchronize): a kernel of
+// the caller's that is still writing an input, on any stream, has finished
+// before the library reads it.  The calling thread's current device is the
+// same after the call as before it.  A contract violation or a
 // CUDA failure marks the engine dead with a reason (v7_engine_is_dead /
 // v7_get_death_reason, src/v7_lib.h:179-184) and leaves the outputs unwritten,
 // where the reference would FATAL (engine_landing.inc:150) or silently
@@ -108,6 +113,24 @@ int pointer_device(const void *p, int *dev)
 // Maps every argument of one call to device memory.
 class Stager {
   public:
+	Stager()
+	{
+		if (cudaGetDevice(&caller_device_) != cudaSuccess) {
+			cudaGetLastError();
+			caller_device_ = -1;
+		}
+	}
+	// The caller's current device again, whatever the call selected.
+	~Stager()
+	{
+		int cur = -1;
+		if (caller_device_ >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != caller_device_)
+			cudaSetDevice(caller_device_);
+		cudaGetLastError();
+	}
+	Stager(const Stager &) = delete;
+	Stager &operator=(const Stager &) = delete;
+
 	struct Arg {
 		void *user;
 		size_t bytes;
@@ -156,6 +179,13 @@ class Stager {
 			die("%s: cannot select CUDA device %d", what, device_);
 			return false;
 		}
+		// a device pointer may still be written by the caller's own queued
+		// work, on a stream this call cannot know: wait for the whole device
+		bool any_device = false;
+		for (const Arg &a : args_)
+			any_device = any_device || (a.user && !a.host);
+		if (any_device && cudaDeviceSynchronize() != cudaSuccess)
+			return fail("waiting for the caller's queued work");
 		size_t total = 0;
 		for (Arg &a : args_)
 			if (a.host && a.alias < 0) {
@@ -202,14 +232,20 @@ class Stager {
 	}
 
   private:
+	// Records the failure; copies already queued on the library stream use
+	// the shared workspace, so they finish before the lock is released.
 	bool fail(const char *step)
 	{
 		cudaError_t e = cudaGetLastError();
 		die("%s: %s failed: %s", what_, step, cudaGetErrorString(e));
+		if (ctx_ && ctx_->stream)
+			cudaStreamSynchronize(ctx_->stream);
+		cudaGetLastError();
 		return false;
 	}
 
 	std::vector<Arg> args_;
+	int caller_device_ = -1;
 	int device_ = -1;
 	bool mixed_ = false;
 	DeviceCtx *ctx_ = nullptr;

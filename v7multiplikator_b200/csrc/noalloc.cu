@@ -13,11 +13,14 @@
 // GPU that loads the library and held until the process exits.
 //
 // The array is shared by every call.  Calls are serialised on the host and
-// each waits for its stream before returning, so two calls of this entry
-// point never overlap on the GPU; anything else that made them overlap would
-// race on the array.  Each call copies its whole input in and its whole
-// output out, so the contents a previous call left behind are never read and
-// nothing needs clearing.
+// each waits for its stream before returning -- on its failure paths too,
+// once anything has been queued -- so two calls of this entry point never
+// overlap on the GPU; anything else that made them overlap would race on the
+// array.  Each call copies its whole input in and its whole output out, so
+// the contents a previous call left behind are never read and nothing needs
+// clearing.  The array's device address is looked up once per device and
+// kept for the life of the process, so a cudaDeviceReset between calls is
+// not supported; `stream` must belong to the current device.
 #include <mutex>
 
 #include "internal.h"
@@ -61,6 +64,17 @@ int cuda_fail(const char *step, cudaError_t e)
 	return set_error(V7G_ERR_CUDA, "v7g_rmsnorm_rows_noalloc: %s failed: %s", step, cudaGetErrorString(e));
 }
 
+// A failure after the first copy was queued: whatever is still queued on `s`
+// reads or writes the shared array, so wait for it before the lock is
+// released (the next call may use another stream).  Returns `rc`, keeping the
+// first failure's message.
+int drain_and_fail(cudaStream_t s, int rc)
+{
+	cudaStreamSynchronize(s);
+	cudaGetLastError();
+	return rc;
+}
+
 } // namespace
 } // namespace v7g
 
@@ -90,6 +104,17 @@ extern "C" int v7g_rmsnorm_rows_noalloc(float *o, const float *x, const float *w
 	int rc = current_device(&dev);
 	if (rc != V7G_OK)
 		return rc;
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	// the default streams (NULL, legacy, per-thread) are the current device's
+	int stream_dev = dev.device;
+	cudaError_t e = cudaSuccess;
+	if (s && s != cudaStreamLegacy && s != cudaStreamPerThread) {
+		e = cudaStreamGetDevice(s, &stream_dev);
+		if (e != cudaSuccess)
+			return cuda_fail("querying the stream's device", e);
+	}
+	if (stream_dev != dev.device)
+		return set_error(V7G_ERR_ARG, "%s: the stream belongs to device %d, the current device is %d", what, stream_dev, dev.device);
 	unsigned char *base = nullptr;
 	rc = scratch_for(dev.device, &base);
 	if (rc != V7G_OK)
@@ -97,21 +122,18 @@ extern "C" int v7g_rmsnorm_rows_noalloc(float *o, const float *x, const float *w
 	float *dw = reinterpret_cast<float *>(base);
 	float *dx = reinterpret_cast<float *>(base + round_up(wb));
 	float *dout = reinterpret_cast<float *>(base + round_up(wb) + round_up(xb));
-	cudaStream_t s = static_cast<cudaStream_t>(stream);
-	cudaError_t e = cudaMemcpyAsync(dw, w, wb, cudaMemcpyDefault, s);
+	e = cudaMemcpyAsync(dw, w, wb, cudaMemcpyDefault, s);
 	if (e != cudaSuccess)
-		return cuda_fail("copying gamma in", e);
+		return drain_and_fail(s, cuda_fail("copying gamma in", e));
 	e = cudaMemcpyAsync(dx, x, xb, cudaMemcpyDefault, s);
 	if (e != cudaSuccess)
-		return cuda_fail("copying x in", e);
+		return drain_and_fail(s, cuda_fail("copying x in", e));
 	rc = v7g_rmsnorm_rows(dout, dx, dw, rows, n, eps, stream);
-	if (rc != V7G_OK) {
-		cudaStreamSynchronize(s);
-		return rc;
-	}
+	if (rc != V7G_OK)
+		return drain_and_fail(s, rc);
 	e = cudaMemcpyAsync(o, dout, xb, cudaMemcpyDefault, s);
 	if (e != cudaSuccess)
-		return cuda_fail("copying o out", e);
+		return drain_and_fail(s, cuda_fail("copying o out", e));
 	e = cudaStreamSynchronize(s);
 	if (e != cudaSuccess)
 		return cuda_fail("stream synchronisation", e);
