@@ -11,18 +11,24 @@ of the fused kernel over the rank's shard.
 
 Reported (one JSON line from rank 0):
   value      whole-job algorithmic GB/s (inputs read once + outputs written
-             once) / max-over-ranks device time, inputs resident in HBM
+             once) / max-over-ranks device time of K launches issued back to
+             back between one start and one end event, inputs resident in HBM
+  verified   every code and scale of the whole job, gathered to rank 0 over
+             NCCL after timing, against the oracle on the same input bytes
+             (bit-exact); a mismatch makes the run exit non-zero
   e2e        the same metric through the public API with host buffers: every
              step copies the shard's gate/up from pinned host memory and reads
              codes/scales back (pipelined in row chunks over three streams);
-             e2e.link times the same copies alone, the step's floor on the
-             host link
+             e2e.link times the same copies alone, per rank and in aggregate,
+             the step's floor on the host link
   roofline   the kernel's achieved GB/s against the measured HBM copy peak
-  cpu_baseline  the oracle port on the host cores, bounded sample (N=1 only)
+  cpu_baseline  the oracle port on the host cores, whole C5 passes for about
+             --cpu-seconds (N=1 only)
   kernels    the other BASELINE configs (C1-C4) and the next rows (add_inplace,
              RMSNorm->Q8, RoPE without the norm, the RoPE table build, the
              Q8-weight GEMVs), device-timed, N=1 only
-``--impl reference`` times the CPU implementation instead (rank 0 only).
+``--impl reference`` times the CPU implementation instead (rank 0 only):
+whole 16384-row C5 passes on the GPU arm's input bytes, all host threads.
 """
 from __future__ import annotations
 
@@ -45,6 +51,7 @@ METRIC = "fused-kernel HBM GB/s (% of B200 peak) and rows/s at 1/2/4/8 GPUs"
 L2_BYTES = 126 * 2**20
 C5_ROWS, C5_N = 16384, 12288
 GROUP = 64
+SEED_GATE, SEED_UP = 12, 13
 
 
 def c5_bytes(rows: int, n: int = C5_N) -> int:
@@ -70,15 +77,19 @@ def ncu_traffic() -> dict:
 
 class ClockSampler:
     """Samples SM clock and clock-event reasons through NVML while running,
-    with the memory clock, board power and GPU temperature beside them."""
+    with the memory clock, board power and GPU temperature beside them.  Each
+    sample carries its host time; mark_start / mark_end bracket the timed
+    region, and summary() reports the samples inside it (all samples when no
+    region was marked)."""
 
     REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4,
                "hw_power_brake_slowdown": 0x80}
 
-    def __init__(self, device_index: int, period_s: float = 0.005):
-        self.samples: list[tuple] = []  # (sm MHz, reasons, util %, memory MHz, board W, GPU C)
+    def __init__(self, device_index: int, period_s: float = 0.001):
+        self.samples: list[tuple] = []  # (t, sm MHz, reasons, memory MHz, board W, GPU C)
         self.period = period_s
         self.ok = False
+        self.t0 = self.t1 = None
         try:
             import pynvml
             pynvml.nvmlInit()
@@ -98,10 +109,10 @@ class ClockSampler:
         n = self.nvml
         while True:
             try:
+                t = time.perf_counter()
                 sm = n.nvmlDeviceGetClockInfo(self.h, n.NVML_CLOCK_SM)
                 reasons = n.nvmlDeviceGetCurrentClocksEventReasons(self.h)
-                util = n.nvmlDeviceGetUtilizationRates(self.h).gpu
-                self.samples.append((sm, reasons, util, self._extra(lambda: n.nvmlDeviceGetClockInfo(self.h, n.NVML_CLOCK_MEM)),
+                self.samples.append((t, sm, reasons, self._extra(lambda: n.nvmlDeviceGetClockInfo(self.h, n.NVML_CLOCK_MEM)),
                                      self._extra(lambda: n.nvmlDeviceGetPowerUsage(self.h) / 1000.0),
                                      self._extra(lambda: n.nvmlDeviceGetTemperature(self.h, n.NVML_TEMPERATURE_GPU))))
             except Exception:
@@ -118,6 +129,12 @@ class ClockSampler:
         except Exception:
             return None
 
+    def mark_start(self):
+        self.t0 = time.perf_counter()
+
+    def mark_end(self):
+        self.t1 = time.perf_counter()
+
     def __enter__(self):
         if self.ok:
             self._t = threading.Thread(target=self._run, daemon=True)
@@ -132,18 +149,17 @@ class ClockSampler:
     def summary(self) -> dict:
         if not self.ok:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": getattr(self, "err", "nvml unavailable")}
-        # every sample falls inside the timed region (the sampler runs only
-        # there); NVML's utilisation reading averages over a window longer
-        # than the region, so it is not used to pick samples
-        loaded = self.samples
-        reasons = sorted({name for _, r, *_ in loaded for name, bit in self.REASONS.items() if r & bit})
+        inside = [x for x in self.samples if self.t0 is None or self.t0 <= x[0] <= self.t1]
+        use = inside or self.samples
+        reasons = sorted({name for _, _, r, *_ in use for name, bit in self.REASONS.items() if r & bit})
+
         def med(i):
-            v = [s[i] for s in loaded if s[i] is not None]
+            v = [x[i] for x in use if x[i] is not None]
             return statistics.median(v) if v else None
-        return {"sm_mhz": med(0), "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(loaded),
-                "mem_mhz": med(3), "mem_max_mhz": self.mem_max_mhz, "power_w": med(4),
-                "temp_c_max": max((s[5] for s in loaded if s[5] is not None), default=None),
-                "source": "NVML, sampled every 5 ms in the timed region"}
+        return {"sm_mhz": med(1), "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(inside),
+                "samples_used": len(use), "mem_mhz": med(3), "mem_max_mhz": self.mem_max_mhz, "power_w": med(4),
+                "temp_c_max": max((x[5] for x in use if x[5] is not None), default=None),
+                "source": f"NVML, sampled every {self.period * 1e3:g} ms; samples = those inside the timed region"}
 
 
 # ------------------------------------------------------------ distributed
@@ -186,6 +202,16 @@ def gather_checksums(chk: torch.Tensor, world: int) -> list:
     return torch.stack(gathered).cpu().tolist()
 
 
+def gather_floats(vals: list, world: int, device: str = "cuda") -> list:
+    """Every rank's list of floats, in rank order (NCCL all-gather, outside timed regions)."""
+    t = torch.tensor(vals, dtype=torch.float64, device=device)
+    if world == 1:
+        return [t.cpu().tolist()]
+    out = [torch.empty_like(t) for _ in range(world)]
+    torch.distributed.all_gather(out, t)
+    return [x.cpu().tolist() for x in out]
+
+
 def barrier(world: int) -> None:
     if world > 1:
         torch.distributed.barrier()
@@ -200,17 +226,36 @@ def output_checksum(codes: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
 # ------------------------------------------------------------ timing helpers
 
 
-def time_launches(fn, steps: int, stream: torch.cuda.Stream, flush: tuple | None = None):
-    """Runs fn() `steps` times on `stream`; returns (region_ms, per-launch ms list).
-    With `flush` = (buffer_a, buffer_b), both larger than L2, buffer_a is
-    rewritten and buffer_b read before every launch (outside the launch's own
-    events): the write evicts the kernel's data, the read leaves L2 holding
-    clean lines, so no write-back of the flush lands inside the timed launch."""
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+def time_region(fn, steps: int, stream: torch.cuda.Stream) -> float:
+    """Runs fn() `steps` times back to back on `stream` between ONE start and
+    ONE end event; returns the region's ms.  No event sits between launches,
+    so each launch may overlap the drain of the one ahead of it (the library's
+    programmatic dependent launch), as in an engine's stream of kernels."""
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
         # head start: keep the GPU busy (a bounded ~2 ms sleep) while the host
         # enqueues every launch, so no launch waits on the host's submission
+        torch.cuda._sleep(4_000_000)
+        start.record(stream)
+        for _ in range(steps):
+            fn()
+        end.record(stream)
+    stream.synchronize()
+    return start.elapsed_time(end)
+
+
+def time_launches(fn, steps: int, stream: torch.cuda.Stream, flush: tuple | None = None):
+    """Runs fn() `steps` times on `stream`, each launch between its own pair of
+    events; returns (region_ms, per-launch ms list).  The events between
+    launches keep a launch from overlapping the one ahead of it, so this gives
+    single-launch times.  With `flush` = (buffer_a, buffer_b, out), both
+    buffers larger than L2, buffer_a is rewritten and buffer_b read before
+    every launch (outside the launch's own events): the write evicts the
+    kernel's data, the read leaves L2 holding clean lines, so no write-back of
+    the flush lands inside the timed launch."""
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
         torch.cuda._sleep(4_000_000)
         start.record(stream)
         for a, b in ev:
@@ -241,8 +286,8 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     rows = r1 - r0
     g = torch.empty(rows, C5_N, device=dev)
     u = torch.empty(rows, C5_N, device=dev)
-    v7g.fill_normal(g, seed=12, mean=0.0, std=2.0, row0=r0)
-    v7g.fill_normal(u, seed=13, mean=0.0, std=2.0, row0=r0)
+    v7g.fill_normal(g, seed=SEED_GATE, mean=0.0, std=2.0, row0=r0)
+    v7g.fill_normal(u, seed=SEED_UP, mean=0.0, std=2.0, row0=r0)
     codes = torch.empty(rows, C5_N, dtype=torch.int8, device=dev)
     scales = torch.empty(rows, C5_N // GROUP, device=dev)
     stream = torch.cuda.Stream(device=dev)
@@ -262,7 +307,9 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         torch.cuda.synchronize()
         barrier(world)
         torch.cuda.synchronize()
-        region_ms, per_launch = time_launches(step, args.steps, stream)
+        clk.mark_start()
+        region_ms = time_region(step, args.steps, stream)
+        clk.mark_end()
         torch.cuda.synchronize()
         barrier(world)
     launches = v7g.launch_count() - launches0
@@ -270,11 +317,16 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     total_bytes = c5_bytes(C5_ROWS) * args.steps
     value = total_bytes / (t_max * 1e-3) / 1e9
     rows_per_s = C5_ROWS * args.steps / (t_max * 1e-3)
-    launch_ms = statistics.mean(per_launch)
+    launch_ms = region_ms / args.steps  # this rank's mean launch in the back-to-back region
     achieved = c5_bytes(rows) / (launch_ms * 1e-3) / 1e9
     gpu_launches = int(sum_over_ranks(launches, world))
+    # single launches (an event pair around each), outside the timed region
+    _, per_launch = time_launches(step, min(args.steps, 20), stream)
+    launch_ms_single = statistics.mean(per_launch)
 
-    # verification gather (NCCL, outside the timed region): per-rank checksums
+    # verification (outside the timed region): every code and scale of the
+    # whole job gathered to rank 0 over NCCL and compared with the oracle
+    verified = verify_outputs(codes, scales, rank, world)
     chk_all = gather_checksums(output_checksum(codes, scales), world)
 
     e2e = run_e2e(args, v7g, dev, g, u, codes, scales, rows, world)
@@ -299,13 +351,14 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         "scaling": "strong",
         "vs_baseline": None,
         "dtype": "f32",
-        "data": "synthetic: counter-based N(0, 2) gate/up (seed 12/13), generated on device per row shard",
+        "data": f"synthetic: counter-based N(0, 2) gate/up (seed {SEED_GATE}/{SEED_UP}), generated on device per row shard",
         "config": {
             "workload": "C5 SwiGLU + Q8 requantisation: gate/up [16384, 12288] fp32 -> int8 codes [16384, 12288] "
                         "+ fp32 scales [16384, 192] (one per 64-element group)",
             "rows": C5_ROWS, "n": C5_N, "rows_per_gpu": rows, "parallelism": f"row-shard x{world}, no collective",
             "bytes_per_row": c5_bytes(1), "l2": "inputs 1.61 GB > 126 MB L2: no flush needed",
             "launch_overlap": v7g.launch_overlap(),
+            "timed_region": "K launches back to back between one start and one end event (no event between launches)",
         },
         "roofline": {
             "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
@@ -313,8 +366,12 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
             "peak_kind": ("measured (MEASURED_PEAKS.json hbm_gbs, a STREAM-style copy)" if peak_kind == "measured"
                           else "fallback 6650 GB/s (MEASURED_PEAKS.json absent)"),
             "traffic": round(traffic * rows) if traffic else None, "launch_ms": round(launch_ms, 5),
+            "launch_ms_single": round(launch_ms_single, 5),
+            "launch_ms_note": "launch_ms = this rank's timed region / K (back to back); launch_ms_single = mean of "
+                              "single launches, each between its own events",
             "kernel": "k_q8_groups<true> (v7g_swiglu_q8_rows)",
         },
+        "verified": verified,
         "e2e": e2e,
         "clocks": clk.summary(),
         "gpu_launches": gpu_launches,
@@ -328,6 +385,62 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
+    if verified.get("mismatches", 1) != 0:
+        sys.exit(3)
+
+
+def verify_outputs(codes: torch.Tensor, scales: torch.Tensor, rank: int, world: int, total_rows: int = C5_ROWS,
+                   n: int = C5_N) -> dict:
+    """Every code and scale of the whole job against the oracle.  The ranks'
+    shards are gathered to every rank with one all-gather each (codes, scale
+    bits; NCCL on the GPUs, verification only, after the timed region); rank 0
+    regenerates all `total_rows` rows of gate/up on the host with the
+    generator's restatement (bit-identical to the device fill), runs the
+    oracle's SwiGLU -> Q8 and compares bit for bit.  The other ranks wait at a
+    barrier, then learn the count by a broadcast."""
+    rows = codes.shape[0]
+    shard_rows = [shard(total_rows, r, world) for r in range(world)]
+    max_rows = max(b - a for a, b in shard_rows)
+    if world > 1:
+        # equal-sized pieces for the all-gather: pad this rank's shard
+        c_pad = torch.zeros(max_rows, n, dtype=torch.int8, device=codes.device)
+        s_pad = torch.zeros(max_rows, n // GROUP, dtype=torch.int32, device=codes.device)
+        c_pad[:rows] = codes
+        s_pad[:rows] = scales.view(torch.int32)
+        c_all = torch.empty(world * max_rows, n, dtype=torch.int8, device=codes.device)
+        s_all = torch.empty(world * max_rows, n // GROUP, dtype=torch.int32, device=codes.device)
+        torch.distributed.all_gather_into_tensor(c_all, c_pad)
+        torch.distributed.all_gather_into_tensor(s_all, s_pad)
+        keep = torch.cat([torch.arange(r * max_rows, r * max_rows + (b - a), device=codes.device)
+                          for r, (a, b) in enumerate(shard_rows)])
+        c_all, s_all = c_all[keep], s_all[keep]
+    else:
+        c_all, s_all = codes, scales.view(torch.int32)
+    out = {"rows": total_rows, "ranks": world}
+    if rank == 0:
+        from oracle.pyoracle import Oracle
+        t = time.perf_counter()
+        orc = Oracle(nthreads=os.cpu_count() or 1)
+        g = orc.fill_normal(total_rows, n, 0, SEED_GATE, 0.0, 2.0)
+        u = orc.fill_normal(total_rows, n, 0, SEED_UP, 0.0, 2.0)
+        want_c, want_s = orc.swiglu_q8(g, u)
+        del g, u
+        got_c = c_all.cpu().numpy()
+        got_s = s_all.cpu().numpy()
+        bad_c = int(np.count_nonzero(got_c != want_c))
+        bad_s = int(np.count_nonzero(got_s != want_s.view(np.int32)))
+        out.update({"codes": int(got_c.size), "scales": int(got_s.size), "code_mismatches": bad_c,
+                    "scale_mismatches": bad_s, "mismatches": bad_c + bad_s,
+                    "method": "all-gather of every rank's codes and scale bits; oracle/v7_oracle.c SwiGLU -> Q8 "
+                              "on host-regenerated gate/up (orc_fill_normal, bit-identical to the device fill); "
+                              "bit-exact comparison of every element",
+                    "seconds": round(time.perf_counter() - t, 2)})
+    barrier(world)
+    if world > 1:
+        flag = torch.tensor([out.get("mismatches", 0)], dtype=torch.int64, device=codes.device)
+        torch.distributed.broadcast(flag, 0)
+        out.setdefault("mismatches", int(flag.item()))
+    return out
 
 
 def run_e2e(args, v7g, dev, g, u, codes, scales, rows, world):
@@ -375,6 +488,10 @@ def run_e2e(args, v7g, dev, g, u, codes, scales, rows, world):
     wall = (time.perf_counter() - t0) * 1e3
     t_max = max_over_ranks(ms, world)
     value = c5_bytes(C5_ROWS) * steps / (t_max * 1e-3) / 1e9
+    # the host buffers the API filled equal the device outputs of the timed region
+    same = bool(torch.equal(hc.to(dev), codes) and torch.equal(hs.to(dev).view(torch.int32), scales.view(torch.int32)))
+    same = int(sum_over_ranks(0 if same else 1, world)) == 0
+    per_rank_ms = gather_floats([ms / steps], world)
     link = host_link(dev, (hg, hu), (g, u), (hc, hs), (codes, scales), world)
     floor_ms = max(link["h2d_ms"], link["d2h_ms"])
     link["floor_ms_per_step"] = round(floor_ms, 4)
@@ -382,6 +499,8 @@ def run_e2e(args, v7g, dev, g, u, codes, scales, rows, world):
     return {"value": round(value, 2), "unit": "GB/s", "steps": steps,
             "h2d_bytes_per_step": int(C5_ROWS * C5_N * 8), "d2h_bytes_per_step": int(C5_ROWS * (C5_N + C5_N // GROUP * 4)),
             "ms_per_step": round(t_max / steps, 4), "wall_ms_per_step_rank0": round(wall / steps, 4),
+            "ms_per_step_per_rank": [round(x[0], 4) for x in per_rank_ms],
+            "outputs_match_device": same,
             "path": f"pinned host -> v7g_swiglu_q8_rows -> pinned host, {nchunks} row chunks on 3 streams",
             "link": link}
 
@@ -410,9 +529,15 @@ def host_link(dev, h_in, d_in, h_out, d_out, world, reps: int = 3) -> dict:
                     b.copy_(a, non_blocking=True)
         end.record(s)
         s.synchronize()
-        ms = max_over_ranks(start.elapsed_time(end), world) / reps
+        mine = start.elapsed_time(end) / reps
+        ranks = [x[0] for x in gather_floats([mine], world)]
+        ms = max(ranks)
         out[f"{name}_ms"] = round(ms, 4)
         out[f"{name}_gbs"] = round(nbytes / (ms * 1e-3) / 1e9, 2)
+        # every rank's own copy rate, and the whole job's (all ranks' bytes over the slowest rank's time)
+        out[f"{name}_gbs_per_rank"] = [round(nbytes / (t * 1e-3) / 1e9, 2) for t in ranks]
+        out[f"{name}_gbs_aggregate"] = round(world * nbytes / (ms * 1e-3) / 1e9, 2)
+    out["copies"] = "all ranks at once (after a barrier), pinned host buffers, one stream per rank"
     return out
 
 
@@ -585,42 +710,45 @@ def gemv_inputs(dev, n: int, d: int, both: bool = True):
     return xq, xs, gq, gs, uq, us
 
 
+def c5_host_inputs(orc, rows: int = C5_ROWS):
+    """C5 gate/up on the host: the generator's restatement, so these are the
+    GPU arm's input bytes (rows 0 .. rows - 1)."""
+    g = orc.fill_normal(rows, C5_N, 0, SEED_GATE, 0.0, 2.0)
+    u = orc.fill_normal(rows, C5_N, 0, SEED_UP, 0.0, 2.0)
+    return g, u
+
+
 def cpu_baseline(args) -> dict:
-    """The oracle port of the reference's AVX2 kernels on the host cores: the C5
-    rows (all 16384, or a calibrated sample where one pass would take longer
-    than --cpu-seconds), passes repeated until about --cpu-seconds of wall
-    time; plus one core on 1024 rows, the way the reference runs a kernel."""
+    """The oracle port of the reference's AVX2 kernels on the host cores, on the
+    GPU arm's own input bytes: whole 16384-row C5 passes into preallocated
+    outputs, repeated until about --cpu-seconds of wall time (one untimed pass
+    first); plus one core on 1024 rows, the way the reference runs a kernel."""
     from oracle.pyoracle import Oracle
     threads = os.cpu_count() or 1
     orc = Oracle(nthreads=threads)
-    rng = np.random.default_rng(0)
-    cal_rows = 64
-    g = rng.normal(0, 2, (cal_rows, C5_N)).astype(np.float32)
-    u = rng.normal(0, 2, (cal_rows, C5_N)).astype(np.float32)
-    t = time.perf_counter()
-    orc.swiglu_q8(g, u)
-    dt = max(time.perf_counter() - t, 1e-4)
-    rows = int(min(C5_ROWS, max(cal_rows, cal_rows * args.cpu_seconds / dt)))
-    g = rng.normal(0, 2, (rows, C5_N)).astype(np.float32)
-    u = rng.normal(0, 2, (rows, C5_N)).astype(np.float32)
+    g, u = c5_host_inputs(orc)
+    out = (np.empty((C5_ROWS, C5_N), np.int8), np.empty((C5_ROWS, C5_N // GROUP), np.float32))
+    orc.swiglu_q8(g, u, out=out)  # untimed: first touch of the outputs
     passes = 0
     t = time.perf_counter()
     while True:
-        orc.swiglu_q8(g, u)
+        orc.swiglu_q8(g, u, out=out)
         passes += 1
         dt = time.perf_counter() - t
         if dt >= args.cpu_seconds:
             break
-    gbs = c5_bytes(rows) * passes / dt / 1e9
+    gbs = c5_bytes(C5_ROWS) * passes / dt / 1e9
     one = Oracle(nthreads=1)
-    rows1 = min(rows, 1024)
+    rows1 = 1024
+    out1 = (out[0][:rows1], out[1][:rows1])
+    one.swiglu_q8(g[:rows1], u[:rows1], out=out1)
     t = time.perf_counter()
-    one.swiglu_q8(g[:rows1], u[:rows1])
+    one.swiglu_q8(g[:rows1], u[:rows1], out=out1)
     dt1 = time.perf_counter() - t
-    return {"value": round(gbs, 3), "unit": "GB/s", "rows_per_s": round(rows * passes / dt, 1), "cores": threads,
+    return {"value": round(gbs, 3), "unit": "GB/s", "rows_per_s": round(C5_ROWS * passes / dt, 1), "cores": threads,
             "kind": "port",
-            "sample": f"{passes} passes over {rows} of 16384 C5 rows ({dt:.1f} s), oracle/v7_oracle.c restatement, "
-                      f"{threads} threads",
+            "sample": f"{passes} passes over all 16384 C5 rows ({dt:.1f} s), oracle/v7_oracle.c restatement, "
+                      f"{threads} threads, the GPU arm's input bytes",
             "value_1_thread": round(c5_bytes(rows1) / dt1 / 1e9, 3),
             "sample_1_thread": f"{rows1} C5 rows ({dt1:.2f} s) on one core",
             "cpu_model": cpu_model()}
@@ -641,35 +769,39 @@ def cpu_model() -> str:
 
 def run_reference(args, rank: int, world: int) -> None:
     """The reference path's CPU implementation (the oracle port: the reference's
-    NASM engine cannot be assembled here), all host threads, C5, each step a
-    bounded row sample.  Rank 0 only."""
+    NASM engine cannot be assembled here) on all host threads, on the GPU arm's
+    config and input bytes: each step one whole 16384-row C5 pass into
+    preallocated outputs, as the reference's loadtest times whole calls in a
+    loop (tools/b_swiglu_q8_loadtest.cpp:134-137).  Rank 0 only."""
     if rank != 0:
         return
     from oracle.pyoracle import Oracle
     threads = os.cpu_count() or 1
     orc = Oracle(nthreads=threads)
-    rng = np.random.default_rng(0)
-    rows = min(C5_ROWS, args.ref_rows)
-    g = rng.normal(0, 2, (rows, C5_N)).astype(np.float32)
-    u = rng.normal(0, 2, (rows, C5_N)).astype(np.float32)
+    g, u = c5_host_inputs(orc)
+    out = (np.empty((C5_ROWS, C5_N), np.int8), np.empty((C5_ROWS, C5_N // GROUP), np.float32))
     for _ in range(args.warmup):
-        orc.swiglu_q8(g, u)
+        orc.swiglu_q8(g, u, out=out)
     times = []
     for _ in range(args.steps):
         t = time.perf_counter()
-        orc.swiglu_q8(g, u)
+        orc.swiglu_q8(g, u, out=out)
         times.append(time.perf_counter() - t)
     total = sum(times)
-    value = c5_bytes(rows) * args.steps / total / 1e9
+    value = c5_bytes(C5_ROWS) * args.steps / total / 1e9
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
-        "rows_per_s": round(rows * args.steps / total, 1), "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(total / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic: numpy N(0, 2) gate/up, seed 0",
-        "config": {"workload": "C5 SwiGLU + Q8 requantisation, gate/up [16384, 12288] fp32 (row sample per step)",
-                   "rows": C5_ROWS, "n": C5_N, "sample_rows_per_step": rows, "parallelism": f"{threads} host threads"},
+        "rows_per_s": round(C5_ROWS * args.steps / total, 1), "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(total / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": f"synthetic: counter-based N(0, 2) gate/up (seed {SEED_GATE}/{SEED_UP}), the GPU arm's input bytes "
+                "(generator restated on the host)",
+        "config": {"workload": "C5 SwiGLU + Q8 requantisation: gate/up [16384, 12288] fp32 -> int8 codes "
+                               "[16384, 12288] + fp32 scales [16384, 192] (one per 64-element group)",
+                   "rows": C5_ROWS, "n": C5_N, "rows_per_step": C5_ROWS, "parallelism": f"{threads} host threads"},
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": f"{rows} rows of C5 per step", "cpu_model": cpu_model()},
+                         "sample": f"all 16384 C5 rows per step, {args.steps} steps after {args.warmup} untimed",
+                         "cpu_model": cpu_model()},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference engine is NASM; nasm is absent on this image, so its restatement (oracle/v7_oracle.c) "
                 "is timed",
@@ -769,7 +901,6 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extras", action="store_true", help="skip the per-config table and the CPU baseline")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample size in seconds of work")
-    ap.add_argument("--ref-rows", type=int, default=1024, help="rows of C5 per reference-arm step")
     ap.add_argument("--profile", choices=sorted(PROFILE_CASES), help="profiling mode: launch one kernel --steps times "
                     "on a --rows-row case and exit (for ncu captures)")
     ap.add_argument("--rows", type=int, default=2048, help="rows of the --profile case")

@@ -219,7 +219,10 @@ const char *v7g_version(void);
 
 /* Deterministic synthetic input: dst[r, j] ~ N(mean, std) for r in [0, rows),
    j in [0, n), generated from (seed, row0 + r, j) alone, so any row shard of a
-   larger matrix is reproducible independently on any device. */
+   larger matrix is reproducible independently on any device.  Box-Muller over
+   a SplitMix64 counter hash, evaluated with correctly rounded IEEE operations
+   only (no math-library calls), so a host program doing the same operations
+   reproduces every value bit for bit. */
 int v7g_fill_normal(float *dst, int64_t rows, int64_t n, int64_t row0, uint64_t seed, float mean, float std, void *stream);
 
 #ifdef __cplusplus

@@ -50,6 +50,7 @@ class Oracle:
             "orc_rmsnorm_quantize_rows": [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_float, c_int],
             "orc_rope_only_rows": [c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p, c_int64, c_int, c_int],
             "orc_rope_freqs": [c_void_p, c_int, c_float, c_int, c_float, c_float, c_float, c_int],
+            "orc_fill_normal": [c_void_p, c_int64, c_int64, c_int64, ctypes.c_uint64, c_float, c_float, c_int],
             "orc_rope_tables": [c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_void_p, c_int],
             "orc_q8_gemv": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_int],
             "orc_q8_fused_gemv": [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_int],
@@ -121,14 +122,30 @@ class Oracle:
         self._ok(self.lib.orc_quantize_rows(_ptr(q), _ptr(s), _ptr(x2), rows, n, self.nthreads), "quantize")
         return q, s
 
-    def swiglu_q8(self, g: np.ndarray, u: np.ndarray):
+    def swiglu_q8(self, g: np.ndarray, u: np.ndarray, out: tuple[np.ndarray, np.ndarray] | None = None):
+        """SwiGLU then Q8 per row -> (codes int8 [rows, n], scales [rows, n/64]);
+        `out` = preallocated (codes, scales) to write instead."""
         g = np.ascontiguousarray(g, np.float32)
         u = np.ascontiguousarray(u, np.float32)
         rows, n = g.reshape(-1, g.shape[-1]).shape
-        q = np.empty((rows, n), np.int8)
-        s = np.empty((rows, n // 64), np.float32)
+        if out is None:
+            q = np.empty((rows, n), np.int8)
+            s = np.empty((rows, n // 64), np.float32)
+        else:
+            q, s = out
+            assert q.shape == (rows, n) and q.dtype == np.int8 and s.shape == (rows, n // 64) and s.dtype == np.float32
         self._ok(self.lib.orc_swiglu_q8_rows(_ptr(q), _ptr(s), _ptr(g), _ptr(u), rows, n, self.nthreads), "swiglu_q8")
         return q, s
+
+    def fill_normal(self, rows: int, n: int, row0: int = 0, seed: int = 0, mean: float = 0.0, std: float = 1.0,
+                    out: np.ndarray | None = None) -> np.ndarray:
+        """The library's synthetic generator (v7g_fill_normal) on the CPU: rows
+        row0 .. row0 + rows - 1 of the N(mean, std) matrix keyed by `seed`,
+        bit-identical to the device's."""
+        o = np.empty((rows, n), np.float32) if out is None else out
+        assert o.shape == (rows, n) and o.dtype == np.float32 and o.flags["C_CONTIGUOUS"]
+        self._ok(self.lib.orc_fill_normal(_ptr(o), rows, n, row0, seed, mean, std, self.nthreads), "fill_normal")
+        return o
 
     def add_inplace(self, x: np.ndarray, y: np.ndarray) -> np.ndarray:
         out = np.array(x, np.float32, copy=True, order="C")

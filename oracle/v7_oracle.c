@@ -509,6 +509,96 @@ static float f32q8_row_dot_single(const float *x, const int8_t *wq, const float 
 
 
 /* ------------------------------------------------------------------------ */
+/* synthetic inputs: the library's counter-based N(mean, std) generator       */
+/* ------------------------------------------------------------------------ */
+
+/* A restatement of v7g_fill_normal (v7multiplikator_b200/csrc/add.cu,
+ * k_fill_normal, fill_ln, fill_cos2pi) -- not reference code: the generator of
+ * the bench's synthetic inputs, restated so that the CPU legs of the bench and
+ * the multi-GPU verification see the same input bytes as the GPU without
+ * copying them from a device.  Box-Muller from correctly rounded IEEE
+ * operations in the same order as the device code (fmaf where it fuses, one
+ * rounding per * + / otherwise; this file is built with -ffp-contract=off),
+ * so the values agree bit for bit. */
+static inline uint64_t fill_mix64(uint64_t z)
+{
+	z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+	z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+	return z ^ (z >> 31);
+}
+
+static inline float f_bits(uint32_t b)
+{
+	float f;
+	memcpy(&f, &b, 4);
+	return f;
+}
+
+static inline uint32_t bits_f(float f)
+{
+	uint32_t b;
+	memcpy(&b, &f, 4);
+	return b;
+}
+
+/* ln u for u in [2^-24, 1]: u = 2^e m, m in [sqrt(1/2), sqrt(2)), ln m = 2 atanh(s) */
+static float fill_ln(float u)
+{
+	uint32_t b = bits_f(u);
+	int e = (int)(b >> 23) - 127;
+	b = (b & 0x007fffffu) | 0x3f800000u;
+	if (b > 0x3FB504F3u) {
+		b -= 0x00800000u;
+		e += 1;
+	}
+	const float m = f_bits(b);
+	const float s = (m - 1.0f) / (m + 1.0f);
+	const float x = s * s;
+	float p = fmaf(x, f_bits(0x3E3A2E8Cu), f_bits(0x3E638E39u));
+	p = fmaf(x, p, f_bits(0x3E924925u));
+	p = fmaf(x, p, f_bits(0x3ECCCCCDu));
+	p = fmaf(x, p, f_bits(0x3F2AAAABu));
+	p = fmaf(x, p, 2.0f);
+	return fmaf((float)e, f_bits(0x3F317218u), s * p);
+}
+
+/* cos(2 pi v) for v in [0, 1): quadrant and Taylor series of cos / sin (f pi/2) */
+static float fill_cos2pi(float v)
+{
+	const float v4 = v * 4.0f;
+	const int q = (int)v4;
+	const float f = v4 - (float)q;
+	const float x = f * f;
+	float c = fmaf(x, f_bits(0xB1DB7128u), f_bits(0x34FCE9C5u));
+	c = fmaf(x, c, f_bits(0xB7D368F9u));
+	c = fmaf(x, c, f_bits(0x3A70FA83u));
+	c = fmaf(x, c, f_bits(0xBCAAE9E4u));
+	c = fmaf(x, c, f_bits(0x3E81E0F8u));
+	c = fmaf(x, c, f_bits(0xBF9DE9E6u));
+	c = fmaf(x, c, 1.0f);
+	float sn = fmaf(x, f_bits(0x33747A1Au), f_bits(0xB67183A8u));
+	sn = fmaf(x, sn, f_bits(0x39283C1Au));
+	sn = fmaf(x, sn, f_bits(0xBB996966u));
+	sn = fmaf(x, sn, f_bits(0x3DA335E3u));
+	sn = fmaf(x, sn, f_bits(0xBF255DE7u));
+	sn = fmaf(x, sn, f_bits(0x3FC90FDBu));
+	sn = f * sn;
+	return q == 0 ? c : q == 1 ? -sn : q == 2 ? -c : sn;
+}
+
+static void fill_normal_row(float *dst, int64_t row, int64_t n, uint64_t seed, float mean, float std)
+{
+	const uint64_t key = fill_mix64(seed ^ 0x9e3779b97f4a7c15ull);
+	for (int64_t c = 0; c < n; ++c) {
+		const uint64_t h = fill_mix64(key ^ fill_mix64((uint64_t)row * 0xd1b54a32d192ed03ull + (uint64_t)c));
+		const float u1 = ((float)(uint32_t)(h >> 40) + 1.0f) * 5.96046448e-08f;
+		const float u2 = (float)(uint32_t)(h & 0xffffffu) * 5.96046448e-08f;
+		const float z = sqrtf(-2.0f * fill_ln(u1)) * fill_cos2pi(u2);
+		dst[c] = mean + std * z;
+	}
+}
+
+/* ------------------------------------------------------------------------ */
 /* row-parallel driver                                                       */
 /* ------------------------------------------------------------------------ */
 
@@ -538,10 +628,13 @@ typedef struct job {
 	const int8_t *qw1, *qw2;
 	const float *sw1, *sw2;
 	int d, variant;
+	/* synthetic fill */
+	uint64_t seed;
+	float mean, std;
 } job;
 
 enum { K_RMSNORM, K_ADD_RMSNORM, K_ROPE, K_SWIGLU, K_QUANT, K_SWIGLU_Q8, K_ADD, K_RMSNORM_Q8, K_ROPE_ONLY, K_ROPE_TABLE,
-       K_Q8_GEMV, K_SWIGLU_Q8_GEMV, K_SWIGLU_F32Q8_GEMV, K_Q8_FUSED_GEMV };
+       K_Q8_GEMV, K_SWIGLU_Q8_GEMV, K_SWIGLU_F32Q8_GEMV, K_Q8_FUSED_GEMV, K_FILL_NORMAL };
 
 static void gemv_row(const job *j, int64_t r)
 {
@@ -655,6 +748,9 @@ static void run_job(job *j)
 			rmsnorm_quantize_row(j->q + r * j->n, j->sc + r * ng, j->fx + r * j->n, j->fw, j->n, j->eps);
 			break;
 		}
+		case K_FILL_NORMAL: /* rows relative to dst; pos0 = global index of row 0 */
+			fill_normal_row(j->fo + r * j->n64, j->pos0 + r, j->n64, j->seed, j->mean, j->std);
+			break;
 		}
 	}
 	_mm_setcsr(saved);
@@ -946,4 +1042,22 @@ int orc_swiglu_f32q8_gemv(float *out, const float *x, const int8_t *gq, const fl
 	j.d = d;
 	j.variant = single_row_path != 0;
 	return run_rows(&j, batch * d, nthreads);
+}
+
+int orc_fill_normal(float *dst, int64_t rows, int64_t n, int64_t row0, uint64_t seed, float mean, float std, int nthreads)
+{
+	if (rows < 0 || n < 0 || row0 < 0 || (!dst && rows && n))
+		return -1;
+	if (rows == 0 || n == 0)
+		return 0;
+	job j = { 0 };
+	j.kind = K_FILL_NORMAL;
+	j.ftz = 0;
+	j.fo = dst;
+	j.n64 = n;
+	j.pos0 = row0;
+	j.seed = seed;
+	j.mean = mean;
+	j.std = std;
+	return run_rows(&j, rows, nthreads);
 }

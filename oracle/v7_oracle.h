@@ -131,6 +131,11 @@ int orc_swiglu_q8_gemv(float *out, const int8_t *xq, const float *xs, const int8
    for the last row of an odd-sized chunk. */
 int orc_swiglu_f32q8_gemv(float *out, const float *x, const int8_t *gq, const float *gs, const int8_t *uq, const float *us, int64_t batch, int n, int d, int single_row_path, int nthreads);
 
+/* The library's synthetic-input generator v7g_fill_normal restated on the
+   CPU (not reference code): dst[r, c] ~ N(mean, std) for global row row0 + r,
+   bit-identical to the device's values for the same (seed, row, column). */
+int orc_fill_normal(float *dst, int64_t rows, int64_t n, int64_t row0, uint64_t seed, float mean, float std, int nthreads);
+
 #ifdef __cplusplus
 }
 #endif

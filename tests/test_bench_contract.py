@@ -41,13 +41,13 @@ def check_common(line: dict, steps: int, warmup: int) -> None:
 
 
 def test_reference_arm_line():
-    line = run_bench("--impl", "reference", "--steps", "3", "--warmup", "3", "--ref-rows", "16", timeout=300)
+    line = run_bench("--impl", "reference", "--steps", "3", "--warmup", "3", timeout=600)
     check_common(line, 3, 3)
     assert line["impl"] == "reference"
     cpu = line["cpu_baseline"]
     assert cpu["kind"] in ("port", "reference") and cpu["cores"] >= 1 and cpu["value"] == line["value"]
     assert line["e2e"]["value"] == line["value"] and line["e2e"]["h2d_bytes_per_step"] == 0
-    assert line["config"]["sample_rows_per_step"] == 16
+    assert line["config"]["rows_per_step"] == 16384  # the benchmark's own config, whole passes
 
 
 @pytest.mark.gpu
@@ -68,19 +68,24 @@ def test_our_arm_line():
     assert link["h2d_gbs"] > 0 and link["d2h_gbs"] > 0
     assert 0 < link["frac"] <= 1.2  # the copies alone cannot be much slower than copies + kernel
     assert line["gpu_launches"] == 5
+    v = line["verified"]
+    assert v["mismatches"] == 0 and v["codes"] == 16384 * 12288 and v["scales"] == 16384 * 192
+    assert e2e["outputs_match_device"] is True
     clk = line["clocks"]
     assert "sm_mhz" in clk and "reasons" in clk
 
 
 def test_clock_summary_tolerates_missing_readings():
     """The clock record keeps the SM clock and throttle reasons when the
-    driver does not give the memory clock, power or temperature."""
+    driver does not give the memory clock, power or temperature, and counts
+    only the samples inside the marked timed region."""
     import bench
     c = bench.ClockSampler.__new__(bench.ClockSampler)
-    c.ok, c.max_mhz, c.mem_max_mhz = True, 1965, None
-    # (sm MHz, reasons, util %, memory MHz, board W, GPU C); a utilisation of 0
-    # (NVML's window is longer than the timed region) does not drop a sample
-    c.samples = [(1965, 0x0, 80, None, 700.0, None), (1950, 0x4, 0, 3996, None, 55), (1965, 0x0, 0, 3996, 690.0, 40)]
+    c.ok, c.max_mhz, c.mem_max_mhz, c.period = True, 1965, None, 0.001
+    # (host time, sm MHz, reasons, memory MHz, board W, GPU C)
+    c.samples = [(0.5, 1000, 0x40, None, 100.0, 30), (1.0, 1965, 0x0, None, 700.0, None),
+                 (1.5, 1950, 0x4, 3996, None, 55), (2.0, 1965, 0x0, 3996, 690.0, 40), (9.0, 900, 0x8, None, None, None)]
+    c.t0, c.t1 = 0.9, 2.1
     s = c.summary()
     assert s["sm_mhz"] == 1965 and s["sm_max_mhz"] == 1965
     assert s["reasons"] == ["sw_power_cap"]

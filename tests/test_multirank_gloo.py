@@ -1,8 +1,9 @@
 """The multi-GPU host logic on CPU ranks (gloo, world size 2): row sharding,
-the max-over-ranks timing reduction, the checksum gather used for
-verification, and a rank that drops out being detected by the others instead
-of hanging them.  The per-shard compute is the oracle (CPU), so the test covers
-the partitioning and the collectives, not the kernels."""
+the max-over-ranks timing reduction, the checksum gather, the whole-job output
+verification against the oracle (with a planted mismatch), and a rank that
+drops out being detected by the others instead of hanging them.  The
+per-shard compute is the oracle (CPU), so the test covers the partitioning
+and the collectives, not the kernels."""
 from __future__ import annotations
 
 import os
@@ -52,6 +53,28 @@ def _shard_worker(rank, world, port, q):
     ref = [bench.output_checksum(torch.from_numpy(full_c[x:y]), torch.from_numpy(full_s[x:y])).tolist()
            for x, y in (bench.shard(rows, r, world) for r in range(world))]
     q.put((rank, allchk == ref, tmax, tsum))
+    dist.destroy_process_group()
+
+
+def _verify_worker(rank, world, port, q):
+    """Each rank's shard of a small SwiGLU -> Q8 job, made by the oracle on the
+    generator's inputs (the CPU stand-in for the kernel), through
+    bench.verify_outputs; then once more with one code changed on rank 1."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+    from oracle.pyoracle import Oracle
+    _init(rank, world, port)
+    rows, n = 37, 256
+    a, b = bench.shard(rows, rank, world)
+    orc = Oracle(nthreads=1)
+    g = orc.fill_normal(b - a, n, a, bench.SEED_GATE, 0.0, 2.0)
+    u = orc.fill_normal(b - a, n, a, bench.SEED_UP, 0.0, 2.0)
+    codes, scales = orc.swiglu_q8(g, u)
+    good = bench.verify_outputs(torch.from_numpy(codes), torch.from_numpy(scales), rank, world, rows, n)
+    if rank == 1:
+        codes[3, 17] = codes[3, 17] + 1 if codes[3, 17] < 127 else 126
+    bad = bench.verify_outputs(torch.from_numpy(codes), torch.from_numpy(scales), rank, world, rows, n)
+    q.put((rank, good, bad))
     dist.destroy_process_group()
 
 
@@ -111,3 +134,12 @@ def test_rank_dropout_is_detected():
     res = dict(_run(_dropout_worker, timeout=90))
     assert res[1] == "left"
     assert res[0].startswith("error"), res[0]
+
+
+def test_two_rank_verification_against_oracle():
+    res = _run(_verify_worker)
+    for rank, good, bad in res:
+        assert good["mismatches"] == 0 and bad["mismatches"] == 1, (rank, good, bad)
+    r0 = res[0]
+    assert r0[1]["codes"] == 37 * 256 and r0[1]["scales"] == 37 * 4 and r0[1]["rows"] == 37
+    assert r0[2]["code_mismatches"] == 1 and r0[2]["scale_mismatches"] == 0

@@ -42,20 +42,79 @@ __device__ __forceinline__ uint64_t mix64(uint64_t z)
 	return z ^ (z >> 31);
 }
 
+// Box-Muller from correctly rounded IEEE operations only, so that a host
+// program doing the same operations in the same order (the oracle's
+// orc_fill_normal) reproduces every value bit for bit.  The logarithm and the
+// cosine are evaluated here rather than with the math library, whose results
+// are not specified to the last bit:
+//   ln u:  u = 2^e * m with m in [sqrt(1/2), sqrt(2)); ln m = 2 atanh(s),
+//          s = (m - 1) / (m + 1), |s| < 0.172, odd series to s^11
+//          (relative error below 1e-9 before rounding);
+//   cos(2 pi v): v*4 = q + f, q the quadrant, f in [0, 1); cos and sin of
+//          f * pi/2 by their Taylor series to f^14 and f^13 (error below
+//          1e-9), the quadrant picking cos, -sin, -cos or sin.
+// The series coefficients are the float32 roundings of (-1)^k (pi/2)^2k/(2k)!,
+// (-1)^k (pi/2)^(2k+1)/(2k+1)! and 2/(2k+1).
+__device__ __forceinline__ float fill_ln(float u)
+{
+	using M = F<false>;
+	uint32_t b = __float_as_uint(u); // u in [2^-24, 1]: normal, positive
+	int e = (int)(b >> 23) - 127;
+	b = (b & 0x007fffffu) | 0x3f800000u; // m in [1, 2)
+	if (b > 0x3FB504F3u) {                 // m > sqrt(2): m / 2, e + 1
+		b -= 0x00800000u;
+		e += 1;
+	}
+	const float m = __uint_as_float(b);
+	const float s = M::div(M::sub(m, 1.0f), M::add(m, 1.0f));
+	const float x = M::mul(s, s);
+	float p = M::fma(x, __uint_as_float(0x3E3A2E8Cu), __uint_as_float(0x3E638E39u));
+	p = M::fma(x, p, __uint_as_float(0x3E924925u));
+	p = M::fma(x, p, __uint_as_float(0x3ECCCCCDu));
+	p = M::fma(x, p, __uint_as_float(0x3F2AAAABu));
+	p = M::fma(x, p, 2.0f);
+	return M::fma((float)e, __uint_as_float(0x3F317218u), M::mul(s, p));
+}
+
+__device__ __forceinline__ float fill_cos2pi(float v)
+{
+	using M = F<false>;
+	const float v4 = M::mul(v, 4.0f); // exact
+	const int q = (int)v4;             // 0..3
+	const float f = M::sub(v4, (float)q);
+	const float x = M::mul(f, f);
+	float c = M::fma(x, __uint_as_float(0xB1DB7128u), __uint_as_float(0x34FCE9C5u));
+	c = M::fma(x, c, __uint_as_float(0xB7D368F9u));
+	c = M::fma(x, c, __uint_as_float(0x3A70FA83u));
+	c = M::fma(x, c, __uint_as_float(0xBCAAE9E4u));
+	c = M::fma(x, c, __uint_as_float(0x3E81E0F8u));
+	c = M::fma(x, c, __uint_as_float(0xBF9DE9E6u));
+	c = M::fma(x, c, 1.0f);
+	float sn = M::fma(x, __uint_as_float(0x33747A1Au), __uint_as_float(0xB67183A8u));
+	sn = M::fma(x, sn, __uint_as_float(0x39283C1Au));
+	sn = M::fma(x, sn, __uint_as_float(0xBB996966u));
+	sn = M::fma(x, sn, __uint_as_float(0x3DA335E3u));
+	sn = M::fma(x, sn, __uint_as_float(0xBF255DE7u));
+	sn = M::fma(x, sn, __uint_as_float(0x3FC90FDBu));
+	sn = M::mul(f, sn);
+	return q == 0 ? c : q == 1 ? -sn : q == 2 ? -c : sn;
+}
+
 // N(mean, std) from the counter (seed, row, col) by the Box-Muller transform.
 __global__ void __launch_bounds__(kBlock) k_fill_normal(float *dst, int64_t rows, int64_t n, int64_t row0, uint64_t seed, float mean, float std)
 {
 	kernel_entry();
+	using M = F<false>;
 	const int64_t total = rows * n;
 	const int64_t stride = (int64_t)gridDim.x * kBlock;
 	const uint64_t key = mix64(seed ^ 0x9e3779b97f4a7c15ull);
 	for (int64_t i = (int64_t)blockIdx.x * kBlock + threadIdx.x; i < total; i += stride) {
 		const int64_t r = i / n, c = i - r * n;
 		const uint64_t h = mix64(key ^ mix64((uint64_t)(row0 + r) * 0xd1b54a32d192ed03ull + (uint64_t)c));
-		const float u1 = ((float)(uint32_t)(h >> 40) + 1.0f) * (1.0f / 16777216.0f); // (0, 1]
-		const float u2 = (float)(uint32_t)(h & 0xffffffu) * (1.0f / 16777216.0f);     // [0, 1)
-		const float z = sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
-		dst[i] = mean + std * z;
+		const float u1 = M::mul((float)(uint32_t)(h >> 40) + 1.0f, 5.96046448e-08f); // (0, 1], exact
+		const float u2 = M::mul((float)(uint32_t)(h & 0xffffffu), 5.96046448e-08f);  // [0, 1), exact
+		const float z = M::mul(M::sqrt(M::mul(-2.0f, fill_ln(u1))), fill_cos2pi(u2));
+		dst[i] = M::add(mean, M::mul(std, z));
 	}
 }
 
