@@ -107,14 +107,22 @@ class ClockSampler:
 
     def _run(self):
         n = self.nvml
+        k = 0
         while True:
             try:
+                # the SM clock and the reasons every sample; the slower readings
+                # that only explain them (memory clock, power, temperature)
+                # every tenth, so a short timed region still gets samples
                 t = time.perf_counter()
                 sm = n.nvmlDeviceGetClockInfo(self.h, n.NVML_CLOCK_SM)
                 reasons = n.nvmlDeviceGetCurrentClocksEventReasons(self.h)
-                self.samples.append((t, sm, reasons, self._extra(lambda: n.nvmlDeviceGetClockInfo(self.h, n.NVML_CLOCK_MEM)),
-                                     self._extra(lambda: n.nvmlDeviceGetPowerUsage(self.h) / 1000.0),
-                                     self._extra(lambda: n.nvmlDeviceGetTemperature(self.h, n.NVML_TEMPERATURE_GPU))))
+                extra = (None, None, None)
+                if k % 10 == 0:
+                    extra = (self._extra(lambda: n.nvmlDeviceGetClockInfo(self.h, n.NVML_CLOCK_MEM)),
+                             self._extra(lambda: n.nvmlDeviceGetPowerUsage(self.h) / 1000.0),
+                             self._extra(lambda: n.nvmlDeviceGetTemperature(self.h, n.NVML_TEMPERATURE_GPU)))
+                self.samples.append((t, sm, reasons) + extra)
+                k += 1
             except Exception:
                 pass
             if self._stop.wait(self.period):
@@ -154,12 +162,13 @@ class ClockSampler:
         reasons = sorted({name for _, _, r, *_ in use for name, bit in self.REASONS.items() if r & bit})
 
         def med(i):
-            v = [x[i] for x in use if x[i] is not None]
+            v = [x[i] for x in use if x[i] is not None] or [x[i] for x in self.samples if x[i] is not None]
             return statistics.median(v) if v else None
         return {"sm_mhz": med(1), "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(inside),
                 "samples_used": len(use), "mem_mhz": med(3), "mem_max_mhz": self.mem_max_mhz, "power_w": med(4),
                 "temp_c_max": max((x[5] for x in use if x[5] is not None), default=None),
-                "source": f"NVML, sampled every {self.period * 1e3:g} ms; samples = those inside the timed region"}
+                "source": f"NVML, sampled every {self.period * 1e3:g} ms (memory clock, power and temperature every "
+                          f"tenth sample); samples = those inside the timed region"}
 
 
 # ------------------------------------------------------------ distributed
@@ -296,23 +305,22 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         v7g.swiglu_q8_rows(codes, scales, g, u, stream=stream)
 
     torch.cuda.synchronize()  # inputs were written on the default stream
-    with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
-            step()
-    stream.synchronize()
-    barrier(world)
-
-    launches0 = v7g.launch_count()
-    with ClockSampler(local) as clk:
+    with ClockSampler(local) as clk:  # running from the warm-up on; summary() keeps the timed region
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                step()
+        stream.synchronize()
+        barrier(world)
+        launches0 = v7g.launch_count()
         torch.cuda.synchronize()
         barrier(world)
         torch.cuda.synchronize()
         clk.mark_start()
         region_ms = time_region(step, args.steps, stream)
         clk.mark_end()
+        launches = v7g.launch_count() - launches0
         torch.cuda.synchronize()
         barrier(world)
-    launches = v7g.launch_count() - launches0
     t_max = max_over_ranks(region_ms, world)
     total_bytes = c5_bytes(C5_ROWS) * args.steps
     value = total_bytes / (t_max * 1e-3) / 1e9

@@ -22,16 +22,19 @@ __device__ __forceinline__ float2 v7_sigmoid_x2(float g0, float g1)
 	// packed subtraction fx - (big - magic) produced different results on
 	// about a quarter of all inputs on sm_100a with CUDA 12.9
 	const float2 f = add2(fx, mul2(add2(big, splat2(-kRoundMagic)), splat2(-1.0f)));
-	// 2^i with i = bits(big) - bits(magic): the magic's low 9 bits are zero,
-	// so (i + 127) << 23 is (bits(big) << 23) + (127 << 23) modulo 2^32
-	const float2 two = make_float2(__uint_as_float((__float_as_uint(big.x) << 23) + 0x3F800000u),
-	                               __uint_as_float((__float_as_uint(big.y) << 23) + 0x3F800000u));
 	float2 p = fma2(splat2(c5), f, splat2(c4));
 	p = fma2(p, f, splat2(c3));
 	p = fma2(p, f, splat2(c2));
 	p = fma2(p, f, splat2(c1));
 	p = fma2(p, f, splat2(1.0f));
-	const float2 e = mul2(two, p);
+	// e = 2^i * p with i = bits(big) - bits(magic) by adding i to p's exponent
+	// field: the magic's low 9 bits are zero, so i << 23 is bits(big) << 23
+	// modulo 2^32.  Exact, and equal to the reference's multiply by the
+	// constructed 2^i: p = P(f) lies in [0.70, 1.42] for |f| <= 1/2 and
+	// |i| <= 116 after the clamp, so 2^i * p is a normal float, which the
+	// product computes without rounding.
+	const float2 e = make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(big.x) << 23)),
+	                             __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(big.y) << 23)));
 	return rcp_nr2(add2(e, splat2(1.0f)));
 }
 
@@ -88,6 +91,26 @@ __device__ __forceinline__ void q8_scale_fast(float wmax, float &scale, float &r
 		scale = sr.x;
 		recip = sr.y;
 	}
+}
+
+// q8_scale_fast of two finite maxima (two groups) in pair arithmetic: the
+// floor, the two-float product by 1/127 with the 2^64 rescaling of tiny
+// maxima, and the Markstein reciprocal, each component the same operations in
+// the same order as q8_scale_fast.  The product by the low constant feeds the
+// pair multiply-add only as its addend, so no contraction can remove its
+// rounding.  Checked against q8_scale for every finite maximum by
+// v7g_selftest_arith.
+__device__ __forceinline__ void q8_scale_finite2(float w0, float w1, float2 &scale, float2 &recip)
+{
+	w0 = fmaxf(w0, kQ8WmaxFloor); // no NaN here: fmaxf is MAXPS
+	w1 = fmaxf(w1, kQ8WmaxFloor);
+	const bool t0 = w0 < 8.67361738e-19f, t1 = w1 < 8.67361738e-19f; // 2^-60
+	const float2 big = mul2(make_float2(w0, w1), splat2(1.84467441e19f)); // * 2^64
+	const float2 w = make_float2(t0 ? big.x : w0, t1 ? big.y : w1);
+	const float2 q = fma2(w, splat2(kInv127Hi), mul2(w, splat2(kInv127Lo)));
+	const float2 back = mul2(q, splat2(5.42101086e-20f)); // * 2^-64
+	scale = make_float2(t0 ? back.x : q.x, t1 ? back.y : q.y);
+	recip = rcp_nr2(scale);
 }
 
 // Codes of four values whose products p = h * recip satisfy |p| < 127.5 (a

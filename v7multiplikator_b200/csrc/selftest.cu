@@ -70,6 +70,16 @@ __global__ void __launch_bounds__(kBlock) k_selftest(unsigned long long *counts)
 		const bool same_s = __float_as_uint(s_fast) == __float_as_uint(s_ref) || (s_fast != s_fast && s_ref != s_ref);
 		const bool same_r = __float_as_uint(r_fast) == __float_as_uint(r_ref) || (r_fast != r_fast && r_ref != r_ref);
 		bad[4] += !(same_s && same_r);
+		// the pair form, for every finite maximum, in either half of the pair
+		if (w <= 3.402823466e38f) {
+			const float w2 = __uint_as_float(__float_as_uint(w) ^ ((uint32_t)i * 2654435761u & 0x007fffffu));
+			float s2_ref, r2_ref;
+			q8_scale(w2, s2_ref, r2_ref);
+			float2 s2, r2;
+			q8_scale_finite2(w, w2, s2, r2);
+			bad[4] += (__float_as_uint(s2.x) != __float_as_uint(s_ref)) + (__float_as_uint(r2.x) != __float_as_uint(r_ref)) +
+			          (__float_as_uint(s2.y) != __float_as_uint(s2_ref)) + (__float_as_uint(r2.y) != __float_as_uint(r2_ref));
+		}
 	}
 	// test 5: magnitudes below 127.5 (bit patterns up to 0x42FEFFFF), both signs
 	for (uint64_t i = tid; i < 0x42ff0000ull; i += stride) {

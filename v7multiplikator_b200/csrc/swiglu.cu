@@ -50,39 +50,146 @@ __global__ void __launch_bounds__(kBlock) k_swiglu(float *out, const float *gate
 // --- A6 / A8  Q8 over flat 64-element groups (n % 64 == 0, 16-byte aligned) ---
 // A warp iteration covers 2*U consecutive groups: half-warp h takes groups
 // base + 2u + h, u < U.  The loads of the warp's next iteration are issued
-// before the current one is computed (register double buffering), so every
-// warp keeps 4U 16-byte loads in flight through its arithmetic.  SWIGLU
+// before the current one is computed (two register sets used in turn), so
+// every warp keeps 4U 16-byte loads in flight through its arithmetic.  SWIGLU
 // computes h = swiglu(a, b) in registers first (A8), otherwise h = a (A6).
+//
+// The kernel is close to its instruction-issue limit at HBM speed, so the
+// common case is kept short: per-lane pointers advance by one increment per
+// iteration (no 64-bit index arithmetic per access), full iterations carry no
+// bounds tests, one vote per iteration decides for all 2U groups whether any
+// holds an infinity or NaN, and when none does the scales come in pair
+// arithmetic and each code from one rounded product and one rounded sum
+// (|h * recip| < 127.5 there, so the reference's saturation never acts).
+// Otherwise the general path runs: the exact MAXPS tree where a NaN makes the
+// order matter, the IEEE scale for an infinite maximum, clamped codes.
+template <int U>
+struct Q8Regs {
+	float4 x[U], y[U];
+};
+
 template <bool SWIGLU, int U>
-__global__ void __launch_bounds__(kBlock) k_q8_groups(uint32_t *codes, float *scales, const float4 *a, const float4 *b, int64_t ngroups)
+__device__ __forceinline__ void q8_load(Q8Regs<U> &r, const float4 *pa, const float4 *pb)
+{
+#pragma unroll
+	for (int u = 0; u < U; ++u) {
+		r.x[u] = ld_stream4(pa + 32 * u);
+		if (SWIGLU)
+			r.y[u] = ld_stream4(pb + 32 * u);
+	}
+}
+
+// Quantises the 2U groups held in r; the group of (u, this half-warp) goes to
+// pc + 32u (codes, 16 words per group) and ps + 2u (its scale).
+template <bool SWIGLU, int U>
+__device__ __forceinline__ void q8_iteration(const Q8Regs<U> &r, uint32_t *pc, float *ps, int lane, int hl)
+{
+	float4 h[U];
+#pragma unroll
+	for (int u = 0; u < U; ++u)
+		h[u] = SWIGLU ? v7_swiglu4(r.x[u], r.y[u]) : r.x[u];
+	uint32_t m[U];
+#pragma unroll
+	for (int u = 0; u < U; ++u)
+		m[u] = max(max(abs_bits(h[u].x), abs_bits(h[u].y)), max(abs_bits(h[u].z), abs_bits(h[u].w)));
+#pragma unroll
+	for (int mask = 1; mask <= 8; mask <<= 1)
+#pragma unroll
+		for (int u = 0; u < U; ++u)
+			m[u] = max(m[u], __shfl_xor_sync(kFullMask, m[u], mask));
+	bool special = false;
+#pragma unroll
+	for (int u = 0; u < U; ++u)
+		special |= m[u] >= 0x7f800000u;
+	if (!__any_sync(kFullMask, special)) {
+		float2 scale[(U + 1) / 2], recip[(U + 1) / 2];
+#pragma unroll
+		for (int u = 0; u < U; u += 2)
+			q8_scale_finite2(__uint_as_float(m[u]), __uint_as_float(m[u + 1 < U ? u + 1 : u]), scale[u / 2], recip[u / 2]);
+#pragma unroll
+		for (int u = 0; u < U; ++u) {
+			const float rc = (u & 1) ? recip[u / 2].y : recip[u / 2].x;
+			__stcs(pc + 32 * u, q8_codes4_small(h[u], rc));
+			if (hl == 0)
+				__stcs(ps + 2 * u, (u & 1) ? scale[u / 2].y : scale[u / 2].x);
+		}
+	} else {
+		// rare (an infinity or NaN in the warp's groups)
+#pragma unroll
+		for (int u = 0; u < U; ++u) {
+			float scale, recip;
+			q8_scale_fast(group_absmax_f4(h[u], lane), scale, recip);
+			__stcs(pc + 32 * u, q8_codes4_x2(h[u], recip));
+			if (hl == 0)
+				__stcs(ps + 2 * u, scale);
+		}
+	}
+}
+
+// four CTAs per SM: at most 64 registers a thread
+template <bool SWIGLU, int U>
+__global__ void __launch_bounds__(kBlock, 4) k_q8_groups(uint32_t *codes, float *scales, const float4 *a, const float4 *b, int64_t ngroups)
 {
 	kernel_entry();
 	const int lane = threadIdx.x & 31;
 	const int half = lane >> 4;
 	const int hl = lane & 15;
 	const int64_t nwarps = ((int64_t)gridDim.x * kBlock) >> 5;
-	auto load = [&](int64_t it, float4 *x, float4 *y) {
-#pragma unroll
-		for (int u = 0; u < U; ++u) {
-			const int64_t g = 2 * U * it + 2 * u + half;
-			x[u] = y[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-			if (g < ngroups) {
-				x[u] = ld_stream4(a + g * 16 + hl);
-				if (SWIGLU)
-					y[u] = ld_stream4(b + g * 16 + hl);
-			}
+	const int64_t warp = ((int64_t)blockIdx.x * kBlock + threadIdx.x) >> 5;
+	const int64_t nfull = ngroups / (2 * U); // iterations with all 2U groups present
+	// this lane's element of its first group: group 2U*warp + half, float4 hl
+	const int64_t g0 = 2 * U * warp + half;
+	const float4 *pa = a + g0 * 16 + hl;
+	const float4 *pb = SWIGLU ? b + g0 * 16 + hl : nullptr;
+	uint32_t *pc = codes + g0 * 16 + hl;
+	float *ps = scales + g0;
+	const int64_t step = 2 * U * nwarps; // groups per sweep of all warps
+	int64_t it = warp;
+	if (it < nfull) {
+		Q8Regs<U> r0, r1;
+		q8_load<SWIGLU, U>(r0, pa, pb);
+		for (;;) {
+			// r0 holds iteration `it`
+			const bool more = it + nwarps < nfull;
+			if (more)
+				q8_load<SWIGLU, U>(r1, pa + step * 16, SWIGLU ? pb + step * 16 : nullptr);
+			q8_iteration<SWIGLU, U>(r0, pc, ps, lane, hl);
+			pa += step * 16;
+			if (SWIGLU)
+				pb += step * 16;
+			pc += step * 16;
+			ps += step;
+			it += nwarps;
+			if (!more)
+				break;
+			// r1 holds iteration `it`
+			const bool more1 = it + nwarps < nfull;
+			if (more1)
+				q8_load<SWIGLU, U>(r0, pa + step * 16, SWIGLU ? pb + step * 16 : nullptr);
+			q8_iteration<SWIGLU, U>(r1, pc, ps, lane, hl);
+			pa += step * 16;
+			if (SWIGLU)
+				pb += step * 16;
+			pc += step * 16;
+			ps += step;
+			it += nwarps;
+			if (!more1)
+				break;
 		}
-	};
-	int64_t it = ((int64_t)blockIdx.x * kBlock + threadIdx.x) >> 5;
-	float4 x[U], y[U];
-	load(it, x, y);
-	for (; 2 * U * it < ngroups; it += nwarps) {
-		float4 xn[U], yn[U];
-		load(it + nwarps, xn, yn);
-#pragma unroll
+	}
+	// the one partial iteration (fewer than 2U groups left), if any: by the
+	// warp whose turn it is, group by group with bounds tests
+	if (it == nfull && nfull * 2 * U < ngroups) {
+#pragma unroll 1
 		for (int u = 0; u < U; ++u) {
 			const int64_t g = 2 * U * it + 2 * u + half;
-			const float4 h = SWIGLU ? v7_swiglu4(x[u], y[u]) : x[u];
+			float4 x = make_float4(0.0f, 0.0f, 0.0f, 0.0f), y = x;
+			if (g < ngroups) {
+				x = ld_stream4(a + g * 16 + hl);
+				if (SWIGLU)
+					y = ld_stream4(b + g * 16 + hl);
+			}
+			const float4 h = SWIGLU ? v7_swiglu4(x, y) : x;
 			float scale, recip;
 			q8_scale_fast(group_absmax_f4(h, lane), scale, recip);
 			if (g < ngroups) {
@@ -90,11 +197,6 @@ __global__ void __launch_bounds__(kBlock) k_q8_groups(uint32_t *codes, float *sc
 				if (hl == 0)
 					__stcs(scales + g, scale);
 			}
-		}
-#pragma unroll
-		for (int u = 0; u < U; ++u) {
-			x[u] = xn[u];
-			y[u] = yn[u];
 		}
 	}
 }
