@@ -73,7 +73,7 @@ def rope_tables_for(oracle, rng, rows, half, rmd, base):
     return np.cos(th).astype(np.float32), np.sin(th).astype(np.float32)
 
 @pytest.mark.parametrize("rows,n", [(1, 32), (3, 64), (17, 96), (64, 2048), (5, 3072), (2, 8192), (7, 4096), (300, 256),
-                                    (1025, 96), (2000, 2048)])
+                                    (1025, 96), (2000, 2048), (257, 32), (777, 4096), (400, 8192), (600, 13000 // 32 * 32)])
 @pytest.mark.parametrize("eps", [0.0, 1e-6])
 def test_rmsnorm_rows(cuda, oracle, rows, n, eps):
     import v7multiplikator_b200 as v7g
@@ -120,8 +120,27 @@ def test_rmsnorm_reference_validator_cases(cuda, oracle, golden, size, seed):
 # --------------------------------------------------- fused add + RMSNorm rows
 
 
+def test_row_kernels_in_place_at_pipeline_sizes(cuda, oracle):
+    """Hundreds of rows (the shared-memory row pipeline): RMSNorm with the
+    output over its input, and fused add + RMSNorm with the output over the
+    residual (the output is the last write, as in the reference)."""
+    import v7multiplikator_b200 as v7g
+    rng = np.random.default_rng(17)
+    x = normal(rng, (600, 2048))
+    w = normal(rng, 2048, 1.0, 0.1)
+    t = dev(x)
+    v7g.rmsnorm_rows(t, t, dev(w), 1e-6)
+    assert_same_f32(host(t), oracle.rmsnorm(x, w, 1e-6))
+    r = normal(rng, (600, 2048))
+    a = normal(rng, (600, 2048), 0, 0.5)
+    rt = dev(r)
+    v7g.fused_add_rmsnorm_rows(rt, rt, dev(a), dev(w), 1e-6)
+    want_o, _ = oracle.fused_add_rmsnorm(r, a, w, 1e-6)
+    assert_same_f32(host(rt), want_o, "out over residual")
+
+
 @pytest.mark.parametrize("rows,n", [(1, 8), (3, 16), (2, 24), (5, 48), (4, 64), (33, 2048), (3, 3072), (2, 8192), (9, 40),
-                                    (1025, 40), (2000, 2048)])
+                                    (1025, 40), (2000, 2048), (513, 8), (300, 24), (700, 2056), (400, 4096), (260, 12296)])
 def test_fused_add_rmsnorm_rows(cuda, oracle, rows, n):
     import v7multiplikator_b200 as v7g
     rng = np.random.default_rng(rows * 7 + n)
@@ -341,7 +360,7 @@ def test_quantize_reference_validator_cases(cuda, golden, pattern):
 
 
 @pytest.mark.parametrize("rows,n", [(1, 64), (3, 128), (9, 2048), (2, 3072), (2, 8192), (1, 12288),
-                                    (3000, 2048), (1500, 4096), (700, 64), (300, 8192)])
+                                    (3000, 2048), (1500, 4096), (700, 64), (300, 8192), (257, 192), (500, 12288)])
 def test_rmsnorm_quantize_rows(cuda, oracle, rows, n):
     """Up to 3000 rows: codes next to a rounding tie occur a few times per
     million elements, so small row counts alone would not show a product that

@@ -42,7 +42,7 @@ KERNEL_SOURCES = ["runtime.cu", "norm.cu", "norm_q8.cu", "rope.cu", "rope_only.c
 # Explicit-PTX arithmetic elsewhere carries its own .ftz or not.
 FTZ_SOURCES = {"norm_q8.cu", "swiglu.cu", "gemv.cu", "selftest.cu"}
 HOST_SOURCES = ["abi.cpp", "rope_freqs.cpp"]
-HEADERS = ["fp.cuh", "arith.cuh", "reduce.cuh", "q8.cuh", "q8_fast.cuh", "internal.h", "launch.cuh", "pipeline.cuh"]
+HEADERS = ["fp.cuh", "arith.cuh", "reduce.cuh", "q8.cuh", "q8_fast.cuh", "internal.h", "launch.cuh", "pipeline.cuh", "rowpipe.cuh"]
 
 
 def exported_names() -> list[str]:

@@ -1072,7 +1072,10 @@ unsigned int v7g_pipeline_timeouts(void)
 		cudaGetLastError();
 		return 0xffffffffu;
 	}
-	return v;
+	const unsigned int a = v7g::norm_pipe_timeouts(), b = v7g::norm_q8_pipe_timeouts();
+	if (a == 0xffffffffu || b == 0xffffffffu)
+		return 0xffffffffu;
+	return v + a + b;
 }
 
 } // extern "C"

@@ -44,4 +44,9 @@ int resident_grid(const void *kernel, int block, size_t smem, int64_t work_block
 
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Given-up bounded waits of the row pipelines in norm.cu and norm_q8.cu
+// (0xffffffff when the count cannot be read).
+unsigned int norm_pipe_timeouts();
+unsigned int norm_q8_pipe_timeouts();
+
 } // namespace v7g

@@ -9,6 +9,7 @@
 #include "internal.h"
 #include "launch.cuh"
 #include "reduce.cuh"
+#include "rowpipe.cuh"
 
 namespace v7g {
 namespace {
@@ -154,6 +155,89 @@ __global__ void __launch_bounds__(BLOCK, MINB) k_fused_add_rmsnorm_rows(float *o
 	}
 }
 
+// --- A1 / A2 on the row pipeline (rowpipe.cuh): many rows, rows of at most
+// a few thousand floats, 16-byte aligned.  Same arithmetic in the same order
+// as the kernels above; only where the row's elements come from differs.
+template <int S>
+__global__ void __launch_bounds__(kPipeMaxWarps * 32, 1) k_rmsnorm_pipe(float *o, const float *x, const float *w, int64_t rows, int n, float eps)
+{
+	extern __shared__ __align__(128) unsigned char smem[];
+	using M = F<false>;
+	const int W = blockDim.x >> 5;
+	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+	const PipeLayout L = pipe_layout(n, 1, W, S);
+	const int64_t nw = (int64_t)gridDim.x * W;
+	const int64_t first = (int64_t)blockIdx.x * W + warp;
+	const float *const src[1] = {x};
+	WarpPipe<S, 1> p = pipe_start<S, 1>(smem, L, src, w, n, first, nw, rows);
+	const float4 *g4 = reinterpret_cast<const float4 *>(smem);
+	bool ok = pipe_wait_gamma(smem, L);
+	const int vpl = n >> 5, n4 = n >> 2;
+	const float nf = (float)n;
+	for (int64_t row = first; ok && row < rows; row += nw) {
+		float *xs = p.slot((int)(p.waited % S), 0);
+		if (!p.wait()) {
+			ok = false;
+			break;
+		}
+		// pass 1: chain l = elements l + 32k, from shared memory
+		float acc = 0.0f;
+#pragma unroll 8
+		for (int k = 0; k < vpl; ++k) {
+			const float v = xs[lane + 32 * k];
+			acc = M::fma(v, v, acc);
+		}
+		const float scale = rms_scale<false>(reduce_chains_4x8<false>(acc), nf, eps);
+		// pass 2: (x * scale) * w, float4 per lane, straight to global memory
+		const float4 *x4 = reinterpret_cast<const float4 *>(xs);
+		float4 *o4 = reinterpret_cast<float4 *>(o + row * n);
+		for (int i = lane; i < n4; i += 32) {
+			const float4 v = x4[i], g = g4[i];
+			st_stream4(o4 + i, make_float4(M::mul(M::mul(v.x, scale), g.x), M::mul(M::mul(v.y, scale), g.y), M::mul(M::mul(v.z, scale), g.z),
+			                               M::mul(M::mul(v.w, scale), g.w)));
+		}
+		__syncwarp(); // every lane is done with the slot before it is refilled
+		const int64_t next = row + S * nw;
+		if (next < rows)
+			p.issue(next, lane == 0);
+	}
+	if (!ok)
+		p.drain();
+}
+
+// Launches a row-pipeline kernel: one CTA per SM (at most one per W rows),
+// W warps as the shared-memory budget allows.  Returns V7G_ERR_UNSUPPORTED
+// when the rows are too long for two warps' slots.
+template <typename Kernel, typename... Args>
+int launch_pipe(Kernel kernel, int stages, uint64_t &smem_flag, const char *what, int64_t rows, int n, int nin, void *stream, Args... args)
+{
+	DeviceInfo dev;
+	int rc = current_device(&dev);
+	if (rc != V7G_OK)
+		return rc;
+	const int W = pipe_warps(n, nin, stages);
+	if (W == 0)
+		return V7G_ERR_UNSUPPORTED;
+	if (pipe_allow_smem(kernel, dev.device, smem_flag) != 0)
+		return V7G_ERR_UNSUPPORTED;
+	const int64_t want = (rows + W - 1) / W;
+	const int grid = (int)(want < dev.sm_count ? want : dev.sm_count);
+	const uint32_t smem = pipe_layout(n, nin, W, stages).total();
+	const cudaError_t launched = launch_kernel(kernel, grid, W * 32, smem, stream, args...);
+	return check_launch(what, launched);
+}
+
+uint64_t g_smem_rms = 0;
+// RMSNorm takes the row pipeline from 257 rows on: measured on B200 at
+// n = 2048, back to back over inputs larger than L2, against the
+// register-chunk kernel above, 2048 rows 7.9 -> 7.6 us, 4096 rows 14.6 ->
+// 12.5 us, 8192 rows 26.5 -> 23.5 us, 16384 rows 48.0 -> 47.0 us; three
+// stages beat two and four.  (The fused add on the same pipeline, two 8 KB
+// rows a slot and so only four warps per SM, was faster at 4096 rows only --
+// 25.0 -> 24.4 us -- and slower at 2048 and 8192; it keeps its
+// register-chunk kernel.)
+constexpr int kRmsPipeStages = 3;
+
 // slots per lane per chunk: as deep as 64 registers allow without spills
 constexpr int kRmsChunk = 32;
 constexpr int kAddChunk = 16;
@@ -205,6 +289,11 @@ int v7g_rmsnorm_rows(float *o, const float *x, const float *w, int64_t rows, int
 		return clear_error();
 	if (!o || !x || !w)
 		return set_error(V7G_ERR_ARG, "v7g_rmsnorm_rows: NULL pointer");
+	if (rows > kSpreadRows && aligned16(o) && aligned16(x) && aligned16(w)) {
+		const int rc = launch_pipe(k_rmsnorm_pipe<kRmsPipeStages>, kRmsPipeStages, g_smem_rms, "v7g_rmsnorm_rows", rows, n, 1, stream, o, x, w, rows, n, eps);
+		if (rc != V7G_ERR_UNSUPPORTED)
+			return rc;
+	}
 	if (rows <= kSpreadRows)
 		return launch_rows(k_rmsnorm_rows<kRmsChunkFew, 1, 32>, "v7g_rmsnorm_rows", rows, 1, 32, stream, o, x, w, rows, n, eps);
 	if (rows <= kFewRows)
@@ -232,3 +321,8 @@ int v7g_fused_add_rmsnorm_rows(float *o, float *residual, const float *add, cons
 }
 
 } // extern "C"
+
+namespace v7g {
+// Given-up waits of this unit's row pipelines (added into v7g_pipeline_timeouts).
+unsigned int norm_pipe_timeouts() { return rowpipe_timeouts_here(); }
+} // namespace v7g

@@ -5,6 +5,7 @@
 #include "launch.cuh"
 #include "q8_fast.cuh"
 #include "reduce.cuh"
+#include "rowpipe.cuh"
 
 namespace v7g {
 namespace {
@@ -71,6 +72,58 @@ __device__ __noinline__ uint2 codes8_general(float4 h0, float4 h1, float recip)
 	return make_uint2(q8_codes4_x2(h0, recip), q8_codes4_x2(h1, recip));
 }
 
+// Rows whose normalised values are all finite take a shorter path.  When the
+// row's sum of squares ss and its scale are finite, every |scale * x| is at
+// most sqrt(n) (x^2 <= ss; a few ulps of rounding aside), below 4097 for rows
+// shorter than 2^24; with every |w| below kTameGamma the products (scale * x)
+// * w are then finite too.  For such a group the MAXPS tree's result is the
+// plain maximum of the magnitudes, the scale needs no IEEE special case and
+// every code comes from the short path.  Whether gamma is tame is decided
+// once per CTA.
+constexpr float kTameGamma = 1e30f;
+
+__device__ __forceinline__ bool row_is_tame(bool gamma_tame, float ss, float scale)
+{
+	return gamma_tame && ss <= 3.402823466e38f && scale <= 3.402823466e38f; // false for inf and NaN
+}
+
+// Largest magnitude of a group of finite values held eight per lane by eight
+// consecutive lanes.
+__device__ __forceinline__ float group_absmax8_finite(const float (&h)[8])
+{
+	float m = fmaxf(fmaxf(fmaxf(fabsf(h[0]), fabsf(h[1])), fmaxf(fabsf(h[2]), fabsf(h[3]))),
+	                fmaxf(fmaxf(fabsf(h[4]), fabsf(h[5])), fmaxf(fabsf(h[6]), fabsf(h[7]))));
+	m = fmaxf(m, __shfl_xor_sync(kFullMask, m, 1));
+	m = fmaxf(m, __shfl_xor_sync(kFullMask, m, 2));
+	return fmaxf(m, __shfl_xor_sync(kFullMask, m, 4));
+}
+
+__device__ __forceinline__ void norm_h8(float (&h)[8], float4 x0, float4 x1, float4 w0, float4 w1, float2 s2)
+{
+	const float2 a = mul2(mul2(s2, make_float2(x0.x, x0.y)), make_float2(w0.x, w0.y));
+	const float2 b = mul2(mul2(s2, make_float2(x0.z, x0.w)), make_float2(w0.z, w0.w));
+	const float2 c = mul2(mul2(s2, make_float2(x1.x, x1.y)), make_float2(w1.x, w1.y));
+	const float2 d = mul2(mul2(s2, make_float2(x1.z, x1.w)), make_float2(w1.z, w1.w));
+	h[0] = a.x;
+	h[1] = a.y;
+	h[2] = b.x;
+	h[3] = b.y;
+	h[4] = c.x;
+	h[5] = c.y;
+	h[6] = d.x;
+	h[7] = d.y;
+}
+
+// Whether every |w[i]| of gamma is below kTameGamma (NaN is not), over the
+// whole CTA; every thread of the CTA must call it.
+__device__ __forceinline__ bool gamma_tame_cta(const float *w, int n)
+{
+	bool ok = true;
+	for (int i = threadIdx.x; i < n; i += blockDim.x)
+		ok = ok && fabsf(w[i]) < kTameGamma;
+	return __syncthreads_and(ok) != 0;
+}
+
 // Pass 1 accumulates the sum of squares in the chain layout (lane l: elements
 // l + 32k) in unguarded chunks of C loads.  Pass 2 re-reads the row from L2 in
 // the quantiser's layout -- four 64-element groups per warp, eight
@@ -92,6 +145,7 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) k_rmsnorm_quantize_rows(ui
 	const int ngr = n >> 6;
 	const float nf = (float)n;
 	const float4 *w4 = reinterpret_cast<const float4 *>(w);
+	const bool gtame = gamma_tame_cta(w, n);
 	for (int64_t row = ((int64_t)blockIdx.x * kBlock + threadIdx.x) >> 5; row < rows; row += nwarps) {
 		const float *xr = x + row * n + lane;
 		float acc = 0.0f;
@@ -111,11 +165,46 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) k_rmsnorm_quantize_rows(ui
 			const float v = xr[32 * k0];
 			acc = M::fma(v, v, acc);
 		}
-		const float scale = rms_scale<true>(reduce_chains_4x8<true>(acc), nf, eps);
+		const float ss = reduce_chains_4x8<true>(acc);
+		const float scale = rms_scale<true>(ss, nf, eps);
 		const float4 *x4 = reinterpret_cast<const float4 *>(x + row * n);
 		uint2 *qr = codes + row * (n >> 3);
 		float *sr = scales + row * ngr;
 		const float2 s2 = splat2(scale);
+		if (row_is_tame(gtame, ss, scale)) { // warp-uniform
+			// two rounds of four groups at a time; their scales in pair arithmetic
+			for (int j = 0; 4 * j < ngr; j += 2) {
+				float h[2][8];
+				bool live[2];
+#pragma unroll
+				for (int t = 0; t < 2; ++t) {
+					const int g = 4 * (j + t) + slot;
+					live[t] = g < ngr;
+					const int gi = live[t] ? g : 0; // past the row's last group: group 0, nothing stored
+					float4 xv[2], wv[2];
+#pragma unroll
+					for (int u = 0; u < 2; ++u) {
+						xv[u] = ld_stream4(x4 + gi * 16 + 2 * q + u);
+						wv[u] = __ldg(w4 + gi * 16 + 2 * q + u);
+					}
+					norm_h8(h[t], xv[0], xv[1], wv[0], wv[1], s2);
+				}
+				float2 gscale, recip;
+				q8_scale_finite2(group_absmax8_finite(h[0]), group_absmax8_finite(h[1]), gscale, recip);
+#pragma unroll
+				for (int t = 0; t < 2; ++t) {
+					if (!live[t])
+						continue;
+					const int g = 4 * (j + t) + slot;
+					const float r = t ? recip.y : recip.x;
+					__stcs(qr + g * 8 + q, make_uint2(q8_codes4_small(make_float4(h[t][0], h[t][1], h[t][2], h[t][3]), r),
+					                                  q8_codes4_small(make_float4(h[t][4], h[t][5], h[t][6], h[t][7]), r)));
+					if (q == 0)
+						__stcs(sr + g, t ? gscale.y : gscale.x);
+				}
+			}
+			continue;
+		}
 		auto load = [&](int j, float4 (&xv)[2], float4 (&wv)[2]) {
 			const int g = 4 * j + slot;
 #pragma unroll
@@ -166,6 +255,135 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) k_rmsnorm_quantize_rows(ui
 	}
 }
 
+// The same on the row pipeline (rowpipe.cuh): the row is in shared memory, so
+// pass 2 reads it in an order free of bank conflicts -- lane q of a group's
+// eight takes elements 4q..4q+3 and 32+4q..32+4q+3 -- and the rare group
+// that needs the exact MAXPS tree (a NaN in the warp) re-reads its elements
+// in the reference's block order (lane q: 8q..8q+7) for the tree alone.  Same
+// arithmetic in the same order as k_rmsnorm_quantize_rows.  Codes and scales
+// are written with ordinary stores (a row's codes are a quarter of its
+// bytes).  x, w 16-byte aligned; codes 4-byte aligned.
+// Stages per warp by row count (measured on B200 at n = 2048, back to back,
+// inputs larger than L2): three (eight warps per SM) up to 8192 rows -- 4096
+// rows 14.3 us with the register-chunk kernel, 13.9 with two stages, 13.3
+// with three -- and two (thirteen warps) beyond, where more warps win (16384
+// rows 36.7, 32.6 and 36.8 us).
+constexpr int64_t kRmsqThreeStageMaxRows = 8192;
+
+template <int S>
+__global__ void __launch_bounds__(kPipeMaxWarps * 32, 1) k_rmsnorm_quantize_pipe(uint32_t *codes, float *scales, const float *x, const float *w, int64_t rows, int n, float eps)
+{
+	extern __shared__ __align__(128) unsigned char smem[];
+	using M = F<true>;
+	const int W = blockDim.x >> 5;
+	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+	const int gs = lane >> 3; // group of the four the warp holds
+	const int q = lane & 7;
+	const PipeLayout L = pipe_layout(n, 1, W, S);
+	const int64_t nw = (int64_t)gridDim.x * W;
+	const int64_t first = (int64_t)blockIdx.x * W + warp;
+	const float *const src[1] = {x};
+	WarpPipe<S, 1> p = pipe_start<S, 1>(smem, L, src, w, n, first, nw, rows);
+	const float4 *w4 = reinterpret_cast<const float4 *>(smem);
+	bool ok = pipe_wait_gamma(smem, L);
+	const bool gtame = gamma_tame_cta(reinterpret_cast<const float *>(smem), n);
+	const int vpl = n >> 5, ngr = n >> 6;
+	const float nf = (float)n;
+	for (int64_t row = first; ok && row < rows; row += nw) {
+		const float *xs = p.slot((int)(p.waited % S), 0);
+		if (!p.wait()) {
+			ok = false;
+			break;
+		}
+		float acc = 0.0f;
+#pragma unroll 8
+		for (int k = 0; k < vpl; ++k) {
+			const float v = xs[lane + 32 * k];
+			acc = M::fma(v, v, acc);
+		}
+		const float ss = reduce_chains_4x8<true>(acc);
+		const float scale = rms_scale<true>(ss, nf, eps);
+		const float2 s2 = splat2(scale);
+		const float4 *x4 = reinterpret_cast<const float4 *>(xs);
+		uint32_t *qr = codes + row * (n >> 2);
+		float *sr = scales + row * ngr;
+		if (row_is_tame(gtame, ss, scale)) { // warp-uniform
+			for (int j = 0; 4 * j < ngr; j += 2) {
+				float h[2][8];
+				bool live[2];
+#pragma unroll
+				for (int t = 0; t < 2; ++t) {
+					const int g = 4 * (j + t) + gs;
+					live[t] = g < ngr;
+					const int gi = live[t] ? g : 0;
+					norm_h8(h[t], x4[gi * 16 + q], x4[gi * 16 + 8 + q], w4[gi * 16 + q], w4[gi * 16 + 8 + q], s2);
+				}
+				float2 gscale, recip;
+				q8_scale_finite2(group_absmax8_finite(h[0]), group_absmax8_finite(h[1]), gscale, recip);
+#pragma unroll
+				for (int t = 0; t < 2; ++t) {
+					if (!live[t])
+						continue;
+					const int g = 4 * (j + t) + gs;
+					const float r = t ? recip.y : recip.x;
+					__stcs(qr + g * 16 + q, q8_codes4_small(make_float4(h[t][0], h[t][1], h[t][2], h[t][3]), r));
+					__stcs(qr + g * 16 + 8 + q, q8_codes4_small(make_float4(h[t][4], h[t][5], h[t][6], h[t][7]), r));
+					if (q == 0)
+						__stcs(sr + g, t ? gscale.y : gscale.x);
+				}
+			}
+			__syncwarp(); // every lane is done with the slot before it is refilled
+			const int64_t next = row + S * nw;
+			if (next < rows)
+				p.issue(next, lane == 0);
+			continue;
+		}
+#pragma unroll 2
+		for (int j = 0; 4 * j < ngr; ++j) { // warp-uniform
+			const int g = 4 * j + gs;
+			const bool live = g < ngr;
+			const int gi = live ? g : 0; // a lane past the row's last group reads group 0, stores nothing
+			float h[8];
+			norm_h8(h, x4[gi * 16 + q], x4[gi * 16 + 8 + q], w4[gi * 16 + q], w4[gi * 16 + 8 + q], s2);
+			uint32_t mb = 0;
+#pragma unroll
+			for (int c = 0; c < 8; ++c)
+				mb = max(mb, abs_bits(h[c]));
+			mb = max(mb, __shfl_xor_sync(kFullMask, mb, 1));
+			mb = max(mb, __shfl_xor_sync(kFullMask, mb, 2));
+			mb = max(mb, __shfl_xor_sync(kFullMask, mb, 4));
+			float wmax = __uint_as_float(mb);
+			if (__any_sync(kFullMask, mb > 0x7f800000u)) {
+				// the exact tree wants lane q to hold the 8-float block q
+				float hb[8], a[8];
+				norm_h8(hb, x4[gi * 16 + 2 * q], x4[gi * 16 + 2 * q + 1], w4[gi * 16 + 2 * q], w4[gi * 16 + 2 * q + 1], s2);
+#pragma unroll
+				for (int c = 0; c < 8; ++c)
+					a[c] = __uint_as_float(abs_bits(hb[c]));
+				wmax = group_absmax8_tree(a, q);
+			}
+			float gscale, recip;
+			q8_scale_fast(wmax, gscale, recip);
+			if (live) {
+				const float4 h0 = make_float4(h[0], h[1], h[2], h[3]), h1 = make_float4(h[4], h[5], h[6], h[7]);
+				uint2 c = make_uint2(q8_codes4_small(h0, recip), q8_codes4_small(h1, recip));
+				if (mb > 0x7f7fffffu)
+					c = codes8_general(h0, h1, recip);
+				__stcs(qr + g * 16 + q, c.x);
+				__stcs(qr + g * 16 + 8 + q, c.y);
+				if (q == 0)
+					__stcs(sr + g, gscale);
+			}
+		}
+		__syncwarp(); // every lane is done with the slot before it is refilled
+		const int64_t next = row + S * nw;
+		if (next < rows)
+			p.issue(next, lane == 0);
+	}
+	if (!ok)
+		p.drain();
+}
+
 // slots per lane per pipelined chunk of the sum-of-squares pass
 constexpr int kChunk = 32;
 
@@ -184,6 +402,25 @@ int launch_rows(Kernel kernel, const char *what, int64_t rows, void *stream, Arg
 }
 
 bool row_len_ok(int n) { return n > 0 && n < (1 << 24); }
+
+uint64_t g_smem_rmsq[2] = {0, 0};
+
+template <int S>
+int launch_rmsq_pipe(int8_t *codes, float *scales, const float *x, const float *w, int64_t rows, int n, float eps, void *stream)
+{
+	DeviceInfo dev;
+	int rc = current_device(&dev);
+	if (rc != V7G_OK)
+		return rc;
+	const int W = pipe_warps(n, 1, S);
+	if (W == 0 || pipe_allow_smem(k_rmsnorm_quantize_pipe<S>, dev.device, g_smem_rmsq[S - 2]) != 0)
+		return V7G_ERR_UNSUPPORTED;
+	const int64_t want = (rows + W - 1) / W;
+	const int grid = (int)(want < dev.sm_count ? want : dev.sm_count);
+	const cudaError_t launched = launch_kernel(k_rmsnorm_quantize_pipe<S>, grid, W * 32, pipe_layout(n, 1, W, S).total(), stream,
+	                                           reinterpret_cast<uint32_t *>(codes), scales, x, w, rows, n, eps);
+	return check_launch("v7g_rmsnorm_quantize_rows", launched);
+}
 
 } // namespace
 } // namespace v7g
@@ -204,8 +441,19 @@ int v7g_rmsnorm_quantize_rows(int8_t *codes, float *scales, const float *x, cons
 		return set_error(V7G_ERR_ARG, "v7g_rmsnorm_quantize_rows: NULL pointer");
 	if ((reinterpret_cast<uintptr_t>(codes) & 7) != 0 || !aligned16(x) || !aligned16(w))
 		return set_error(V7G_ERR_ARG, "v7g_rmsnorm_quantize_rows: x and w must be 16-byte aligned, codes 8-byte aligned");
+	if (rows > 256 && aligned16(codes)) {
+		const int rc = rows <= kRmsqThreeStageMaxRows ? launch_rmsq_pipe<3>(codes, scales, x, w, rows, n, eps, stream)
+		                                              : launch_rmsq_pipe<2>(codes, scales, x, w, rows, n, eps, stream);
+		if (rc != V7G_ERR_UNSUPPORTED)
+			return rc;
+	}
 	return launch_rows(k_rmsnorm_quantize_rows<kChunk>, "v7g_rmsnorm_quantize_rows", rows, stream,
 	                   reinterpret_cast<uint2 *>(codes), scales, x, w, rows, n, eps);
 }
 
 } // extern "C"
+
+namespace v7g {
+// Given-up waits of this unit's row pipeline (added into v7g_pipeline_timeouts).
+unsigned int norm_q8_pipe_timeouts() { return rowpipe_timeouts_here(); }
+} // namespace v7g
