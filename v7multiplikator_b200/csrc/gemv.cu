@@ -142,19 +142,16 @@ __device__ __noinline__ void stage_quantized(const float *x, int n, uint32_t *sq
 					h[u] = vec ? __ldg(reinterpret_cast<const float4 *>(p)) : make_float4(__ldg(p), __ldg(p + 1), __ldg(p + 2), __ldg(p + 3));
 			}
 		}
-		float amax[U];
-		group_absmax_f4_n<U>(h, lane, amax);
+		uint32_t code[U];
+		float scale[U];
+		q8_groups_f4<U>(h, lane, code, scale); // groups past the end hold zeros: harmless
 #pragma unroll
 		for (int u = 0; u < U; ++u) {
-			if (g0 + u * step >= groups) // warp-uniform: both halves stop together
-				break;
 			const int g = g0 + u * step + half;
-			float scale, recip;
-			q8_scale_fast(amax[u], scale, recip);
 			if (g < groups) {
-				sq[g * 16 + hl] = q8_codes4_x2(h[u], recip);
+				sq[g * 16 + hl] = code[u];
 				if (hl == 0)
-					ss[g] = scale;
+					ss[g] = scale[u];
 			}
 		}
 	}
@@ -571,13 +568,17 @@ __host__ __device__ inline size_t stream_fixed(int mode, int rows_per_block, int
 	return slots + act;
 }
 
+// Consumer threads of a row block of R rows: eight a row, rounded up to whole
+// warps (the threads of rows R.. of the last warp compute nothing).
+__host__ __device__ constexpr int stream_consumers(int rows_per_block) { return (rows_per_block * kLanes + 31) / 32 * 32; }
+
 template <int MODE, bool FUSED, int R, int P, int CG>
-__global__ void __launch_bounds__(R * kLanes + 32 * P, 2) k_q8_gemv_stream(GemvArgs p, int stages, int xstaged_arg)
+__global__ void __launch_bounds__(stream_consumers(R) + 32 * P, 2) k_q8_gemv_stream(GemvArgs p, int stages, int xstaged_arg)
 {
 	kernel_entry();
 	static_assert(P >= 1 && P <= 4, "one to four producer warps");
 	constexpr int NM = MODE == 0 ? 1 : 2;
-	constexpr int kConsumers = R * kLanes;
+	constexpr int kConsumers = stream_consumers(R);
 	static_assert(CG % 16 == 0, "whole 16-group batches per chunk");
 	constexpr int kSlot = row_slot(CG);
 	constexpr int kStageBytes = NM * R * kSlot;
@@ -923,21 +924,75 @@ StreamLayout stream_layout(int mode, bool fused, int rows_per_block, int n, bool
 }
 
 // Streaming-kernel shapes, measured on B200 at the decode shapes (d = 2048
-// .. 12288): 16 rows per block everywhere (also where that leaves SMs idle:
-// a block's 16 copies per stage keep more bytes in flight per CTA than two
-// blocks of 8); four producer warps and 2 KB row copies for the one-matrix
+// .. 12288): four producer warps and 2 KB row copies for the one-matrix
 // product (it is paced by how fast copies are issued), two producer warps
 // and 1 KB copies for the two-matrix ones (their stages are twice as big).
+// Rows per block: 16, or 14 where that spreads the row blocks more evenly
+// over the SMs (launch_gemv_stream); fewer rows per block than that keep too
+// few bytes in flight per CTA.
 template <int MODE, bool FUSED>
 struct StreamShape {
-	static constexpr int R = 16;
 	static constexpr int P = MODE == 0 ? 4 : 2;
 	static constexpr int CG = MODE == 0 ? 32 : kChunkGroups;
 };
 
+// The most rows any SM streams when `nrb` row blocks of R rows are walked by
+// `grid` CTAs (CTA c takes blocks c, c + grid, ...; CTA c sits on SM
+// c % sm_count).
+int64_t busiest_sm_rows(int64_t nrb, int64_t grid, int sm_count, int rows_per_block)
+{
+	int64_t worst = 0;
+	for (int64_t sm = 0; sm < std::min<int64_t>(grid, sm_count); ++sm) {
+		int64_t blocks = 0;
+		for (int64_t c = sm; c < grid; c += sm_count)
+			blocks += (nrb - c + grid - 1) / grid;
+		worst = std::max(worst, blocks);
+	}
+	return worst * rows_per_block;
+}
+
+struct StreamPlan {
+	StreamLayout lay;
+	const void *kernel;
+	int threads;
+	dim3 grid;
+	int64_t busiest;
+};
+
+// The layout, kernel and grid of one rows-per-block choice; busiest < 0 when
+// it does not fit (or groups % 4 != 0).
+template <int MODE, bool FUSED, int R>
+int plan_stream(const char *what, const GemvArgs &a, int64_t batch, const DeviceInfo &dev, StreamPlan &plan)
+{
+	using S = StreamShape<MODE, FUSED>;
+	plan.busiest = -1;
+	const int64_t nrb = (a.d + R - 1) / R;
+	plan.lay = stream_layout(MODE, FUSED, R, a.n, aligned16(a.xf), S::CG, nrb * batch <= dev.sm_count);
+	if (plan.lay.stages < 2)
+		return V7G_OK;
+	plan.kernel = (const void *)k_q8_gemv_stream<MODE, FUSED, R, S::P, S::CG>;
+	plan.threads = stream_consumers(R) + 32 * S::P;
+	// the shared-memory ceiling of the kernel is raised once per device
+	static std::atomic<bool> raised[kMaxDevicesTracked];
+	if (dev.device >= kMaxDevicesTracked || !raised[dev.device].load(std::memory_order_relaxed)) {
+		if (cudaFuncSetAttribute(plan.kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kStreamSmemOne) != cudaSuccess)
+			return check_launch(what);
+		if (dev.device < kMaxDevicesTracked)
+			raised[dev.device].store(true, std::memory_order_relaxed);
+	}
+	int per_sm = 0;
+	if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, plan.kernel, plan.threads, plan.lay.smem) != cudaSuccess || per_sm < 1)
+		return check_launch(what);
+	const int64_t slots = std::max<int64_t>(1, (int64_t)per_sm * dev.sm_count / batch);
+	plan.grid = dim3((unsigned)std::min(nrb, slots), (unsigned)batch);
+	plan.busiest = busiest_sm_rows(nrb, plan.grid.x, dev.sm_count, R);
+	return V7G_OK;
+}
+
 // grid = the resident CTAs (split over the batch), at most one per row
-// block.  V7G_ERR_UNSUPPORTED when the layout does not fit or groups % 4 != 0,
-// for the caller to fall back.
+// block; 16 or 14 rows per block, whichever leaves the busiest SM fewer rows
+// (16 on a tie).  V7G_ERR_UNSUPPORTED when the layout does not fit or
+// groups % 4 != 0, for the caller to fall back.
 template <int MODE, bool FUSED>
 int launch_gemv_stream(const char *what, const GemvArgs &a, int64_t batch, void *stream)
 {
@@ -949,26 +1004,17 @@ int launch_gemv_stream(const char *what, const GemvArgs &a, int64_t batch, void 
 	int rc = current_device(&dev);
 	if (rc != V7G_OK)
 		return rc;
-	const int64_t nrb = (a.d + S::R - 1) / S::R;
-	const StreamLayout lay = stream_layout(MODE, FUSED, S::R, a.n, aligned16(a.xf), S::CG, nrb * batch <= dev.sm_count);
-	if (lay.stages < 2)
+	StreamPlan p16, p14;
+	if ((rc = plan_stream<MODE, FUSED, 16>(what, a, batch, dev, p16)) != V7G_OK || (rc = plan_stream<MODE, FUSED, 14>(what, a, batch, dev, p14)) != V7G_OK)
+		return rc;
+	const bool use14 = p14.busiest >= 0 && (p16.busiest < 0 || p14.busiest < p16.busiest);
+	const StreamPlan &pl = use14 ? p14 : p16;
+	if (pl.busiest < 0)
 		return V7G_ERR_UNSUPPORTED;
-	const void *kernel = (const void *)k_q8_gemv_stream<MODE, FUSED, S::R, S::P, S::CG>;
-	const int threads = S::R * kLanes + 32 * S::P;
-	// the shared-memory ceiling of the kernel is raised once per device
-	static std::atomic<bool> raised[kMaxDevicesTracked];
-	if (dev.device >= kMaxDevicesTracked || !raised[dev.device].load(std::memory_order_relaxed)) {
-		if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kStreamSmemOne) != cudaSuccess)
-			return check_launch(what);
-		if (dev.device < kMaxDevicesTracked)
-			raised[dev.device].store(true, std::memory_order_relaxed);
-	}
-	int per_sm = 0;
-	if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, lay.smem) != cudaSuccess || per_sm < 1)
-		return check_launch(what);
-	const int64_t slots = std::max<int64_t>(1, (int64_t)per_sm * dev.sm_count / batch);
-	const dim3 grid((unsigned)std::min(nrb, slots), (unsigned)batch);
-	const cudaError_t launched = launch_kernel((k_q8_gemv_stream<MODE, FUSED, S::R, S::P, S::CG>), grid, threads, lay.smem, stream, a, lay.stages, lay.xstaged ? 1 : 0);
+	const int stages = pl.lay.stages, xs = pl.lay.xstaged ? 1 : 0;
+	const cudaError_t launched =
+	    use14 ? launch_kernel((k_q8_gemv_stream<MODE, FUSED, 14, S::P, S::CG>), pl.grid, pl.threads, pl.lay.smem, stream, a, stages, xs)
+	          : launch_kernel((k_q8_gemv_stream<MODE, FUSED, 16, S::P, S::CG>), pl.grid, pl.threads, pl.lay.smem, stream, a, stages, xs);
 	return check_launch(what, launched);
 }
 

@@ -91,41 +91,6 @@ __device__ __forceinline__ float group_absmax_f4(float4 h, int lane)
 	return __uint_as_float(m);
 }
 
-// The exact tree out of line, for paths that take it rarely (all 32 lanes).
-static __device__ __noinline__ float group_absmax_f4_tree_call(float4 h, int lane) { return group_absmax_f4_tree(h, lane); }
-
-// group_absmax_f4 of U groups at once (a group per half-warp per u): the
-// shuffle rounds of all U interleave and one vote decides whether any of them
-// needs the exact tree (the tree gives the integer maximum's result wherever
-// there is no NaN, so taking it for all U changes nothing).
-template <int U>
-__device__ __forceinline__ void group_absmax_f4_n(const float4 (&h)[U], int lane, float (&out)[U])
-{
-	uint32_t m[U];
-#pragma unroll
-	for (int u = 0; u < U; ++u)
-		m[u] = max(max(abs_bits(h[u].x), abs_bits(h[u].y)), max(abs_bits(h[u].z), abs_bits(h[u].w)));
-#pragma unroll
-	for (int mask = 1; mask <= 8; mask <<= 1)
-#pragma unroll
-		for (int u = 0; u < U; ++u)
-			m[u] = max(m[u], __shfl_xor_sync(kFullMask, m[u], mask));
-	bool nan = false;
-#pragma unroll
-	for (int u = 0; u < U; ++u)
-		nan |= m[u] > 0x7f800000u;
-	if (__any_sync(kFullMask, nan)) {
-		// rare (a NaN in the warp): the tree out of line keeps this code small
-#pragma unroll 1
-		for (int u = 0; u < U; ++u)
-			out[u] = group_absmax_f4_tree_call(h[u], lane);
-	} else {
-#pragma unroll
-		for (int u = 0; u < U; ++u)
-			out[u] = __uint_as_float(m[u]);
-	}
-}
-
 // Scale and reciprocal of a group from its absmax (quantize_kernel.inc:84-88).
 __device__ __forceinline__ void q8_scale(float wmax, float &scale, float &recip)
 {

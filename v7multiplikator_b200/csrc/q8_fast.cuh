@@ -153,4 +153,53 @@ __device__ __forceinline__ uint32_t q8_codes4_x2(float4 h, float recip)
 	return pack4_low_bytes(q0, q1, q2, q3);
 }
 
+// Q8 of U groups held one per half-warp (lane L of a half: elements 4L..4L+3
+// of its group as one float4), every group with the reference's rules: codes
+// (one word per lane, four codes) and scales.  One vote decides for all of
+// the warp's groups whether any holds an infinity or a NaN; when none does,
+// the maxima are plain integer maxima of the magnitudes, the scales come in
+// pair arithmetic and each code from one rounded product and one rounded sum
+// (|h * recip| < 127.5 there, so the reference's saturation never acts);
+// otherwise the general path runs: the exact MAXPS tree (a NaN makes the
+// order matter), the IEEE scale for an infinite maximum, clamped codes.
+// Must be called by all 32 lanes.
+template <int U>
+__device__ __forceinline__ void q8_groups_f4(const float4 (&h)[U], int lane, uint32_t (&code)[U], float (&scale)[U])
+{
+	uint32_t m[U];
+#pragma unroll
+	for (int u = 0; u < U; ++u)
+		m[u] = max(max(abs_bits(h[u].x), abs_bits(h[u].y)), max(abs_bits(h[u].z), abs_bits(h[u].w)));
+#pragma unroll
+	for (int mask = 1; mask <= 8; mask <<= 1)
+#pragma unroll
+		for (int u = 0; u < U; ++u)
+			m[u] = max(m[u], __shfl_xor_sync(kFullMask, m[u], mask));
+	bool special = false;
+#pragma unroll
+	for (int u = 0; u < U; ++u)
+		special |= m[u] >= 0x7f800000u;
+	if (!__any_sync(kFullMask, special)) {
+#pragma unroll
+		for (int u = 0; u < U; u += 2) {
+			float2 sc, rc;
+			q8_scale_finite2(__uint_as_float(m[u]), __uint_as_float(m[u + 1 < U ? u + 1 : u]), sc, rc);
+			scale[u] = sc.x;
+			code[u] = q8_codes4_small(h[u], rc.x);
+			if (u + 1 < U) {
+				scale[u + 1] = sc.y;
+				code[u + 1] = q8_codes4_small(h[u + 1], rc.y);
+			}
+		}
+	} else {
+		// rare (an infinity or NaN in the warp's groups)
+#pragma unroll
+		for (int u = 0; u < U; ++u) {
+			float recip;
+			q8_scale_fast(group_absmax_f4(h[u], lane), scale[u], recip);
+			code[u] = q8_codes4_x2(h[u], recip);
+		}
+	}
+}
+
 } // namespace v7g

@@ -88,41 +88,14 @@ __device__ __forceinline__ void q8_iteration(const Q8Regs<U> &r, uint32_t *pc, f
 #pragma unroll
 	for (int u = 0; u < U; ++u)
 		h[u] = SWIGLU ? v7_swiglu4(r.x[u], r.y[u]) : r.x[u];
-	uint32_t m[U];
+	uint32_t code[U];
+	float scale[U];
+	q8_groups_f4<U>(h, lane, code, scale);
 #pragma unroll
-	for (int u = 0; u < U; ++u)
-		m[u] = max(max(abs_bits(h[u].x), abs_bits(h[u].y)), max(abs_bits(h[u].z), abs_bits(h[u].w)));
-#pragma unroll
-	for (int mask = 1; mask <= 8; mask <<= 1)
-#pragma unroll
-		for (int u = 0; u < U; ++u)
-			m[u] = max(m[u], __shfl_xor_sync(kFullMask, m[u], mask));
-	bool special = false;
-#pragma unroll
-	for (int u = 0; u < U; ++u)
-		special |= m[u] >= 0x7f800000u;
-	if (!__any_sync(kFullMask, special)) {
-		float2 scale[(U + 1) / 2], recip[(U + 1) / 2];
-#pragma unroll
-		for (int u = 0; u < U; u += 2)
-			q8_scale_finite2(__uint_as_float(m[u]), __uint_as_float(m[u + 1 < U ? u + 1 : u]), scale[u / 2], recip[u / 2]);
-#pragma unroll
-		for (int u = 0; u < U; ++u) {
-			const float rc = (u & 1) ? recip[u / 2].y : recip[u / 2].x;
-			__stcs(pc + 32 * u, q8_codes4_small(h[u], rc));
-			if (hl == 0)
-				__stcs(ps + 2 * u, (u & 1) ? scale[u / 2].y : scale[u / 2].x);
-		}
-	} else {
-		// rare (an infinity or NaN in the warp's groups)
-#pragma unroll
-		for (int u = 0; u < U; ++u) {
-			float scale, recip;
-			q8_scale_fast(group_absmax_f4(h[u], lane), scale, recip);
-			__stcs(pc + 32 * u, q8_codes4_x2(h[u], recip));
-			if (hl == 0)
-				__stcs(ps + 2 * u, scale);
-		}
+	for (int u = 0; u < U; ++u) {
+		__stcs(pc + 32 * u, code[u]);
+		if (hl == 0)
+			__stcs(ps + 2 * u, scale[u]);
 	}
 }
 
