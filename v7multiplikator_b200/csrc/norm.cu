@@ -171,7 +171,7 @@ __global__ void __launch_bounds__(kPipeMaxWarps * 32, 1) k_rmsnorm_pipe(float *o
 	const float *const src[1] = {x};
 	WarpPipe<S, 1> p = pipe_start<S, 1>(smem, L, src, w, n, first, nw, rows);
 	const float4 *g4 = reinterpret_cast<const float4 *>(smem);
-	bool ok = pipe_wait_gamma(smem, L);
+	bool ok = pipe_wait_gamma(p, smem, L, first, nw, rows);
 	const int vpl = n >> 5, n4 = n >> 2;
 	const float nf = (float)n;
 	for (int64_t row = first; ok && row < rows; row += nw) {

@@ -285,7 +285,7 @@ __global__ void __launch_bounds__(kPipeMaxWarps * 32, 1) k_rmsnorm_quantize_pipe
 	const float *const src[1] = {x};
 	WarpPipe<S, 1> p = pipe_start<S, 1>(smem, L, src, w, n, first, nw, rows);
 	const float4 *w4 = reinterpret_cast<const float4 *>(smem);
-	bool ok = pipe_wait_gamma(smem, L);
+	bool ok = pipe_wait_gamma(p, smem, L, first, nw, rows);
 	const bool gtame = gamma_tame_cta(reinterpret_cast<const float *>(smem), n);
 	const int vpl = n >> 5, ngr = n >> 6;
 	const float nf = (float)n;

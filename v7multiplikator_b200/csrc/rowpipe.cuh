@@ -113,7 +113,9 @@ struct WarpPipe {
 
 // CTA set-up shared by the row pipelines: barriers initialised, then (after
 // the wait for the kernel ahead in the stream) gamma's copy started.  Returns
-// this warp's pipe with its first S rows started.
+// this warp's pipe with its first row started; pipe_wait_gamma starts the
+// other S - 1, so that every warp's first row is queued at the copy engine
+// before any warp's second.
 template <int S, int NIN>
 __device__ __forceinline__ WarpPipe<S, NIN> pipe_start(unsigned char *smem, const PipeLayout &L, const float *const (&src)[NIN], const float *w, int64_t n,
                                                       int64_t first_row, int64_t row_step, int64_t rows)
@@ -141,17 +143,23 @@ __device__ __forceinline__ WarpPipe<S, NIN> pipe_start(unsigned char *smem, cons
 	p.slot_bytes = L.slot_bytes;
 	p.row_bytes = L.row_bytes;
 	p.n = n;
-	for (int s = 0; s < S; ++s) {
+	if (first_row < rows)
+		p.issue(first_row, lane == 0);
+	return p;
+}
+
+// Starts the warp's rows 1 .. S-1, then waits (bounded) for gamma's barrier
+// (phase 0).
+template <int S, int NIN>
+__device__ __forceinline__ bool pipe_wait_gamma(WarpPipe<S, NIN> &p, unsigned char *smem, const PipeLayout &L, int64_t first_row, int64_t row_step,
+                                                int64_t rows)
+{
+	const int lane = threadIdx.x & 31;
+	for (int s = 1; s < S; ++s) {
 		const int64_t row = first_row + s * row_step;
 		if (row < rows)
 			p.issue(row, lane == 0);
 	}
-	return p;
-}
-
-// gamma's barrier (phase 0), bounded
-__device__ __forceinline__ bool pipe_wait_gamma(unsigned char *smem, const PipeLayout &L)
-{
 	uint64_t *gbar = reinterpret_cast<uint64_t *>(smem + L.bars_off()) + L.warps * L.stages;
 	return __all_sync(0xffffffffu, mbar_wait(gbar, 0, &g_rowpipe_timeouts));
 }

@@ -8,14 +8,15 @@
 //   test 3  q8_codes4_x2 code == q8_code_bits code for all 2^32 bit patterns
 //           of p = h * recip (recip = 1, so p = h)
 //   test 4  q8_scale_fast == q8_scale (scale and reciprocal) for every normal
-//           absmax in [2^-127, 2^128) plus inf and NaN
+//           absmax in [2^-127, 2^128) plus inf and NaN; q8_scale_finite2 ==
+//           q8_scale for every finite absmax, in both halves of the pair
 //   test 5  q8_codes4_small code == q8_code_bits code for every p with
 //           |p| < 127.5 (recip = 1, so p = h)
-//   test 6  q8_codes4_small and q8_codes4_x2 == q8_code_bits of the rounded
-//           product h * recip, for 2^31 products within a few ulps of a
-//           rounding tie m + 1/2 under 2^16 reciprocals: where the product's
-//           own rounding decides the code (a fused multiply-add would not
-//           round it)
+//   test 6  q8_codes4_small and q8_codes4_x2 == q8_code_bits
+//           of the rounded product h * recip, for 2^31 products within a few
+//           ulps of a rounding tie m + 1/2 under 2^16 reciprocals: where the
+//           product's own rounding decides the code (a fused multiply-add
+//           would not round it)
 // The counts of mismatches are the kernel's output (all zero when the fast
 // forms are exact over their whole input range).
 #include "internal.h"
