@@ -697,6 +697,19 @@ def kernel_table(v7g, dev, stream, peak) -> dict:
     sets = copies(sets_for(nb), r, torch.empty(4096, 2048, dtype=torch.int8, device=dev), torch.empty(4096, 32, device=dev))
     rec("rmsnorm_quantize_4096x2048",
         [lambda t=t: v7g.rmsnorm_quantize_rows(t[1], t[2], t[0], w, 1e-6, stream=stream) for t in sets], nb, 4096, True)
+    # RMSNorm at the C2 shape (4096 rows: the shared-memory row pipeline)
+    nb = 4096 * 2048 * 8 + 2048 * 4
+    sets = copies(sets_for(nb), r, torch.empty_like(r))
+    rec("rmsnorm_4096x2048", [lambda t=t: v7g.rmsnorm_rows(t[1], t[0], w, 1e-6, stream=stream) for t in sets], nb, 4096, True)
+    del sets
+    # size-matched floors: torch's own copy_ of as many bytes (half read, half
+    # written) as the row kernels above move, timed the same way
+    for label, nbytes in (("42MB", 42_475_520), ("67MB", 67_117_056), ("134MB", 134_225_920)):
+        n = nbytes // 8 // 4 * 4
+        sets = copies(sets_for(8 * n), torch.zeros(n, device=dev), torch.empty(n, device=dev))
+        rec(f"copy_floor_{label}", [lambda t=t: t[1].copy_(t[0]) for t in sets], 8 * n, 1, True,
+            "torch copy_ of the row kernels' byte count: what a plain copy reaches at this size")
+        del sets
     return out
 
 
