@@ -89,7 +89,11 @@ __global__ void __launch_bounds__(BLOCK, MINB) k_rmsnorm_rows(float *o, const fl
 // groups from block L on; chain lane l then covers e = 8L + l + 32k.  Pass 1
 // writes the new residual as it goes; pass 2 re-reads it (L2) for the output;
 // both in unguarded chunks as in k_rmsnorm_rows.
-template <int C, int MINB = kMinBlocks, int BLOCK = kBlock>
+// VEC: pass 2 -- elementwise, so free of the chain layout -- reads the new
+// residual and gamma and writes the output as float4 (rows 16-byte aligned),
+// a quarter of the load/store instructions of 4-byte lanes; the lanes then
+// read residual values other lanes wrote in pass 1, hence the __syncwarp.
+template <int C, int MINB = kMinBlocks, int BLOCK = kBlock, bool VEC = false>
 __global__ void __launch_bounds__(BLOCK, MINB) k_fused_add_rmsnorm_rows(float *o, float *res, const float *add, const float *__restrict__ w, int64_t rows, int n, float eps)
 {
 	kernel_entry();
@@ -135,6 +139,32 @@ __global__ void __launch_bounds__(BLOCK, MINB) k_fused_add_rmsnorm_rows(float *o
 			rm[32 * k0] = sv;
 		}
 		const float scale = rms_scale<false>(reduce_chains_4x8<false>(acc), nf, eps);
+		if (VEC) {
+			__syncwarp(); // the lanes' residual stores are visible to the whole warp
+			const float4 *r4 = reinterpret_cast<const float4 *>(rr);
+			const float4 *w4 = reinterpret_cast<const float4 *>(w);
+			float4 *o4 = reinterpret_cast<float4 *>(orow);
+			const int n4 = n >> 2;
+			int i = lane;
+			for (; i + 32 * (C / 2 - 1) < n4; i += 32 * (C / 2)) {
+				float4 v[C / 2];
+#pragma unroll
+				for (int k = 0; k < C / 2; ++k)
+					v[k] = r4[i + 32 * k];
+#pragma unroll
+				for (int k = 0; k < C / 2; ++k) {
+					const float4 g = __ldg(w4 + i + 32 * k);
+					st_stream4(o4 + i + 32 * k, make_float4(M::mul(M::mul(v[k].x, scale), g.x), M::mul(M::mul(v[k].y, scale), g.y),
+					                                        M::mul(M::mul(v[k].z, scale), g.z), M::mul(M::mul(v[k].w, scale), g.w)));
+				}
+			}
+			for (; i < n4; i += 32) {
+				const float4 v = r4[i], g = __ldg(w4 + i);
+				st_stream4(o4 + i, make_float4(M::mul(M::mul(v.x, scale), g.x), M::mul(M::mul(v.y, scale), g.y), M::mul(M::mul(v.z, scale), g.z),
+				                               M::mul(M::mul(v.w, scale), g.w)));
+			}
+			continue;
+		}
 		if (left != 0 && lane < 8) {
 			for (int b = 0; b < left; ++b)
 				st_stream(orow + 8 * b + lane, M::mul(M::mul(rr[8 * b + lane], scale), __ldg(w + 8 * b + lane)));
@@ -311,12 +341,21 @@ int v7g_fused_add_rmsnorm_rows(float *o, float *residual, const float *add, cons
 		return clear_error();
 	if (!o || !residual || !add || !w)
 		return set_error(V7G_ERR_ARG, "v7g_fused_add_rmsnorm_rows: NULL pointer");
+	// pass 2 in float4 when the rows allow it
+	const bool vec = aligned16(o) && aligned16(residual) && aligned16(w) && n % 4 == 0;
 	if (rows <= kSpreadRows)
-		return launch_rows(k_fused_add_rmsnorm_rows<kAddChunkFew, 1, 32>, "v7g_fused_add_rmsnorm_rows", rows, 4, 32, stream, o, residual, add, w, rows, n,
-		                   eps);
+		return vec ? launch_rows(k_fused_add_rmsnorm_rows<kAddChunkFew, 1, 32, true>, "v7g_fused_add_rmsnorm_rows", rows, 4, 32, stream, o, residual, add, w,
+		                         rows, n, eps)
+		           : launch_rows(k_fused_add_rmsnorm_rows<kAddChunkFew, 1, 32>, "v7g_fused_add_rmsnorm_rows", rows, 4, 32, stream, o, residual, add, w, rows, n,
+		                         eps);
 	if (rows <= kFewRows)
-		return launch_rows(k_fused_add_rmsnorm_rows<kAddChunkFew, 1>, "v7g_fused_add_rmsnorm_rows", rows, 4, kBlock, stream, o, residual, add, w, rows,
-		                   n, eps);
+		return vec ? launch_rows(k_fused_add_rmsnorm_rows<kAddChunkFew, 1, kBlock, true>, "v7g_fused_add_rmsnorm_rows", rows, 4, kBlock, stream, o, residual,
+		                         add, w, rows, n, eps)
+		           : launch_rows(k_fused_add_rmsnorm_rows<kAddChunkFew, 1>, "v7g_fused_add_rmsnorm_rows", rows, 4, kBlock, stream, o, residual, add, w, rows,
+		                         n, eps);
+	if (vec)
+		return launch_rows(k_fused_add_rmsnorm_rows<kAddChunk, kMinBlocks, kBlock, true>, "v7g_fused_add_rmsnorm_rows", rows, 4, kBlock, stream, o, residual,
+		                   add, w, rows, n, eps);
 	return launch_rows(k_fused_add_rmsnorm_rows<kAddChunk>, "v7g_fused_add_rmsnorm_rows", rows, 4, kBlock, stream, o, residual, add, w, rows, n, eps);
 }
 
