@@ -51,6 +51,7 @@ class Oracle:
             "orc_rope_only_rows": [c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p, c_int64, c_int, c_int],
             "orc_rope_freqs": [c_void_p, c_int, c_float, c_int, c_float, c_float, c_float, c_int],
             "orc_fill_normal": [c_void_p, c_int64, c_int64, c_int64, ctypes.c_uint64, c_float, c_float, c_int],
+            "orc_swiglu_q8_rows_avx2": [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int],
             "orc_rope_tables": [c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_void_p, c_int],
             "orc_q8_gemv": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_int],
             "orc_q8_fused_gemv": [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_int],
@@ -135,6 +136,21 @@ class Oracle:
             q, s = out
             assert q.shape == (rows, n) and q.dtype == np.int8 and s.shape == (rows, n // 64) and s.dtype == np.float32
         self._ok(self.lib.orc_swiglu_q8_rows(_ptr(q), _ptr(s), _ptr(g), _ptr(u), rows, n, self.nthreads), "swiglu_q8")
+        return q, s
+
+    def swiglu_q8_avx2(self, g: np.ndarray, u: np.ndarray, out: tuple[np.ndarray, np.ndarray] | None = None):
+        """swiglu_q8 in AVX2 (the reference's instruction forms, eight lanes
+        at a time): identical bits, the form the CPU baseline times."""
+        g = np.ascontiguousarray(g, np.float32)
+        u = np.ascontiguousarray(u, np.float32)
+        rows, n = g.reshape(-1, g.shape[-1]).shape
+        if out is None:
+            q = np.empty((rows, n), np.int8)
+            s = np.empty((rows, n // 64), np.float32)
+        else:
+            q, s = out
+            assert q.shape == (rows, n) and q.dtype == np.int8 and s.shape == (rows, n // 64) and s.dtype == np.float32
+        self._ok(self.lib.orc_swiglu_q8_rows_avx2(_ptr(q), _ptr(s), _ptr(g), _ptr(u), rows, n, self.nthreads), "swiglu_q8_avx2")
         return q, s
 
     def fill_normal(self, rows: int, n: int, row0: int = 0, seed: int = 0, mean: float = 0.0, std: float = 1.0,

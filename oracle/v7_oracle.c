@@ -18,6 +18,7 @@
 #include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
+#include <immintrin.h>
 #include <xmmintrin.h>
 
 /* ------------------------------------------------------------------------ */
@@ -509,6 +510,82 @@ static float f32q8_row_dot_single(const float *x, const int8_t *wq, const float 
 
 
 /* ------------------------------------------------------------------------ */
+/* SwiGLU -> Q8 in AVX2, the reference's own instruction forms               */
+/* ------------------------------------------------------------------------ */
+
+/* The same operations as swiglu_v7 and quantize_group64 above, eight lanes
+ * per instruction the way the reference's AVX2 kernels run them
+ * (EVAL_SIGMOID v7_macros.inc:98-160: vxorps, vmaxps, vminps, vmulps,
+ * vroundps, vsubps, vcvttps2dq, vfmadd, vpaddd/vpslld, vmulps, vaddps,
+ * vdivps; quantize_kernel.inc:62-106: vandps, the vmaxps tree, vdivss,
+ * vmulps, vcvtps2dq, vpackssdw, vpacksswb, vpmaxsb).  The scalar versions
+ * are the readable statement and this one the fast one: the CPU baseline
+ * times it, and tests/test_oracle_props.py checks the two give identical
+ * bits (NaN, infinities and subnormals included).  Runs under the job's
+ * MXCSR (FTZ+DAZ, as the reference's dispatched workers). */
+static inline __m256 sigmoid8_v7(__m256 g)
+{
+	const __m256 sign = _mm256_castsi256_ps(_mm256_set1_epi32((int)0x80000000u));
+	__m256 t = _mm256_xor_ps(g, sign);
+	t = _mm256_max_ps(t, _mm256_set1_ps(-80.0f)); /* NaN -> -80, as x86_max(t, -80) */
+	t = _mm256_min_ps(t, _mm256_set1_ps(80.0f));
+	const __m256 fx = _mm256_mul_ps(t, _mm256_set1_ps(1.4426950408889634f));
+	const __m256 ip = _mm256_round_ps(fx, _MM_FROUND_TO_NEAREST_INT | _MM_FROUND_NO_EXC);
+	const __m256 f = _mm256_sub_ps(fx, ip);
+	const __m256i ipi = _mm256_cvttps_epi32(ip);
+	__m256 p = _mm256_fmadd_ps(_mm256_set1_ps(bits_to_float(SIG_C5)), f, _mm256_set1_ps(bits_to_float(SIG_C4)));
+	p = _mm256_fmadd_ps(p, f, _mm256_set1_ps(bits_to_float(SIG_C3)));
+	p = _mm256_fmadd_ps(p, f, _mm256_set1_ps(bits_to_float(SIG_C2)));
+	p = _mm256_fmadd_ps(p, f, _mm256_set1_ps(bits_to_float(SIG_C1)));
+	p = _mm256_fmadd_ps(p, f, _mm256_set1_ps(1.0f));
+	const __m256 two = _mm256_castsi256_ps(_mm256_slli_epi32(_mm256_add_epi32(ipi, _mm256_set1_epi32(127)), 23));
+	const __m256 d = _mm256_add_ps(_mm256_mul_ps(two, p), _mm256_set1_ps(1.0f));
+	return _mm256_div_ps(_mm256_set1_ps(1.0f), d);
+}
+
+/* One row of SwiGLU -> Q8 (n % 64 == 0): h = (sig(g) * g) * u per 64-group,
+ * then the group's scale and codes. */
+static void swiglu_q8_row_avx2(int8_t *q, float *s, const float *g, const float *u, int n)
+{
+	const __m256 absmask = _mm256_castsi256_ps(_mm256_set1_epi32(0x7fffffff));
+	const __m256i order = _mm256_setr_epi32(0, 4, 1, 5, 2, 6, 3, 7);
+	const __m256i floor127 = _mm256_set1_epi8(-127);
+	for (int grp = 0; grp < n / ORC_Q8_GS; ++grp) {
+		const float *gg = g + (int64_t)grp * ORC_Q8_GS, *uu = u + (int64_t)grp * ORC_Q8_GS;
+		__m256 h[8], a[8];
+		for (int b = 0; b < 8; ++b) {
+			const __m256 gv = _mm256_loadu_ps(gg + 8 * b);
+			h[b] = _mm256_mul_ps(_mm256_mul_ps(sigmoid8_v7(gv), gv), _mm256_loadu_ps(uu + 8 * b));
+			a[b] = _mm256_and_ps(h[b], absmask);
+		}
+		/* the MAXPS tree: blocks (0,1),(2,3) -> (01,23), (4,5),(6,7) -> (45,67), then (03,47) */
+		const __m256 m03 = _mm256_max_ps(_mm256_max_ps(a[0], a[1]), _mm256_max_ps(a[2], a[3]));
+		const __m256 m47 = _mm256_max_ps(_mm256_max_ps(a[4], a[5]), _mm256_max_ps(a[6], a[7]));
+		const __m256 m = _mm256_max_ps(m03, m47);
+		/* lanes j vs j + 4, then (0,2), (1,3), then (0,1) */
+		const __m128 v = _mm_max_ps(_mm256_castps256_ps128(m), _mm256_extractf128_ps(m, 1));
+		const __m128 w = _mm_max_ps(v, _mm_movehl_ps(v, v));
+		__m128 wmax = _mm_max_ss(w, _mm_shuffle_ps(w, w, 1));
+		wmax = _mm_max_ss(wmax, _mm_set_ss(ORC_Q8_WMAX_FLOOR));
+		const __m128 scale = _mm_div_ss(wmax, _mm_set_ss(127.0f));
+		const __m128 recip = _mm_div_ss(_mm_set_ss(1.0f), scale);
+		s[grp] = _mm_cvtss_f32(scale);
+		const __m256 r8 = _mm256_broadcastss_ps(recip);
+		__m256i c[8];
+		for (int b = 0; b < 8; ++b)
+			c[b] = _mm256_cvtps_epi32(_mm256_mul_ps(h[b], r8));
+		for (int half = 0; half < 2; ++half) {
+			const __m256i p01 = _mm256_packs_epi32(c[4 * half], c[4 * half + 1]);
+			const __m256i p23 = _mm256_packs_epi32(c[4 * half + 2], c[4 * half + 3]);
+			__m256i bytes = _mm256_packs_epi16(p01, p23);
+			bytes = _mm256_permutevar8x32_epi32(bytes, order);
+			bytes = _mm256_max_epi8(bytes, floor127);
+			_mm256_storeu_si256((__m256i *)(q + (int64_t)grp * ORC_Q8_GS + 32 * half), bytes);
+		}
+	}
+}
+
+/* ------------------------------------------------------------------------ */
 /* synthetic inputs: the library's counter-based N(mean, std) generator       */
 /* ------------------------------------------------------------------------ */
 
@@ -634,7 +711,7 @@ typedef struct job {
 } job;
 
 enum { K_RMSNORM, K_ADD_RMSNORM, K_ROPE, K_SWIGLU, K_QUANT, K_SWIGLU_Q8, K_ADD, K_RMSNORM_Q8, K_ROPE_ONLY, K_ROPE_TABLE,
-       K_Q8_GEMV, K_SWIGLU_Q8_GEMV, K_SWIGLU_F32Q8_GEMV, K_Q8_FUSED_GEMV, K_FILL_NORMAL };
+       K_Q8_GEMV, K_SWIGLU_Q8_GEMV, K_SWIGLU_F32Q8_GEMV, K_Q8_FUSED_GEMV, K_FILL_NORMAL, K_SWIGLU_Q8_AVX2 };
 
 static void gemv_row(const job *j, int64_t r)
 {
@@ -748,6 +825,9 @@ static void run_job(job *j)
 			rmsnorm_quantize_row(j->q + r * j->n, j->sc + r * ng, j->fx + r * j->n, j->fw, j->n, j->eps);
 			break;
 		}
+		case K_SWIGLU_Q8_AVX2:
+			swiglu_q8_row_avx2(j->q + r * j->n, j->sc + r * (j->n / ORC_Q8_GS), j->fx + r * j->n, j->fy + r * j->n, j->n);
+			break;
 		case K_FILL_NORMAL: /* rows relative to dst; pos0 = global index of row 0 */
 			fill_normal_row(j->fo + r * j->n64, j->pos0 + r, j->n64, j->seed, j->mean, j->std);
 			break;
@@ -1059,5 +1139,20 @@ int orc_fill_normal(float *dst, int64_t rows, int64_t n, int64_t row0, uint64_t 
 	j.seed = seed;
 	j.mean = mean;
 	j.std = std;
+	return run_rows(&j, rows, nthreads);
+}
+
+int orc_swiglu_q8_rows_avx2(int8_t *q, float *s, const float *g, const float *u, int64_t rows, int n, int nthreads)
+{
+	if (n <= 0 || n % ORC_Q8_GS != 0 || rows < 0)
+		return -1;
+	job j = { 0 };
+	j.kind = K_SWIGLU_Q8_AVX2;
+	j.ftz = 1;
+	j.q = q;
+	j.sc = s;
+	j.fx = g;
+	j.fy = u;
+	j.n = n;
 	return run_rows(&j, rows, nthreads);
 }

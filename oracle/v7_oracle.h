@@ -131,6 +131,11 @@ int orc_swiglu_q8_gemv(float *out, const int8_t *xq, const float *xs, const int8
    for the last row of an odd-sized chunk. */
 int orc_swiglu_f32q8_gemv(float *out, const float *x, const int8_t *gq, const float *gs, const int8_t *uq, const float *us, int64_t batch, int n, int d, int single_row_path, int nthreads);
 
+/* orc_swiglu_q8_rows in AVX2 (eight lanes per instruction, the reference's
+   own instruction forms): identical bits, several times faster; the CPU
+   baseline times this form.  n % 64 == 0. */
+int orc_swiglu_q8_rows_avx2(int8_t *q, float *s, const float *g, const float *u, int64_t rows, int n, int nthreads);
+
 /* The library's synthetic-input generator v7g_fill_normal restated on the
    CPU (not reference code): dst[r, c] ~ N(mean, std) for global row row0 + r,
    bit-identical to the device's values for the same (seed, row, column). */

@@ -139,6 +139,32 @@ def test_swiglu_q8_equals_quantize_of_swiglu(oracle):
     np.testing.assert_array_equal(s, s2)
 
 
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_swiglu_q8_avx2_equals_scalar(oracle, seed):
+    """The AVX2 form of SwiGLU -> Q8 (the one the CPU baseline times) gives
+    the scalar restatement's bits: ordinary N(0, 2) rows, and rows planted
+    with NaN, infinities, subnormals, huge values, signed zeros, all-zero and
+    all-subnormal groups (every position of the MAXPS tree gets a NaN)."""
+    rng = np.random.default_rng(seed)
+    rows, n = 67, 1024
+    g = rng.normal(0, 2, (rows, n)).astype(np.float32)
+    u = rng.normal(0, 2, (rows, n)).astype(np.float32)
+    specials = np.array([np.nan, np.inf, -np.inf, 1e-40, -1e-42, 3e38, -3e38, 0.0, -0.0, 85.0, -85.0, 1e-30], np.float32)
+    for arr in (g, u):
+        flat = arr.reshape(-1)
+        idx = rng.choice(flat.size, flat.size // 50, replace=False)
+        flat[idx] = specials[rng.integers(0, specials.size, idx.size)]
+    g[3, :64] = 0.0
+    u[3, :64] = 0.0
+    g[4, 64:128] = 1e-40
+    for pos in range(64):  # a NaN at every position of a group, one group each (rows 5..8)
+        g[5 + pos // 16, 64 * (pos % 16) + pos] = np.nan
+    q_a, s_a = oracle.swiglu_q8_avx2(g, u)
+    q_s, s_s = oracle.swiglu_q8(g, u)
+    assert np.array_equal(q_a, q_s)
+    assert np.array_equal(s_a.view(np.uint32), s_s.view(np.uint32))
+
+
 def test_swiglu_vs_float64(oracle):
     rng = np.random.default_rng(2)
     g = rng.normal(0, 2, 100000).astype(F)
