@@ -245,7 +245,7 @@ int launch_pipe(Kernel kernel, int stages, uint64_t &smem_flag, const char *what
 	int rc = current_device(&dev);
 	if (rc != V7G_OK)
 		return rc;
-	const int W = pipe_warps(n, nin, stages);
+	const int W = pipe_warps_for(n, nin, stages, rows, dev.sm_count);
 	if (W == 0)
 		return V7G_ERR_UNSUPPORTED;
 	if (pipe_allow_smem(kernel, dev.device, smem_flag) != 0)

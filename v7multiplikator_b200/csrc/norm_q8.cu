@@ -263,12 +263,13 @@ __global__ void __launch_bounds__(kBlock, kMinBlocks) k_rmsnorm_quantize_rows(ui
 // arithmetic in the same order as k_rmsnorm_quantize_rows.  Codes and scales
 // are written with ordinary stores (a row's codes are a quarter of its
 // bytes).  x, w 16-byte aligned; codes 4-byte aligned.
-// Stages per warp by row count (measured on B200 at n = 2048, back to back,
-// inputs larger than L2): three (eight warps per SM) up to 8192 rows -- 4096
-// rows 14.3 us with the register-chunk kernel, 13.9 with two stages, 13.3
-// with three -- and two (thirteen warps) beyond, where more warps win (16384
-// rows 36.7, 32.6 and 36.8 us).
-constexpr int64_t kRmsqThreeStageMaxRows = 8192;
+// One slot per warp, so that sixteen warps fit beside the slots: the
+// quantiser pass is latency-bound, and more warps hide more of it than more
+// rows in flight per warp do.  Measured on B200 at n = 2048, back to back,
+// inputs larger than L2 (2048 / 4096 / 16384 rows): one slot and 16 warps 6.95
+// / 11.3 / 32.5 us, three slots and 8 warps 8.6 / 13.0 / 32.4 us, two slots and
+// 13 warps 8.5 / 13.9 / 32.4 us, one slot and 20 warps 7.3 / 12.0 / 32.1 us.
+constexpr int kRmsqPipeStages = 1;
 
 template <int S>
 __global__ void __launch_bounds__(kPipeMaxWarps * 32, 1) k_rmsnorm_quantize_pipe(uint32_t *codes, float *scales, const float *x, const float *w, int64_t rows, int n, float eps)
@@ -403,7 +404,7 @@ int launch_rows(Kernel kernel, const char *what, int64_t rows, void *stream, Arg
 
 bool row_len_ok(int n) { return n > 0 && n < (1 << 24); }
 
-uint64_t g_smem_rmsq[2] = {0, 0};
+uint64_t g_smem_rmsq = 0;
 
 template <int S>
 int launch_rmsq_pipe(int8_t *codes, float *scales, const float *x, const float *w, int64_t rows, int n, float eps, void *stream)
@@ -412,8 +413,8 @@ int launch_rmsq_pipe(int8_t *codes, float *scales, const float *x, const float *
 	int rc = current_device(&dev);
 	if (rc != V7G_OK)
 		return rc;
-	const int W = pipe_warps(n, 1, S);
-	if (W == 0 || pipe_allow_smem(k_rmsnorm_quantize_pipe<S>, dev.device, g_smem_rmsq[S - 2]) != 0)
+	const int W = pipe_warps_for(n, 1, S, rows, dev.sm_count);
+	if (W == 0 || pipe_allow_smem(k_rmsnorm_quantize_pipe<S>, dev.device, g_smem_rmsq) != 0)
 		return V7G_ERR_UNSUPPORTED;
 	const int64_t want = (rows + W - 1) / W;
 	const int grid = (int)(want < dev.sm_count ? want : dev.sm_count);
@@ -442,8 +443,7 @@ int v7g_rmsnorm_quantize_rows(int8_t *codes, float *scales, const float *x, cons
 	if ((reinterpret_cast<uintptr_t>(codes) & 7) != 0 || !aligned16(x) || !aligned16(w))
 		return set_error(V7G_ERR_ARG, "v7g_rmsnorm_quantize_rows: x and w must be 16-byte aligned, codes 8-byte aligned");
 	if (rows > 256 && aligned16(codes)) {
-		const int rc = rows <= kRmsqThreeStageMaxRows ? launch_rmsq_pipe<3>(codes, scales, x, w, rows, n, eps, stream)
-		                                              : launch_rmsq_pipe<2>(codes, scales, x, w, rows, n, eps, stream);
+		const int rc = launch_rmsq_pipe<kRmsqPipeStages>(codes, scales, x, w, rows, n, eps, stream);
 		if (rc != V7G_ERR_UNSUPPORTED)
 			return rc;
 	}

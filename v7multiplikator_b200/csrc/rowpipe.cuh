@@ -68,6 +68,18 @@ inline int pipe_warps(int n, int nin, int stages)
 	return 0;
 }
 
+// Warps per CTA for a launch: as many as the budget allows, but no more than
+// spread the rows over every SM (a few hundred rows in CTAs of 16 warps
+// would leave most SMs idle); 0 when the rows are too long for two warps.
+inline int pipe_warps_for(int n, int nin, int stages, int64_t rows, int sm_count)
+{
+	const int w = pipe_warps(n, nin, stages);
+	if (w == 0)
+		return 0;
+	const int64_t spread = (rows + sm_count - 1) / sm_count;
+	return (int)(spread < w ? (spread < 1 ? 1 : spread) : w);
+}
+
 // One warp's slots.  issue() is called by one lane.
 template <int S, int NIN>
 struct WarpPipe {
