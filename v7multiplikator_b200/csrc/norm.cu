@@ -263,9 +263,11 @@ uint64_t g_smem_rms = 0;
 // register-chunk kernel above, 2048 rows 7.9 -> 7.6 us, 4096 rows 14.6 ->
 // 12.5 us, 8192 rows 26.5 -> 23.5 us, 16384 rows 48.0 -> 47.0 us; three
 // stages beat two and four.  (The fused add on the same pipeline, two 8 KB
-// rows a slot and so only four warps per SM, was faster at 4096 rows only --
-// 25.0 -> 24.4 us -- and slower at 2048 and 8192; it keeps its
-// register-chunk kernel.)
+// rows a slot: with three slots and four warps per SM faster at 4096 rows
+// only -- 25.0 -> 24.4 us -- and slower at 2048 and 8192; with one slot and
+// 13 warps slower still against the register-chunk kernel with its float4
+// pass 2 -- 4096 rows 24.6 -> 25.8 us, 2048 rows 12.5 -> 16.3 us; it keeps
+// the register-chunk kernel.)
 constexpr int kRmsPipeStages = 3;
 
 // slots per lane per chunk: as deep as 64 registers allow without spills
