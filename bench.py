@@ -105,26 +105,41 @@ class ClockSampler:
         self._stop = threading.Event()
         self._t = None
 
-    def _run(self):
+    def sample(self, full: bool = False) -> None:
+        """One reading: the SM clock and the reasons; with `full` also the
+        slower readings that only explain them (memory clock, power,
+        temperature)."""
         n = self.nvml
+        try:
+            t = time.perf_counter()
+            sm = n.nvmlDeviceGetClockInfo(self.h, n.NVML_CLOCK_SM)
+            reasons = n.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            extra = (None, None, None)
+            if full:
+                extra = (self._extra(lambda: n.nvmlDeviceGetClockInfo(self.h, n.NVML_CLOCK_MEM)),
+                         self._extra(lambda: n.nvmlDeviceGetPowerUsage(self.h) / 1000.0),
+                         self._extra(lambda: n.nvmlDeviceGetTemperature(self.h, n.NVML_TEMPERATURE_GPU)))
+            self.samples.append((t, sm, reasons) + extra)
+        except Exception:
+            pass
+
+    def sample_until(self, event: "torch.cuda.Event") -> None:
+        """Samples from the calling thread until `event` has completed on the
+        device: called with the timed region's launches queued, so every
+        reading falls inside the region however short it is."""
+        if not self.ok:
+            return
+        k = 0
+        while not event.query():
+            self.sample(full=k % 10 == 0)
+            k += 1
+
+    def _run(self):
         k = 0
         while True:
-            try:
-                # the SM clock and the reasons every sample; the slower readings
-                # that only explain them (memory clock, power, temperature)
-                # every tenth, so a short timed region still gets samples
-                t = time.perf_counter()
-                sm = n.nvmlDeviceGetClockInfo(self.h, n.NVML_CLOCK_SM)
-                reasons = n.nvmlDeviceGetCurrentClocksEventReasons(self.h)
-                extra = (None, None, None)
-                if k % 10 == 0:
-                    extra = (self._extra(lambda: n.nvmlDeviceGetClockInfo(self.h, n.NVML_CLOCK_MEM)),
-                             self._extra(lambda: n.nvmlDeviceGetPowerUsage(self.h) / 1000.0),
-                             self._extra(lambda: n.nvmlDeviceGetTemperature(self.h, n.NVML_TEMPERATURE_GPU)))
-                self.samples.append((t, sm, reasons) + extra)
-                k += 1
-            except Exception:
-                pass
+            # every tenth sample with the slower readings
+            self.sample(full=k % 10 == 0)
+            k += 1
             if self._stop.wait(self.period):
                 break
 
@@ -167,8 +182,9 @@ class ClockSampler:
         return {"sm_mhz": med(1), "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(inside),
                 "samples_used": len(use), "mem_mhz": med(3), "mem_max_mhz": self.mem_max_mhz, "power_w": med(4),
                 "temp_c_max": max((x[5] for x in use if x[5] is not None), default=None),
-                "source": f"NVML, sampled every {self.period * 1e3:g} ms (memory clock, power and temperature every "
-                          f"tenth sample); samples = those inside the timed region"}
+                "source": f"NVML: a background thread every {self.period * 1e3:g} ms, and back-to-back readings from the "
+                          f"launching thread while the queued timed region runs (memory clock, power and temperature every "
+                          f"tenth reading); samples = those inside the timed region"}
 
 
 # ------------------------------------------------------------ distributed
@@ -235,11 +251,13 @@ def output_checksum(codes: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
 # ------------------------------------------------------------ timing helpers
 
 
-def time_region(fn, steps: int, stream: torch.cuda.Stream) -> float:
+def time_region(fn, steps: int, stream: torch.cuda.Stream, clk: "ClockSampler | None" = None) -> float:
     """Runs fn() `steps` times back to back on `stream` between ONE start and
     ONE end event; returns the region's ms.  No event sits between launches,
     so each launch may overlap the drain of the one ahead of it (the library's
-    programmatic dependent launch), as in an engine's stream of kernels."""
+    programmatic dependent launch), as in an engine's stream of kernels.
+    With `clk`, the clocks are sampled from this thread while the queued
+    region runs."""
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
         # head start: keep the GPU busy (a bounded ~2 ms sleep) while the host
@@ -249,6 +267,8 @@ def time_region(fn, steps: int, stream: torch.cuda.Stream) -> float:
         for _ in range(steps):
             fn()
         end.record(stream)
+    if clk is not None:
+        clk.sample_until(end)
     stream.synchronize()
     return start.elapsed_time(end)
 
@@ -316,7 +336,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         barrier(world)
         torch.cuda.synchronize()
         clk.mark_start()
-        region_ms = time_region(step, args.steps, stream)
+        region_ms = time_region(step, args.steps, stream, clk)
         clk.mark_end()
         launches = v7g.launch_count() - launches0
         torch.cuda.synchronize()

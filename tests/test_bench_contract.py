@@ -73,6 +73,7 @@ def test_our_arm_line():
     assert e2e["outputs_match_device"] is True
     clk = line["clocks"]
     assert "sm_mhz" in clk and "reasons" in clk
+    assert clk["samples"] >= 1  # readings taken while the queued timed region runs
 
 
 def test_clock_summary_tolerates_missing_readings():
