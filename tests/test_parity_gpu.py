@@ -408,6 +408,83 @@ def test_rmsnorm_quantize_specials_at_every_group_position(cuda, oracle):
         assert_same_f32(host(scales), ws, f"position {p}")
 
 
+@pytest.mark.parametrize("eps", [0.0, 1e-6])
+def test_rmsnorm_pipeline_special_rows(cuda, oracle, eps):
+    """The RMSNorm row pipeline (600 rows) on rows with NaN, infinities, an
+    overflowing sum of squares, all zeros, subnormals (no FTZ here) and a
+    huge value, among ordinary rows."""
+    import v7multiplikator_b200 as v7g
+    rng = np.random.default_rng(91)
+    rows, n = 600, 2048
+    x = normal(rng, (rows, n))
+    x[1, 17] = np.nan
+    x[2, 1000] = np.inf
+    x[3, 5] = -np.inf
+    x[4] = 0.0
+    x[5] = rng.uniform(1e19, 3e19, n).astype(F)
+    x[6] = 1e-39
+    x[7, 3] = 3e38
+    x[590:597] = x[1:8]
+    w = normal(rng, n, 1.0, 0.1)
+    out = torch.empty(rows, n, device=cuda)
+    v7g.rmsnorm_rows(out, dev(x), dev(w), eps)
+    with np.errstate(all="ignore"):
+        want = oracle.rmsnorm(x, w, eps)
+    assert_same_f32(host(out), want)
+
+
+@pytest.mark.parametrize("rows", [9, 300, 1200])
+@pytest.mark.parametrize("gamma", ["plain", "nan", "inf", "huge", "tiny"])
+@pytest.mark.parametrize("eps", [0.0, 1e-6])
+def test_rmsnorm_quantize_special_rows(cuda, oracle, rows, gamma, eps):
+    """Rows that must leave the finite-row shortcut -- NaN or infinities in x,
+    a sum of squares that overflows, an all-zero row (infinite scale when eps is
+    0), subnormal and huge values -- mixed among ordinary rows in one launch,
+    under gammas that are tame or not (NaN, infinity, |w| >= 1e30, subnormal):
+    each row takes its own path (the shortcut or the general one) and every
+    code and scale equals the oracle's.  300 and 1200 rows run the row
+    pipeline, 9 the register-chunk kernel."""
+    import v7multiplikator_b200 as v7g
+    rng = np.random.default_rng(rows * 31 + len(gamma))
+    n = 2048
+    x = rng.uniform(-1, 1, (rows, n)).astype(F)
+    specials = {1: ("nan", 17), 2: ("inf", 1000), 3: ("-inf", 5), 4: ("zero", None), 5: ("overflow", None),
+                6: ("subnormal", None), 7: ("huge", 3)}
+    for r, (kind, col) in specials.items():
+        if kind == "nan":
+            x[r, col] = np.nan
+        elif kind == "inf":
+            x[r, col] = np.inf
+        elif kind == "-inf":
+            x[r, col] = -np.inf
+        elif kind == "zero":
+            x[r] = 0.0
+        elif kind == "overflow":
+            x[r] = rng.uniform(1e19, 3e19, n).astype(F)  # squares overflow float
+        elif kind == "subnormal":
+            x[r] = 1e-39
+        else:
+            x[r, col] = 3e38
+    if rows > 100:  # the same rows again deep into the launch (other warps and SMs)
+        x[rows - 8:rows - 1] = x[1:8]
+    w = rng.uniform(0.5, 1.5, n).astype(F)
+    if gamma == "nan":
+        w[700] = np.nan
+    elif gamma == "inf":
+        w[64] = np.inf
+    elif gamma == "huge":
+        w[5] = 2e30
+    elif gamma == "tiny":
+        w[::7] = 1e-39
+    codes = torch.empty(rows, n, dtype=torch.int8, device=cuda)
+    scales = torch.empty(rows, n // 64, device=cuda)
+    v7g.rmsnorm_quantize_rows(codes, scales, dev(x), dev(w), eps)
+    with np.errstate(all="ignore"):
+        wq, ws = oracle.rmsnorm_quantize(x, w, eps)
+    np.testing.assert_array_equal(host(codes), wq)
+    assert_same_f32(host(scales), ws)
+
+
 def test_rmsnorm_quantize_rejects_unaligned_codes(cuda):
     import v7multiplikator_b200 as v7g
     x = torch.zeros(2, 64, device=cuda)
