@@ -106,14 +106,21 @@ struct WarpPipe {
 		++issued;
 	}
 
-	// waits (all lanes) for the warp's row number `waited`; false when the bound ran out
+	// waits (all lanes) for the warp's row number `waited`; false when the
+	// bound ran out, and then the row stays counted as not waited for, so
+	// drain() waits for its copy again
 	__device__ bool wait()
 	{
-		const int64_t k = waited++;
-		return __all_sync(0xffffffffu, mbar_wait(bar + (int)(k % S), (uint32_t)((k / S) & 1), &g_rowpipe_timeouts));
+		const int64_t k = waited;
+		const bool ok = __all_sync(0xffffffffu, mbar_wait(bar + (int)(k % S), (uint32_t)((k / S) & 1), &g_rowpipe_timeouts));
+		if (ok)
+			++waited;
+		return ok;
 	}
 
-	// after a failed wait: the copies still in flight land before the warp leaves
+	// after a failed wait: every copy the warp started and has not seen land
+	// (the one whose wait ran out included) lands before the warp leaves, each
+	// wait bounded again
 	__device__ void drain()
 	{
 		while (waited < issued) {
@@ -161,7 +168,9 @@ __device__ __forceinline__ WarpPipe<S, NIN> pipe_start(unsigned char *smem, cons
 }
 
 // Starts the warp's rows 1 .. S-1, then waits (bounded) for gamma's barrier
-// (phase 0).
+// (phase 0).  When that wait runs out it waits once more (bounded) before
+// returning false, so that gamma's copy, started by the CTA's first thread,
+// has landed before any warp of the CTA can leave.
 template <int S, int NIN>
 __device__ __forceinline__ bool pipe_wait_gamma(WarpPipe<S, NIN> &p, unsigned char *smem, const PipeLayout &L, int64_t first_row, int64_t row_step,
                                                 int64_t rows)
@@ -173,7 +182,10 @@ __device__ __forceinline__ bool pipe_wait_gamma(WarpPipe<S, NIN> &p, unsigned ch
 			p.issue(row, lane == 0);
 	}
 	uint64_t *gbar = reinterpret_cast<uint64_t *>(smem + L.bars_off()) + L.warps * L.stages;
-	return __all_sync(0xffffffffu, mbar_wait(gbar, 0, &g_rowpipe_timeouts));
+	if (__all_sync(0xffffffffu, mbar_wait(gbar, 0, &g_rowpipe_timeouts)))
+		return true;
+	mbar_wait(gbar, 0, &g_rowpipe_timeouts);
+	return false;
 }
 
 // Host: the pipeline kernel's shared-memory ceiling raised to the budget,
