@@ -197,7 +197,10 @@ __global__ void __launch_bounds__(kPipeMaxWarps * 32, 1) k_rmsnorm_pipe(float *o
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 	const PipeLayout L = pipe_layout(n, 1, W, S);
 	const int64_t nw = (int64_t)gridDim.x * W;
-	const int64_t first = (int64_t)blockIdx.x * W + warp;
+	// rows interleaved over the CTAs first: CTA b holds rows b, b + G, b + 2G,
+	// ... (every SM within one row of the average), its warp w the ones from
+	// b + G w on, every G W
+	const int64_t first = (int64_t)warp * gridDim.x + blockIdx.x;
 	const float *const src[1] = {x};
 	WarpPipe<S, 1> p = pipe_start<S, 1>(smem, L, src, w, n, first, nw, rows);
 	const float4 *g4 = reinterpret_cast<const float4 *>(smem);

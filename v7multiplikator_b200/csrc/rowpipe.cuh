@@ -1,7 +1,8 @@
 // rowpipe.cuh -- persistent row kernels fed by bulk copies (sm_100).
 //
-// One CTA per SM, W warps, each warp working through its own rows (warp g of
-// G takes rows g, g + G, g + 2G, ...).  Every warp owns S shared-memory slots;
+// One CTA per SM, W warps, each warp working through its own rows (warp w of
+// CTA b of G takes rows b + G w, then every G W rows, so every CTA holds
+// rows b, b + G, b + 2G, ... and the SMs' shares differ by one row at most).  Every warp owns S shared-memory slots;
 // one lane starts the copy of a future row into a free slot with a 1-D bulk
 // copy (cp.async.bulk: the TMA engine without a tensor map, no multicast)
 // that completes on the slot's transaction-counting mbarrier, so the row's
