@@ -114,6 +114,47 @@ def test_gemv_neg128_weights_and_extreme_scales(cuda, oracle):
         assert_same_f32(host(out2), oracle.swiglu_q8_gemv(xq, xs, wq, ws, wq[::-1], ws[::-1]))
 
 
+@pytest.mark.parametrize("n,d", [(512, 64), (8192, 2048)])
+def test_gemv_neg128_screen_patterns(cuda, oracle, n, d):
+    """The streaming kernel screens weight words for -128 bytes with one
+    subtraction, so a byte's test can see a borrow from the byte below: a
+    0x81 byte above a 0x00 byte passes the screen (and must then get no
+    correction), and a -128 byte above a 0x00 byte (with a borrow) or above a
+    chain of them must still be corrected.  Each pattern at a different byte
+    position of the 4-byte words, in some rows and groups only, against a
+    signed activation; every form of the streaming kernel."""
+    import v7multiplikator_b200 as v7g
+    rng = np.random.default_rng(n + d)
+    xq = rng.integers(-128, 128, (1, n), dtype=np.int8)
+    wq = rng.integers(-127, 128, (d, n), dtype=np.int8)
+    wq[wq == 0] = 1
+    u = wq.view(np.uint8)
+    for r in range(0, d, 3):
+        for c in range(r % 5 * 4, n, 40):
+            k = c + (r % 3)                      # byte 0, 1 or 2 of its word
+            pattern = (r // 3) % 3
+            if pattern == 0:
+                u[r, k], u[r, k + 1] = 0x00, 0x81  # screen fires, nothing to correct
+            elif pattern == 1:
+                u[r, k], u[r, k + 1] = 0x00, 0x80  # a -128 reached by the borrow
+            elif k % 4 < 2:
+                u[r, k], u[r, k + 1], u[r, k + 2] = 0x00, 0x00, 0x80
+    xs = (0.001 + rng.random((1, n // 64)) * 0.02).astype(F)
+    ws = (0.001 + rng.random((d, n // 64)) * 0.02).astype(F)
+    out = torch.empty(1, d, device=cuda)
+    v7g.q8_gemv(out, dev(xq), dev(xs), dev(wq), dev(ws))
+    assert_same_f32(host(out), oracle.q8_gemv(xq, xs, wq, ws), "q8")
+    x = rng.normal(0, 1, (1, n)).astype(F)
+    out_f = torch.empty(1, d, device=cuda)
+    v7g.q8_fused_gemv(out_f, dev(x), dev(wq), dev(ws))
+    assert_same_f32(host(out_f), oracle.q8_fused_gemv(x, wq, ws), "q8 fused")
+    uq, us = wq[::-1].copy(), ws[::-1].copy()
+    out_s = torch.empty(1, d, device=cuda)
+    v7g.swiglu_q8_gemv(out_s, dev(xq), dev(xs), dev(wq), dev(ws), dev(uq), dev(us))
+    with np.errstate(all="ignore"):
+        assert_same_f32(host(out_s), oracle.swiglu_q8_gemv(xq, xs, wq, ws, uq, us), "swiglu q8")
+
+
 @pytest.mark.parametrize("n,d", [(64, 1), (576, 13), (1024, 3000), (2048, 5000), (8192, 2048)])
 def test_gemv_stream_pipeline_and_direct_kernels_agree(cuda, oracle, n, d):
     """16-byte aligned weights and scales take the streaming kernel, aligned

@@ -73,6 +73,7 @@ __device__ __forceinline__ uint32_t has_neg128(uint32_t w)
 	return (t - 0x01010101u) & ~t & 0x80808080u;
 }
 
+
 // One lane's dot over one group (the low word and the high word) as the
 // true products; *flag collects whether a -128 weight byte needs the
 // correction, which the callers apply once per batch of groups so that the
@@ -120,7 +121,9 @@ struct GemvArgs {
 // float4 per lane; `nthreads` (a multiple of 32) threads take part.  SHARED:
 // x is a 16-byte aligned copy in shared memory (plain loads), else global.
 // Groups [gbeg, gend) only when gend >= 0 (x, sq, ss still indexed from group 0).
-template <bool SHARED = false>
+// IL: the codes land in the interleaved layout of the streaming kernel (word
+// 2l of a group = word l, word 2l + 1 = word 8 + l).
+template <bool SHARED = false, bool IL = false>
 __device__ __noinline__ void stage_quantized(const float *x, int n, uint32_t *sq, float *ss, int nthreads = kBlock, int gbeg = 0, int gend = -1)
 {
 	constexpr int U = 4; // group pairs per warp loaded before any is processed: one latency per U (and compact code)
@@ -149,7 +152,7 @@ __device__ __noinline__ void stage_quantized(const float *x, int n, uint32_t *sq
 		for (int u = 0; u < U; ++u) {
 			const int g = g0 + u * step + half;
 			if (g < groups) {
-				sq[g * 16 + hl] = code[u];
+				sq[g * 16 + (IL ? (hl < 8 ? 2 * hl : 2 * hl - 15) : hl)] = code[u];
 				if (hl == 0)
 					ss[g] = scale[u];
 			}
@@ -491,12 +494,106 @@ __global__ void __launch_bounds__(R * kLanes + 32, 2) k_q8_gemv_tma(GemvArgs p, 
 //   per block its weight scales, one bulk copy per matrix (the block's rows
 //             are contiguous) into a two-slot ring;
 //   per chunk the block's CG groups of every row and matrix into a ring of
-//             up to kMaxStages stages.
-// The consumers form the combined scale (weight scale x activation scale,
-// rounded once as the reference's vmulps) as they go.  Requires every weight
-// and scale pointer 16-byte aligned and groups % 4 == 0 (16-byte scale rows).
+//             up to kMaxStages stages (kMaxStagesOne for the one-matrix
+//             product: with fewer chunks in flight the first ones land
+//             sooner, and its consumers, which are the slower side at
+//             decode sizes, start sooner -- 6.98 -> 6.80 us at d = 2048,
+//             n = 8192, where all four chunks of a block fitted before).
+// The consumers re-lay the activation codes so that a lane's two words of a
+// group are adjacent (one 8-byte load), and form the combined scale (weight
+// scale x activation scale, rounded once as the reference's vmulps) as they
+// go.  Requires every weight and scale pointer 16-byte aligned and
+// groups % 4 == 0 (16-byte scale rows).
 constexpr int kMaxStages = 8;
+constexpr int kMaxStagesOne = 3;
 
+// The lane's two activation words of group g in the streaming kernel's
+// interleaved layout (word 2l = word l of the group, 2l + 1 = word 8 + l).
+__device__ __forceinline__ uint2 act_words(const uint32_t *a, int g, int l) { return reinterpret_cast<const uint2 *>(a)[g * 8 + l]; }
+
+// One batch of SB groups of one matrix: the lane dots, then the chain.
+// EXACT: a group holding a -128 weight byte gets the reference's product
+// (lane_dot_correction).  Otherwise the dots are the true products and the
+// returned word is non-zero when a weight byte of the batch is -128: per
+// word the zero-byte test of w ^ 0x80808080 ((t - 0x01010101) & ~t, nonzero
+// in bit 7 of some byte exactly when a byte of t is zero), the groups' tests
+// OR-ed as a tree, not as one dependent chain, and masked once.
+template <bool EXACT, bool FULL, int R, int SB, int CG>
+__device__ __forceinline__ uint32_t batch_chain1(float &acc, const uint32_t *st, const uint32_t *a, const float *wsr, const float *xsc, int l, int b0, int gk)
+{
+	using M = F<true>;
+	int dots[SB];
+	uint32_t f[SB];
+#pragma unroll
+	for (int j = 0; j < SB; ++j) {
+		f[j] = 0;
+		if (FULL || b0 + j < gk) {
+			const uint2 av = act_words(a, b0 + j, l);
+			const uint32_t *wr = st + (b0 + j) * 16;
+			const uint32_t wlo = wr[l], whi = wr[8 + l];
+			dots[j] = __dp4a((int)av.y, (int)whi, __dp4a((int)av.x, (int)wlo, 0));
+			if (EXACT) {
+				if (has_neg128(wlo) | has_neg128(whi))
+					dots[j] += lane_dot_correction_call(av.x, wlo, av.y, whi);
+			} else {
+				const uint32_t tlo = wlo ^ 0x80808080u, thi = whi ^ 0x80808080u;
+				f[j] = ((tlo - 0x01010101u) & ~tlo) | ((thi - 0x01010101u) & ~thi);
+			}
+		}
+	}
+	uint32_t flag = 0;
+	if (!EXACT) {
+#pragma unroll
+		for (int w = SB / 2; w >= 1; w /= 2)
+#pragma unroll
+			for (int j = 0; j < w; ++j)
+				f[j] |= f[j + w];
+		flag = f[0] & 0x80808080u;
+	}
+#pragma unroll
+	for (int q = 0; q < SB / 4; ++q) {
+		const float4 x4 = *reinterpret_cast<const float4 *>(xsc + b0 + 4 * q);
+		const float4 w4 = *reinterpret_cast<const float4 *>(wsr + b0 + 4 * q);
+		const float xv[4] = {x4.x, x4.y, x4.z, x4.w}, wv[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+		for (int u = 0; u < 4; ++u)
+			if (FULL || b0 + 4 * q + u < gk)
+				acc = M::fma((float)dots[4 * q + u], M::mul(wv[u], xv[u]), acc);
+	}
+	return flag;
+}
+
+// The chain of one chunk of one matrix (gk groups of the stage's row; FULL:
+// gk == CG, so no group needs a bound check).  The fast pass takes the true
+// products and tests the weights on the side; if a weight byte of the chunk
+// was -128 (outside the exporter's contract), the chunk runs again from the
+// accumulator it started with, with the reference's products.  Keeping the
+// test's outcome out of the batch loop lets the chain run without waiting on
+// it: measured 7.36 -> 6.98 us at d = 2048, n = 8192 against a per-batch
+// branch on a serially OR-ed flag.
+template <int R, int SB, int CG, bool FULL>
+__device__ __forceinline__ void chunk_chain1(float &acc, const uint32_t *st, const uint32_t *a, const float *wsr, const float *xsc, int l, int gk)
+{
+	static_assert(SB % 4 == 0 && CG % SB == 0 && (SB & (SB - 1)) == 0, "batches of whole float4 scale words, a power-of-two tree");
+	const int nb = FULL ? CG / SB : (gk + SB - 1) / SB;
+	const float acc0 = acc;
+	uint32_t flag = 0;
+#pragma unroll 1
+	for (int k = 0; k < nb; ++k)
+		flag |= batch_chain1<false, FULL, R, SB, CG>(acc, st, a, wsr, xsc, l, k * SB, gk);
+	if (flag) { // cold
+		acc = acc0;
+#pragma unroll 1
+		for (int k = 0; k < nb; ++k)
+			batch_chain1<true, FULL, R, SB, CG>(acc, st, a, wsr, xsc, l, k * SB, gk);
+	}
+}
+
+// The chains of one chunk of NM matrices (the SwiGLU pair): per batch of SB
+// groups the dots of both matrices, the -128 test folded into them, the
+// correction (when a byte was -128) before the chains.  With two matrices
+// this per-batch form measured faster than chunk_chain1's deferred one (more
+// registers live across the chunk there).
 template <int NM, int R, int SB = 8, int CG = kChunkGroups>
 __device__ __forceinline__ void chunk_chains_ws(float (&acc)[NM], const uint32_t *st, const uint32_t *a, const float *wsr, int mstride, const float *xsc, int l, int gk)
 {
@@ -511,21 +608,25 @@ __device__ __forceinline__ void chunk_chains_ws(float (&acc)[NM], const uint32_t
 		uint32_t flag = 0;
 #pragma unroll
 		for (int j = 0; j < SB; ++j)
-			if (b0 + j < gk)
+			if (b0 + j < gk) {
+				const uint2 av = act_words(a, b0 + j, l);
 #pragma unroll
 				for (int m = 0; m < NM; ++m) {
 					const uint32_t *wr = st + m * R * kSlotWords + (b0 + j) * 16;
-					dots[m][j] = lane_dot(a[(b0 + j) * 16 + l], wr[l], a[(b0 + j) * 16 + 8 + l], wr[8 + l], flag);
+					dots[m][j] = lane_dot(av.x, wr[l], av.y, wr[8 + l], flag);
 				}
+			}
 		if (flag) { // cold: the exporter never writes -128
 #pragma unroll
 			for (int j = 0; j < SB; ++j)
-				if (b0 + j < gk)
+				if (b0 + j < gk) {
+					const uint2 av = act_words(a, b0 + j, l);
 #pragma unroll
 					for (int m = 0; m < NM; ++m) {
 						const uint32_t *wr = st + m * R * kSlotWords + (b0 + j) * 16;
-						dots[m][j] += lane_dot_correction_call(a[(b0 + j) * 16 + l], wr[l], a[(b0 + j) * 16 + 8 + l], wr[8 + l]);
+						dots[m][j] += lane_dot_correction_call(av.x, wr[l], av.y, wr[8 + l]);
 					}
+				}
 		}
 		float xv[SB];
 #pragma unroll
@@ -624,9 +725,9 @@ __global__ void __launch_bounds__(stream_consumers(R) + 32 * P, 2) k_q8_gemv_str
 	auto quantise_all = [&]() {
 		if (xstaged) {
 			mbar_wait(pro, 0, &g_pipeline_timeouts);
-			stage_quantized<true>(xstage, n, sq, ss, kConsumers + 32 * P);
+			stage_quantized<true, true>(xstage, n, sq, ss, kConsumers + 32 * P);
 		} else {
-			stage_quantized<false>(p.xf + b * n, n, sq, ss, kConsumers + 32 * P);
+			stage_quantized<false, true>(p.xf + b * n, n, sq, ss, kConsumers + 32 * P);
 		}
 		named_sync(2, kConsumers + 32 * P);
 	};
@@ -731,6 +832,19 @@ __global__ void __launch_bounds__(stream_consumers(R) + 32 * P, 2) k_q8_gemv_str
 	}
 	if (FUSED)
 		quantise_all();
+	if (MODE != 2 && !FUSED) {
+		// the copied codes into the interleaved layout, in place: word 2l of a
+		// group = word l, word 2l + 1 = word 8 + l (one 8-byte load per lane and group)
+		for (int g = threadIdx.x; g < groups; g += kConsumers) {
+			uint4 *pg = reinterpret_cast<uint4 *>(sq + g * 16);
+			const uint4 q0 = pg[0], q1 = pg[1], q2 = pg[2], q3 = pg[3];
+			pg[0] = make_uint4(q0.x, q2.x, q0.y, q2.y);
+			pg[1] = make_uint4(q0.z, q2.z, q0.w, q2.w);
+			pg[2] = make_uint4(q1.x, q3.x, q1.y, q3.y);
+			pg[3] = make_uint4(q1.z, q3.z, q1.w, q3.w);
+		}
+		named_sync(1, kConsumers);
+	}
 	const int r = threadIdx.x / kLanes, l = threadIdx.x & (kLanes - 1);
 	uint32_t q = 0;
 	int i = 0;
@@ -755,10 +869,16 @@ __global__ void __launch_bounds__(stream_consumers(R) + 32 * P, 2) k_q8_gemv_str
 				const uint32_t *st = reinterpret_cast<const uint32_t *>(smem + (size_t)s * kStageBytes) + r * (kSlot / 4);
 				if constexpr (MODE == 2)
 					chunk_f32<R, CG>(acc, st, xt + l * xstride + g0 * 8, wsr + g0, groups, l, gk);
-				else if (gk == CG) // one matrix: 16-group batches, the most independent work per wait
-					chunk_chains_ws<NM, R, NM == 1 ? 16 : 8, CG>(acc, st, sq + g0 * 16, wsr + g0, mstride, ss + g0, l, CG);
-				else
+				else if constexpr (NM == 1) { // 16-group batches, the most independent work per wait
+					if (gk == CG)
+						chunk_chain1<R, 16, CG, true>(acc[0], st, sq + g0 * 16, wsr + g0, ss + g0, l, CG);
+					else
+						chunk_chain1<R, 16, CG, false>(acc[0], st, sq + g0 * 16, wsr + g0, ss + g0, l, gk);
+				} else if (gk == CG) { // a constant bound: no group needs a check
+					chunk_chains_ws<NM, R, 8, CG>(acc, st, sq + g0 * 16, wsr + g0, mstride, ss + g0, l, CG);
+				} else {
 					chunk_chains_ws<NM, R, 8, CG>(acc, st, sq + g0 * 16, wsr + g0, mstride, ss + g0, l, gk);
+				}
 			}
 			__syncwarp();
 			if ((threadIdx.x & 31) == 0)
@@ -917,22 +1037,24 @@ StreamLayout stream_layout(int mode, bool fused, int rows_per_block, int n, bool
 			const size_t base = fixed + (xs ? 4 * (size_t)n : 0);
 			if (base + 2 * stage > budget)
 				continue;
-			const int stages = (int)std::min<size_t>(kMaxStages, (budget - base) / stage);
+			const int stages = (int)std::min<size_t>(mode == 0 ? kMaxStagesOne : kMaxStages, (budget - base) / stage);
 			return StreamLayout{stages, xs != 0, base + (size_t)stages * stage};
 		}
 	return StreamLayout{0, false, 0};
 }
 
 // Streaming-kernel shapes, measured on B200 at the decode shapes (d = 2048
-// .. 12288): four producer warps and 2 KB row copies for the one-matrix
-// product (it is paced by how fast copies are issued), two producer warps
-// and 1 KB copies for the two-matrix ones (their stages are twice as big).
+// .. 12288): 2 KB row copies for the one-matrix product, 1 KB for the
+// two-matrix ones (their stages are twice as big); two producer warps, four
+// for the fused one-matrix product, whose producers also quantise the
+// activation (at d = 2048, n = 8192 two warps measured 6.80 -> 6.72 us
+// without the quantiser, 7.75 -> 8.6 us with it).
 // Rows per block: 16, or 14 where that spreads the row blocks more evenly
 // over the SMs (launch_gemv_stream); fewer rows per block than that keep too
 // few bytes in flight per CTA.
 template <int MODE, bool FUSED>
 struct StreamShape {
-	static constexpr int P = MODE == 0 ? 4 : 2;
+	static constexpr int P = MODE == 0 && FUSED ? 4 : 2;
 	static constexpr int CG = MODE == 0 ? 32 : kChunkGroups;
 };
 
