@@ -122,11 +122,11 @@ struct GemvArgs {
 // x is a 16-byte aligned copy in shared memory (plain loads), else global.
 // Groups [gbeg, gend) only when gend >= 0 (x, sq, ss still indexed from group 0).
 // IL: the codes land in the interleaved layout of the streaming kernel (word
-// 2l of a group = word l, word 2l + 1 = word 8 + l).
-template <bool SHARED = false, bool IL = false>
+// 2l of a group = word l, word 2l + 1 = word 8 + l).  U: group pairs per
+// warp loaded before any is processed (one latency per U, and compact code).
+template <bool SHARED = false, bool IL = false, int U = 4>
 __device__ __noinline__ void stage_quantized(const float *x, int n, uint32_t *sq, float *ss, int nthreads = kBlock, int gbeg = 0, int gend = -1)
 {
-	constexpr int U = 4; // group pairs per warp loaded before any is processed: one latency per U (and compact code)
 	const int lane = threadIdx.x & 31, half = lane >> 4, hl = lane & 15;
 	const int groups = gend >= 0 ? gend : n / kQ8Group;
 	const int step = (nthreads / 32) * 2;
@@ -717,19 +717,22 @@ __global__ void __launch_bounds__(stream_consumers(R) + 32 * P, 2) k_q8_gemv_str
 	}
 	__syncthreads();
 	const bool pro_copy = (MODE != 2 && !FUSED) || xstaged;
-	// FUSED: every thread of the CTA quantises its share of the activation
-	// (the producer warps once they have issued their first stages, before
-	// which no stage can be freed anyway), then all meet at named barrier 2.
-	// Each thread arrives there exactly once and waits for nothing unbounded
-	// before it.
+	// FUSED: the consumer warps quantise the activation while the producers
+	// issue the first weight chunks, then meet at named barrier 2 (consumers
+	// only).  With the producers taking part the barrier waited for them to
+	// get their first stages issued, which the memory system paces: the
+	// activation was quantised 1.9 us after its copy landed instead of by the
+	// time the first chunk had (v7d_q8_fused 8192 -> 2048: 7.72 -> 7.21 us).
+	// Each consumer thread arrives there exactly once and waits for nothing
+	// unbounded before it.
 	auto quantise_all = [&]() {
 		if (xstaged) {
 			mbar_wait(pro, 0, &g_pipeline_timeouts);
-			stage_quantized<true, true>(xstage, n, sq, ss, kConsumers + 32 * P);
+			stage_quantized<true, true>(xstage, n, sq, ss, kConsumers);
 		} else {
-			stage_quantized<false, true>(p.xf + b * n, n, sq, ss, kConsumers + 32 * P);
+			stage_quantized<false, true>(p.xf + b * n, n, sq, ss, kConsumers);
 		}
-		named_sync(2, kConsumers + 32 * P);
+		named_sync(2, kConsumers);
 	};
 	if (threadIdx.x >= kConsumers) {
 		// P producer warps: warp 0 also copies the activation and the scales;
@@ -751,14 +754,7 @@ __global__ void __launch_bounds__(stream_consumers(R) + 32 * P, 2) k_q8_gemv_str
 		uint32_t q = 0;
 		int i = 0;
 		bool ok = true;
-		// FUSED: join the quantisation just before the first wait of any kind
-		// (row block 2's scale slot, or chunk `stages`), or at the end
-		bool joined = !FUSED;
 		for (int64_t rb = blockIdx.x; rb < nrb && ok; rb += gridDim.x, ++i) {
-			if (!joined && i >= 2) {
-				quantise_all();
-				joined = true;
-			}
 			const int64_t row0 = rb * R;
 			const int rows = (int)min((int64_t)R, p.d - row0);
 			const int slot = i & 1;
@@ -778,10 +774,6 @@ __global__ void __launch_bounds__(stream_consumers(R) + 32 * P, 2) k_q8_gemv_str
 			const int mine = ncopy > pw ? (ncopy - pw + P - 1) / P : 0; // copies pw, pw + P, ...
 			for (int k = 0; k < nchunks; ++k, ++q) {
 				const int s = (int)(q % (uint32_t)stages);
-				if (!joined && q >= (uint32_t)stages) {
-					quantise_all();
-					joined = true;
-				}
 				if (q >= (uint32_t)stages && lane == 0)
 					ok = mbar_wait(empty + s, ((q / stages) - 1) & 1, &g_pipeline_timeouts);
 				if (!__shfl_sync(0xffffffffu, ok, 0))
@@ -803,8 +795,6 @@ __global__ void __launch_bounds__(stream_consumers(R) + 32 * P, 2) k_q8_gemv_str
 				}
 			}
 		}
-		if (!joined)
-			quantise_all();
 		// leave only once every copy issued has landed
 		if (lane == 0) {
 			for (uint32_t k = q > (uint32_t)stages ? q - stages : 0; k < q; ++k)
@@ -1045,16 +1035,14 @@ StreamLayout stream_layout(int mode, bool fused, int rows_per_block, int n, bool
 
 // Streaming-kernel shapes, measured on B200 at the decode shapes (d = 2048
 // .. 12288): 2 KB row copies for the one-matrix product, 1 KB for the
-// two-matrix ones (their stages are twice as big); two producer warps, four
-// for the fused one-matrix product, whose producers also quantise the
-// activation (at d = 2048, n = 8192 two warps measured 6.80 -> 6.72 us
-// without the quantiser, 7.75 -> 8.6 us with it).
+// two-matrix ones (their stages are twice as big); two producer warps (four
+// measured slower for v7d_q8 at d = 2048, n = 8192: 6.80 against 6.72 us).
 // Rows per block: 16, or 14 where that spreads the row blocks more evenly
 // over the SMs (launch_gemv_stream); fewer rows per block than that keep too
 // few bytes in flight per CTA.
 template <int MODE, bool FUSED>
 struct StreamShape {
-	static constexpr int P = MODE == 0 && FUSED ? 4 : 2;
+	static constexpr int P = 2;
 	static constexpr int CG = MODE == 0 ? 32 : kChunkGroups;
 };
 
