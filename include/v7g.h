@@ -131,7 +131,11 @@ int v7g_get_rope_tables(const float **cos_table, const float **sin_table, int *h
    activation vectors of n; out [batch, d] fp32.  Contract: n > 0,
    n % 64 == 0, n <= 65536, batch <= 65535.  Weight bytes in [-127, 127] (the
    exporter's contract); a -128 weight is multiplied as the reference's
-   vpsignb forms it.  Every output equals the reference's bit for bit. */
+   vpsignb forms it.  Every output equals the reference's bit for bit.
+   v7g_q8_gemv and v7g_swiglu_q8_gemv with batch >= 2 stream the weights once
+   per block of 2 or 4 activation rows, as the reference's four-token
+   v7d_q8_batch4 does (src/q8_batch4.h:5-19, q8_batch4_kernel.inc:5-10); each
+   row's result is its one-row result. */
 
 /* v7d_q8 (src/v7_lib.h:113, q8_kernel.inc:84-207): out[b, i] = dot(x_b, w_i),
    x Q8: codes [batch, n] (16-byte aligned) + scales [batch, n/64]. */

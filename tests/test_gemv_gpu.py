@@ -240,6 +240,39 @@ def test_gemv_longest_rows(cuda, oracle):
                     torch.zeros(4, m // 64, device=cuda))
 
 
+@pytest.mark.parametrize("n,d", [(8192, 2048), (1024, 3000)])
+@pytest.mark.parametrize("batch", [2, 4, 5, 9])
+def test_gemv_token_blocks(cuda, oracle, n, d, batch):
+    """A batch of two or more activation rows takes the streaming kernel's
+    token blocks (two or four rows a CTA sharing one weight stream, the last
+    block possibly partial): every row equal to the oracle's one-row product,
+    with -128 weight bytes in some groups (the correction path of a block)."""
+    import v7multiplikator_b200 as v7g
+    rng = np.random.default_rng(n + d + 31 * batch)
+    xq, xs, gq, gs = q8_case(rng, batch, n, d)
+    _, _, uq, us = q8_case(rng, 1, n, d)
+    gq[::5, 3::97] = -128
+    out = torch.empty(batch, d, device=cuda)
+    v7g.q8_gemv(out, dev(xq), dev(xs), dev(gq), dev(gs))
+    assert_same_f32(host(out), oracle.q8_gemv(xq, xs, gq, gs), f"v7d_q8 batch {batch}")
+    out2 = torch.empty(batch, d, device=cuda)
+    v7g.swiglu_q8_gemv(out2, dev(xq), dev(xs), dev(gq), dev(gs), dev(uq), dev(us))
+    with np.errstate(all="ignore"):
+        assert_same_f32(host(out2), oracle.swiglu_q8_gemv(xq, xs, gq, gs, uq, us), f"v7d_swiglu_q8 batch {batch}")
+
+
+def test_gemv_token_blocks_many(cuda, oracle):
+    """Many token blocks (4099 rows: 1025 blocks of four, the last with
+    three) through the streaming kernel, against the oracle."""
+    import v7multiplikator_b200 as v7g
+    batch, n, d = 4099, 256, 40
+    rng = np.random.default_rng(11)
+    xq, xs, wq, ws = q8_case(rng, batch, n, d)
+    out = torch.empty(batch, d, device=cuda)
+    v7g.q8_gemv(out, dev(xq), dev(xs), dev(wq), dev(ws))
+    assert_same_f32(host(out), oracle.q8_gemv(xq, xs, wq, ws), "v7d_q8 batch 4099")
+
+
 def test_gemv_largest_batch(cuda, oracle):
     """The largest batch (65535 activation rows: the grid's second dimension)
     against the oracle; one row more is refused."""

@@ -114,6 +114,7 @@ struct GemvArgs {
 	const int8_t *wq[2];   // gate (or the only matrix), up: [d, n]
 	const float *ws[2];    // [d, n/64]
 	int n, d;
+	int batch;             // activation rows (the token-block kernels)
 };
 
 // Quantise the CTA's activation row into shared memory with v7d_quantize's
@@ -511,7 +512,9 @@ constexpr int kMaxStagesOne = 3;
 // interleaved layout (word 2l = word l of the group, 2l + 1 = word 8 + l).
 __device__ __forceinline__ uint2 act_words(const uint32_t *a, int g, int l) { return reinterpret_cast<const uint2 *>(a)[g * 8 + l]; }
 
-// One batch of SB groups of one matrix: the lane dots, then the chain.
+// One batch of SB groups of one matrix for one token: the lane dots, then
+// the chain.  The one-token kernels keep this form: the token-block form
+// below with NB = 1 measured about 1 % slower at the decode shapes.
 // EXACT: a group holding a -128 weight byte gets the reference's product
 // (lane_dot_correction).  Otherwise the dots are the true products and the
 // returned word is non-zero when a weight byte of the batch is -128: per
@@ -519,7 +522,7 @@ __device__ __forceinline__ uint2 act_words(const uint32_t *a, int g, int l) { re
 // in bit 7 of some byte exactly when a byte of t is zero), the groups' tests
 // OR-ed as a tree, not as one dependent chain, and masked once.
 template <bool EXACT, bool FULL, int R, int SB, int CG>
-__device__ __forceinline__ uint32_t batch_chain1(float &acc, const uint32_t *st, const uint32_t *a, const float *wsr, const float *xsc, int l, int b0, int gk)
+__device__ __forceinline__ uint32_t batch_chain1_one(float &acc, const uint32_t *st, const uint32_t *a, const float *wsr, const float *xsc, int l, int b0, int gk)
 {
 	using M = F<true>;
 	int dots[SB];
@@ -572,7 +575,7 @@ __device__ __forceinline__ uint32_t batch_chain1(float &acc, const uint32_t *st,
 // it: measured 7.36 -> 6.98 us at d = 2048, n = 8192 against a per-batch
 // branch on a serially OR-ed flag.
 template <int R, int SB, int CG, bool FULL>
-__device__ __forceinline__ void chunk_chain1(float &acc, const uint32_t *st, const uint32_t *a, const float *wsr, const float *xsc, int l, int gk)
+__device__ __forceinline__ void chunk_chain1_one(float &acc, const uint32_t *st, const uint32_t *a, const float *wsr, const float *xsc, int l, int gk)
 {
 	static_assert(SB % 4 == 0 && CG % SB == 0 && (SB & (SB - 1)) == 0, "batches of whole float4 scale words, a power-of-two tree");
 	const int nb = FULL ? CG / SB : (gk + SB - 1) / SB;
@@ -580,22 +583,119 @@ __device__ __forceinline__ void chunk_chain1(float &acc, const uint32_t *st, con
 	uint32_t flag = 0;
 #pragma unroll 1
 	for (int k = 0; k < nb; ++k)
-		flag |= batch_chain1<false, FULL, R, SB, CG>(acc, st, a, wsr, xsc, l, k * SB, gk);
+		flag |= batch_chain1_one<false, FULL, R, SB, CG>(acc, st, a, wsr, xsc, l, k * SB, gk);
 	if (flag) { // cold
 		acc = acc0;
 #pragma unroll 1
 		for (int k = 0; k < nb; ++k)
-			batch_chain1<true, FULL, R, SB, CG>(acc, st, a, wsr, xsc, l, k * SB, gk);
+			batch_chain1_one<true, FULL, R, SB, CG>(acc, st, a, wsr, xsc, l, k * SB, gk);
 	}
 }
 
-// The chains of one chunk of NM matrices (the SwiGLU pair): per batch of SB
-// groups the dots of both matrices, the -128 test folded into them, the
-// correction (when a byte was -128) before the chains.  With two matrices
-// this per-batch form measured faster than chunk_chain1's deferred one (more
-// registers live across the chunk there).
-template <int NM, int R, int SB = 8, int CG = kChunkGroups>
-__device__ __forceinline__ void chunk_chains_ws(float (&acc)[NM], const uint32_t *st, const uint32_t *a, const float *wsr, int mstride, const float *xsc, int l, int gk)
+// One batch of SB groups of one matrix for NB tokens (activations a + t *
+// astride words, their scales xsc + t * sstride): the weight words loaded
+// and tested once, each token's lane dots, then each token's chain.
+// EXACT: a group holding a -128 weight byte gets the reference's product
+// (lane_dot_correction).  Otherwise the dots are the true products and the
+// returned word is non-zero when a weight byte of the batch is -128: per
+// word the zero-byte test of w ^ 0x80808080 ((t - 0x01010101) & ~t, nonzero
+// in bit 7 of some byte exactly when a byte of t is zero), the groups' tests
+// OR-ed as a tree, not as one dependent chain, and masked once.
+template <bool EXACT, bool FULL, int NB, int SB, int CG>
+__device__ __forceinline__ uint32_t batch_chain1(float (&acc)[NB], const uint32_t *st, const uint32_t *a, int astride, const float *wsr, const float *xsc,
+                                                 int sstride, int l, int b0, int gk)
+{
+	using M = F<true>;
+	int dots[NB][SB];
+	uint32_t f[SB];
+#pragma unroll
+	for (int j = 0; j < SB; ++j) {
+		f[j] = 0;
+		if (FULL || b0 + j < gk) {
+			const uint32_t *wr = st + (b0 + j) * 16;
+			const uint32_t wlo = wr[l], whi = wr[8 + l];
+			bool neg = false;
+			if (EXACT)
+				neg = (has_neg128(wlo) | has_neg128(whi)) != 0;
+			else {
+				const uint32_t tlo = wlo ^ 0x80808080u, thi = whi ^ 0x80808080u;
+				f[j] = ((tlo - 0x01010101u) & ~tlo) | ((thi - 0x01010101u) & ~thi);
+			}
+#pragma unroll
+			for (int t = 0; t < NB; ++t) {
+				const uint2 av = act_words(a + t * astride, b0 + j, l);
+				dots[t][j] = __dp4a((int)av.y, (int)whi, __dp4a((int)av.x, (int)wlo, 0));
+				if (EXACT && neg)
+					dots[t][j] += lane_dot_correction_call(av.x, wlo, av.y, whi);
+			}
+		}
+	}
+	uint32_t flag = 0;
+	if (!EXACT) {
+#pragma unroll
+		for (int w = SB / 2; w >= 1; w /= 2)
+#pragma unroll
+			for (int j = 0; j < w; ++j)
+				f[j] |= f[j + w];
+		flag = f[0] & 0x80808080u;
+	}
+#pragma unroll
+	for (int q = 0; q < SB / 4; ++q) {
+		const float4 w4 = *reinterpret_cast<const float4 *>(wsr + b0 + 4 * q);
+		const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+		for (int t = 0; t < NB; ++t) {
+			const float4 x4 = *reinterpret_cast<const float4 *>(xsc + t * sstride + b0 + 4 * q);
+			const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+			for (int u = 0; u < 4; ++u)
+				if (FULL || b0 + 4 * q + u < gk)
+					acc[t] = M::fma((float)dots[t][4 * q + u], M::mul(wv[u], xv[u]), acc[t]);
+		}
+	}
+	return flag;
+}
+
+// The chains of one chunk of one matrix for NB tokens (gk groups of the
+// stage's row; FULL: gk == CG, so no group needs a bound check).  The fast
+// pass takes the true products and tests the weights on the side; if a
+// weight byte of the chunk was -128 (outside the exporter's contract), the
+// chunk runs again from the accumulators it started with, with the
+// reference's products.  Keeping the test's outcome out of the batch loop
+// lets the chains run without waiting on it: measured 7.36 -> 6.98 us at
+// d = 2048, n = 8192 against a per-batch branch on a serially OR-ed flag.
+template <int NB, int SB, int CG, bool FULL>
+__device__ __forceinline__ void chunk_chain1(float (&acc)[NB], const uint32_t *st, const uint32_t *a, int astride, const float *wsr, const float *xsc, int sstride,
+                                             int l, int gk)
+{
+	static_assert(SB % 4 == 0 && CG % SB == 0 && (SB & (SB - 1)) == 0, "batches of whole float4 scale words, a power-of-two tree");
+	const int nb = FULL ? CG / SB : (gk + SB - 1) / SB;
+	float acc0[NB];
+#pragma unroll
+	for (int t = 0; t < NB; ++t)
+		acc0[t] = acc[t];
+	uint32_t flag = 0;
+#pragma unroll 1
+	for (int k = 0; k < nb; ++k)
+		flag |= batch_chain1<false, FULL, NB, SB, CG>(acc, st, a, astride, wsr, xsc, sstride, l, k * SB, gk);
+	if (flag) { // cold
+#pragma unroll
+		for (int t = 0; t < NB; ++t)
+			acc[t] = acc0[t];
+#pragma unroll 1
+		for (int k = 0; k < nb; ++k)
+			batch_chain1<true, FULL, NB, SB, CG>(acc, st, a, astride, wsr, xsc, sstride, l, k * SB, gk);
+	}
+}
+
+// The chains of one chunk of NM matrices (the SwiGLU pair) for NB tokens:
+// per batch of SB groups the dots of both matrices, the -128 test folded
+// into them, the correction (when a byte was -128) before the chains.  With
+// two matrices this per-batch form measured faster than chunk_chain1's
+// deferred one (more registers live across the chunk there).
+template <int NM, int NB, int R, int SB = 8, int CG = kChunkGroups>
+__device__ __forceinline__ void chunk_chains_ws(float (&acc)[NM][NB], const uint32_t *st, const uint32_t *a, int astride, const float *wsr, int mstride,
+                                                const float *xsc, int sstride, int l, int gk)
 {
 	using M = F<true>;
 	static_assert(SB % 4 == 0 && CG % SB == 0, "batches of whole float4 scale words");
@@ -604,48 +704,59 @@ __device__ __forceinline__ void chunk_chains_ws(float (&acc)[NM], const uint32_t
 	for (int b0 = 0; b0 < CG; b0 += SB) {
 		if (b0 >= gk)
 			break;
-		int dots[NM][SB];
+		int dots[NM][NB][SB];
 		uint32_t flag = 0;
 #pragma unroll
 		for (int j = 0; j < SB; ++j)
 			if (b0 + j < gk) {
-				const uint2 av = act_words(a, b0 + j, l);
+				uint2 av[NB];
+#pragma unroll
+				for (int t = 0; t < NB; ++t)
+					av[t] = act_words(a + t * astride, b0 + j, l);
 #pragma unroll
 				for (int m = 0; m < NM; ++m) {
 					const uint32_t *wr = st + m * R * kSlotWords + (b0 + j) * 16;
-					dots[m][j] = lane_dot(av.x, wr[l], av.y, wr[8 + l], flag);
+#pragma unroll
+					for (int t = 0; t < NB; ++t)
+						dots[m][t][j] = lane_dot(av[t].x, wr[l], av[t].y, wr[8 + l], flag);
 				}
 			}
 		if (flag) { // cold: the exporter never writes -128
 #pragma unroll
 			for (int j = 0; j < SB; ++j)
 				if (b0 + j < gk) {
-					const uint2 av = act_words(a, b0 + j, l);
 #pragma unroll
 					for (int m = 0; m < NM; ++m) {
 						const uint32_t *wr = st + m * R * kSlotWords + (b0 + j) * 16;
-						dots[m][j] += lane_dot_correction_call(av.x, wr[l], av.y, wr[8 + l]);
+#pragma unroll
+						for (int t = 0; t < NB; ++t) {
+							const uint2 av = act_words(a + t * astride, b0 + j, l);
+							dots[m][t][j] += lane_dot_correction_call(av.x, wr[l], av.y, wr[8 + l]);
+						}
 					}
 				}
 		}
-		float xv[SB];
 #pragma unroll
-		for (int q = 0; q < SB / 4; ++q) {
-			const float4 x4 = *reinterpret_cast<const float4 *>(xsc + b0 + 4 * q);
-			xv[4 * q] = x4.x, xv[4 * q + 1] = x4.y, xv[4 * q + 2] = x4.z, xv[4 * q + 3] = x4.w;
-		}
-#pragma unroll
-		for (int m = 0; m < NM; ++m) {
-			float wv[SB];
+		for (int t = 0; t < NB; ++t) {
+			float xv[SB];
 #pragma unroll
 			for (int q = 0; q < SB / 4; ++q) {
-				const float4 w4 = *reinterpret_cast<const float4 *>(wsr + m * mstride + b0 + 4 * q);
-				wv[4 * q] = w4.x, wv[4 * q + 1] = w4.y, wv[4 * q + 2] = w4.z, wv[4 * q + 3] = w4.w;
+				const float4 x4 = *reinterpret_cast<const float4 *>(xsc + t * sstride + b0 + 4 * q);
+				xv[4 * q] = x4.x, xv[4 * q + 1] = x4.y, xv[4 * q + 2] = x4.z, xv[4 * q + 3] = x4.w;
 			}
 #pragma unroll
-			for (int j = 0; j < SB; ++j)
-				if (b0 + j < gk)
-					acc[m] = M::fma((float)dots[m][j], M::mul(wv[j], xv[j]), acc[m]);
+			for (int m = 0; m < NM; ++m) {
+				float wv[SB];
+#pragma unroll
+				for (int q = 0; q < SB / 4; ++q) {
+					const float4 w4 = *reinterpret_cast<const float4 *>(wsr + m * mstride + b0 + 4 * q);
+					wv[4 * q] = w4.x, wv[4 * q + 1] = w4.y, wv[4 * q + 2] = w4.z, wv[4 * q + 3] = w4.w;
+				}
+#pragma unroll
+				for (int j = 0; j < SB; ++j)
+					if (b0 + j < gk)
+						acc[m][t] = M::fma((float)dots[m][t][j], M::mul(wv[j], xv[j]), acc[m][t]);
+			}
 		}
 	}
 }
@@ -660,12 +771,12 @@ struct StreamLayout {
 // [2][NM][R * groups] + 16 | activation: codes [n] + scales [groups + 16]
 // (MODE 2: fp32 lane-major [8][xstride]) | fp32 staging [n] when xstaged |
 // barriers full[stages], empty[stages], sfull[2], sempty[2], pro.
-__host__ __device__ inline size_t stream_fixed(int mode, int rows_per_block, int n)
+__host__ __device__ inline size_t stream_fixed(int mode, int rows_per_block, int n, int tokens = 1)
 {
 	const int nm = mode == 0 ? 1 : 2;
 	const size_t groups = (size_t)n / kQ8Group;
 	const size_t slots = 4 * (2 * (size_t)nm * rows_per_block * groups + 16);
-	const size_t act = mode == 2 ? 32 * (groups * 8 + 4) : (size_t)n + 4 * (groups + 16);
+	const size_t act = mode == 2 ? 32 * (groups * 8 + 4) : (size_t)tokens * ((size_t)n + 4 * (groups + 16));
 	return slots + act;
 }
 
@@ -673,11 +784,16 @@ __host__ __device__ inline size_t stream_fixed(int mode, int rows_per_block, int
 // warps (the threads of rows R.. of the last warp compute nothing).
 __host__ __device__ constexpr int stream_consumers(int rows_per_block) { return (rows_per_block * kLanes + 31) / 32 * 32; }
 
-template <int MODE, bool FUSED, int R, int P, int CG>
+// NB > 1 (the Q8-activation forms without the fused quantiser): a CTA takes
+// NB activation rows (tokens) at once and streams the weights once for all
+// of them; each token keeps its own dots and chains, so its result is the
+// one-token result, bit for bit.
+template <int MODE, bool FUSED, int R, int P, int CG, int NB = 1>
 __global__ void __launch_bounds__(stream_consumers(R) + 32 * P, 2) k_q8_gemv_stream(GemvArgs p, int stages, int xstaged_arg)
 {
 	kernel_entry();
 	static_assert(P >= 1 && P <= 4, "one to four producer warps");
+	static_assert(NB == 1 || (MODE != 2 && !FUSED), "token blocks: the Q8-activation forms");
 	constexpr int NM = MODE == 0 ? 1 : 2;
 	constexpr int kConsumers = stream_consumers(R);
 	static_assert(CG % 16 == 0, "whole 16-group batches per chunk");
@@ -687,7 +803,9 @@ __global__ void __launch_bounds__(stream_consumers(R) + 32 * P, 2) k_q8_gemv_str
 	const int n = p.n, groups = n / kQ8Group;
 	const int nchunks = (groups + CG - 1) / CG;
 	const int64_t nrb = (p.d + R - 1) / R;
-	const int64_t b = blockIdx.y;
+	const int64_t b = (int64_t)blockIdx.y * NB; // the block's first token
+	const int nt = NB == 1 ? 1 : (int)min((int64_t)NB, (int64_t)p.batch - b);
+	const int astride = n + 4 * (groups + 16); // bytes: a token's codes and scales
 	// only the fp32-activation forms have a staging area in their layout
 	const bool xstaged = (MODE == 2 || FUSED) && xstaged_arg != 0;
 	const int mstride = R * groups; // floats between a slot's matrices
@@ -697,7 +815,7 @@ __global__ void __launch_bounds__(stream_consumers(R) + 32 * P, 2) k_q8_gemv_str
 	float *ss = reinterpret_cast<float *>(act + n);
 	float *xt = reinterpret_cast<float *>(act);
 	const int xstride = groups * 8 + 4; // MODE 2: the 8 lanes' rows start 4 banks apart
-	float *xstage = reinterpret_cast<float *>(reinterpret_cast<unsigned char *>(sws) + stream_fixed(MODE, R, n));
+	float *xstage = reinterpret_cast<float *>(reinterpret_cast<unsigned char *>(sws) + stream_fixed(MODE, R, n, NB));
 	uint64_t *full = reinterpret_cast<uint64_t *>(reinterpret_cast<unsigned char *>(xstage) + (xstaged ? 4 * (size_t)n : 0));
 	uint64_t *empty = full + stages;
 	uint64_t *sfull = empty + stages;
@@ -743,9 +861,11 @@ __global__ void __launch_bounds__(stream_consumers(R) + 32 * P, 2) k_q8_gemv_str
 		const int pw = (threadIdx.x - kConsumers) >> 5;
 		if (pro_copy && pw == 0 && lane == 0) {
 			if (MODE != 2 && !FUSED) {
-				mbar_arrive_expect_tx(pro, (uint32_t)(n + 4 * groups));
-				bulk_copy_g2s(sq, p.xq + b * n, (uint32_t)n, pro);
-				bulk_copy_g2s(ss, p.xs + b * groups, (uint32_t)(4 * groups), pro);
+				mbar_arrive_expect_tx(pro, (uint32_t)(nt * (n + 4 * groups)));
+				for (int t = 0; t < nt; ++t) {
+					bulk_copy_g2s(act + t * astride, p.xq + (b + t) * n, (uint32_t)n, pro);
+					bulk_copy_g2s(act + t * astride + n, p.xs + (b + t) * groups, (uint32_t)(4 * groups), pro);
+				}
 			} else {
 				mbar_arrive_expect_tx(pro, (uint32_t)(4 * n));
 				bulk_copy_g2s(xstage, p.xf + b * n, (uint32_t)(4 * n), pro);
@@ -825,14 +945,15 @@ __global__ void __launch_bounds__(stream_consumers(R) + 32 * P, 2) k_q8_gemv_str
 	if (MODE != 2 && !FUSED) {
 		// the copied codes into the interleaved layout, in place: word 2l of a
 		// group = word l, word 2l + 1 = word 8 + l (one 8-byte load per lane and group)
-		for (int g = threadIdx.x; g < groups; g += kConsumers) {
-			uint4 *pg = reinterpret_cast<uint4 *>(sq + g * 16);
-			const uint4 q0 = pg[0], q1 = pg[1], q2 = pg[2], q3 = pg[3];
-			pg[0] = make_uint4(q0.x, q2.x, q0.y, q2.y);
-			pg[1] = make_uint4(q0.z, q2.z, q0.w, q2.w);
-			pg[2] = make_uint4(q1.x, q3.x, q1.y, q3.y);
-			pg[3] = make_uint4(q1.z, q3.z, q1.w, q3.w);
-		}
+		for (int t = 0; t < nt; ++t)
+			for (int g = threadIdx.x; g < groups; g += kConsumers) {
+				uint4 *pg = reinterpret_cast<uint4 *>(act + t * astride) + g * 4;
+				const uint4 q0 = pg[0], q1 = pg[1], q2 = pg[2], q3 = pg[3];
+				pg[0] = make_uint4(q0.x, q2.x, q0.y, q2.y);
+				pg[1] = make_uint4(q0.z, q2.z, q0.w, q2.w);
+				pg[2] = make_uint4(q1.x, q3.x, q1.y, q3.y);
+				pg[3] = make_uint4(q1.z, q3.z, q1.w, q3.w);
+			}
 		named_sync(1, kConsumers);
 	}
 	const int r = threadIdx.x / kLanes, l = threadIdx.x & (kLanes - 1);
@@ -845,10 +966,12 @@ __global__ void __launch_bounds__(stream_consumers(R) + 32 * P, 2) k_q8_gemv_str
 		const int slot = i & 1;
 		live = live && __all_sync(0xffffffffu, mbar_wait(sfull + slot, (i >> 1) & 1, &g_pipeline_timeouts));
 		const float *wsr = sws + slot * NM * mstride + r * groups;
-		float acc[NM];
+		float acc[NM][NB];
 #pragma unroll
 		for (int m = 0; m < NM; ++m)
-			acc[m] = 0.0f;
+#pragma unroll
+			for (int t = 0; t < NB; ++t)
+				acc[m][t] = 0.0f;
 		for (int k = 0; k < nchunks; ++k, ++q) {
 			const int s = (int)(q % (uint32_t)stages);
 			const int g0 = k * CG;
@@ -857,29 +980,44 @@ __global__ void __launch_bounds__(stream_consumers(R) + 32 * P, 2) k_q8_gemv_str
 			live = live && __all_sync(0xffffffffu, mbar_wait(full + s, (q / stages) & 1, &g_pipeline_timeouts));
 			if (live && valid) {
 				const uint32_t *st = reinterpret_cast<const uint32_t *>(smem + (size_t)s * kStageBytes) + r * (kSlot / 4);
-				if constexpr (MODE == 2)
-					chunk_f32<R, CG>(acc, st, xt + l * xstride + g0 * 8, wsr + g0, groups, l, gk);
-				else if constexpr (NM == 1) { // 16-group batches, the most independent work per wait
-					if (gk == CG)
-						chunk_chain1<R, 16, CG, true>(acc[0], st, sq + g0 * 16, wsr + g0, ss + g0, l, CG);
-					else
-						chunk_chain1<R, 16, CG, false>(acc[0], st, sq + g0 * 16, wsr + g0, ss + g0, l, gk);
-				} else if (gk == CG) { // a constant bound: no group needs a check
-					chunk_chains_ws<NM, R, 8, CG>(acc, st, sq + g0 * 16, wsr + g0, mstride, ss + g0, l, CG);
+				if constexpr (MODE == 2) {
+					float a2[2] = {acc[0][0], acc[NM - 1][0]};
+					chunk_f32<R, CG>(a2, st, xt + l * xstride + g0 * 8, wsr + g0, groups, l, gk);
+					acc[0][0] = a2[0];
+					acc[NM - 1][0] = a2[1];
+				} else if constexpr (NM == 1) { // 16-group batches (8 for token blocks), the most independent work per wait
+					constexpr int SB = NB == 1 ? 16 : 8;
+					if constexpr (NB == 1) {
+						if (gk == CG)
+							chunk_chain1_one<R, 16, CG, true>(acc[0][0], st, sq + g0 * 16, wsr + g0, ss + g0, l, CG);
+						else
+							chunk_chain1_one<R, 16, CG, false>(acc[0][0], st, sq + g0 * 16, wsr + g0, ss + g0, l, gk);
+					} else if (gk == CG) {
+						chunk_chain1<NB, SB, CG, true>(acc[0], st, sq + g0 * 16, astride / 4, wsr + g0, ss + g0, astride / 4, l, CG);
+					} else {
+						chunk_chain1<NB, SB, CG, false>(acc[0], st, sq + g0 * 16, astride / 4, wsr + g0, ss + g0, astride / 4, l, gk);
+					}
 				} else {
-					chunk_chains_ws<NM, R, 8, CG>(acc, st, sq + g0 * 16, wsr + g0, mstride, ss + g0, l, gk);
+					constexpr int SB = NB == 4 ? 4 : 8;
+					if (gk == CG) // a constant bound: no group needs a check
+						chunk_chains_ws<NM, NB, R, SB, CG>(acc, st, sq + g0 * 16, astride / 4, wsr + g0, mstride, ss + g0, astride / 4, l, CG);
+					else
+						chunk_chains_ws<NM, NB, R, SB, CG>(acc, st, sq + g0 * 16, astride / 4, wsr + g0, mstride, ss + g0, astride / 4, l, gk);
 				}
 			}
 			__syncwarp();
 			if ((threadIdx.x & 31) == 0)
 				mbar_arrive(empty + s);
 		}
-		float res[NM];
 #pragma unroll
-		for (int m = 0; m < NM; ++m)
-			res[m] = hadd_lanes(acc[m]);
-		if (live && valid && l == 0)
-			p.out[b * p.d + row0 + r] = MODE == 0 ? res[0] : v7_swiglu(res[0], res[NM - 1]);
+		for (int t = 0; t < NB; ++t) {
+			float res[NM];
+#pragma unroll
+			for (int m = 0; m < NM; ++m)
+				res[m] = hadd_lanes(acc[m][t]);
+			if (live && valid && l == 0 && t < nt)
+				p.out[(b + t) * p.d + row0 + r] = MODE == 0 ? res[0] : v7_swiglu(res[0], res[NM - 1]);
+		}
 		__syncwarp();
 		if ((threadIdx.x & 31) == 0)
 			mbar_arrive(sempty + slot);
@@ -1015,12 +1153,12 @@ int launch_gemv_tma(const char *what, const GemvArgs &a, int64_t batch, void *st
 constexpr size_t kStreamSmemTwo = 110 * 1024;
 constexpr size_t kStreamSmemOne = 220 * 1024;
 
-StreamLayout stream_layout(int mode, bool fused, int rows_per_block, int n, bool x_aligned, int cg, bool one_per_sm = false)
+StreamLayout stream_layout(int mode, bool fused, int rows_per_block, int n, bool x_aligned, int cg, bool one_per_sm = false, int tokens = 1)
 {
 	const int nm = mode == 0 ? 1 : 2;
 	const size_t stage = (size_t)nm * rows_per_block * row_slot(cg);
 	const size_t bars = 8 * (2 * (size_t)kMaxStages + 5);
-	const size_t fixed = stream_fixed(mode, rows_per_block, n) + bars;
+	const size_t fixed = stream_fixed(mode, rows_per_block, n, tokens) + bars;
 	const bool want_x = (mode == 2 || fused) && x_aligned;
 	for (size_t budget : {one_per_sm ? kStreamSmemOne : kStreamSmemTwo, kStreamSmemOne})
 		for (int xs = want_x ? 1 : 0; xs >= 0; --xs) {
@@ -1069,18 +1207,19 @@ struct StreamPlan {
 	int64_t busiest;
 };
 
-// The layout, kernel and grid of one rows-per-block choice; busiest < 0 when
-// it does not fit (or groups % 4 != 0).
-template <int MODE, bool FUSED, int R>
+// The layout, kernel and grid of one rows-per-block choice with NB tokens a
+// CTA; busiest < 0 when it does not fit (or groups % 4 != 0).
+template <int MODE, bool FUSED, int R, int NB>
 int plan_stream(const char *what, const GemvArgs &a, int64_t batch, const DeviceInfo &dev, StreamPlan &plan)
 {
 	using S = StreamShape<MODE, FUSED>;
 	plan.busiest = -1;
 	const int64_t nrb = (a.d + R - 1) / R;
-	plan.lay = stream_layout(MODE, FUSED, R, a.n, aligned16(a.xf), S::CG, nrb * batch <= dev.sm_count);
+	const int64_t blocks_y = (batch + NB - 1) / NB;
+	plan.lay = stream_layout(MODE, FUSED, R, a.n, aligned16(a.xf), S::CG, nrb * blocks_y <= dev.sm_count, NB);
 	if (plan.lay.stages < 2)
 		return V7G_OK;
-	plan.kernel = (const void *)k_q8_gemv_stream<MODE, FUSED, R, S::P, S::CG>;
+	plan.kernel = (const void *)k_q8_gemv_stream<MODE, FUSED, R, S::P, S::CG, NB>;
 	plan.threads = stream_consumers(R) + 32 * S::P;
 	// the shared-memory ceiling of the kernel is raised once per device
 	static std::atomic<bool> raised[kMaxDevicesTracked];
@@ -1093,29 +1232,23 @@ int plan_stream(const char *what, const GemvArgs &a, int64_t batch, const Device
 	int per_sm = 0;
 	if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, plan.kernel, plan.threads, plan.lay.smem) != cudaSuccess || per_sm < 1)
 		return check_launch(what);
-	const int64_t slots = std::max<int64_t>(1, (int64_t)per_sm * dev.sm_count / batch);
-	plan.grid = dim3((unsigned)std::min(nrb, slots), (unsigned)batch);
+	const int64_t slots = std::max<int64_t>(1, (int64_t)per_sm * dev.sm_count / blocks_y);
+	plan.grid = dim3((unsigned)std::min(nrb, slots), (unsigned)blocks_y);
 	plan.busiest = busiest_sm_rows(nrb, plan.grid.x, dev.sm_count, R);
 	return V7G_OK;
 }
 
-// grid = the resident CTAs (split over the batch), at most one per row
-// block; 16 or 14 rows per block, whichever leaves the busiest SM fewer rows
-// (16 on a tie).  V7G_ERR_UNSUPPORTED when the layout does not fit or
-// groups % 4 != 0, for the caller to fall back.
-template <int MODE, bool FUSED>
-int launch_gemv_stream(const char *what, const GemvArgs &a, int64_t batch, void *stream)
+// grid = the resident CTAs (split over the token blocks), at most one per
+// row block; 16 or 14 rows per block, whichever leaves the busiest SM fewer
+// rows (16 on a tie).  V7G_ERR_UNSUPPORTED when the layout does not fit, for
+// the caller to fall back.
+template <int MODE, bool FUSED, int NB>
+int launch_stream_tokens(const char *what, const GemvArgs &a, int64_t batch, const DeviceInfo &dev, void *stream)
 {
 	using S = StreamShape<MODE, FUSED>;
-	const int groups = a.n / kQ8Group;
-	if (groups % 4 != 0)
-		return V7G_ERR_UNSUPPORTED;
-	DeviceInfo dev;
-	int rc = current_device(&dev);
-	if (rc != V7G_OK)
-		return rc;
 	StreamPlan p16, p14;
-	if ((rc = plan_stream<MODE, FUSED, 16>(what, a, batch, dev, p16)) != V7G_OK || (rc = plan_stream<MODE, FUSED, 14>(what, a, batch, dev, p14)) != V7G_OK)
+	int rc;
+	if ((rc = plan_stream<MODE, FUSED, 16, NB>(what, a, batch, dev, p16)) != V7G_OK || (rc = plan_stream<MODE, FUSED, 14, NB>(what, a, batch, dev, p14)) != V7G_OK)
 		return rc;
 	const bool use14 = p14.busiest >= 0 && (p16.busiest < 0 || p14.busiest < p16.busiest);
 	const StreamPlan &pl = use14 ? p14 : p16;
@@ -1123,9 +1256,30 @@ int launch_gemv_stream(const char *what, const GemvArgs &a, int64_t batch, void 
 		return V7G_ERR_UNSUPPORTED;
 	const int stages = pl.lay.stages, xs = pl.lay.xstaged ? 1 : 0;
 	const cudaError_t launched =
-	    use14 ? launch_kernel((k_q8_gemv_stream<MODE, FUSED, 14, S::P, S::CG>), pl.grid, pl.threads, pl.lay.smem, stream, a, stages, xs)
-	          : launch_kernel((k_q8_gemv_stream<MODE, FUSED, 16, S::P, S::CG>), pl.grid, pl.threads, pl.lay.smem, stream, a, stages, xs);
+	    use14 ? launch_kernel((k_q8_gemv_stream<MODE, FUSED, 14, S::P, S::CG, NB>), pl.grid, pl.threads, pl.lay.smem, stream, a, stages, xs)
+	          : launch_kernel((k_q8_gemv_stream<MODE, FUSED, 16, S::P, S::CG, NB>), pl.grid, pl.threads, pl.lay.smem, stream, a, stages, xs);
 	return check_launch(what, launched);
+}
+
+// The Q8-activation forms without the fused quantiser take 2 tokens a CTA
+// for a batch of 2 and 4 from 3 on, so the weights stream once per four
+// activation rows instead of once per row; groups % 4 != 0 is unsupported.
+template <int MODE, bool FUSED>
+int launch_gemv_stream(const char *what, const GemvArgs &a, int64_t batch, void *stream)
+{
+	if ((a.n / kQ8Group) % 4 != 0)
+		return V7G_ERR_UNSUPPORTED;
+	DeviceInfo dev;
+	int rc = current_device(&dev);
+	if (rc != V7G_OK)
+		return rc;
+	if constexpr (MODE != 2 && !FUSED) {
+		if (batch >= 3)
+			return launch_stream_tokens<MODE, FUSED, 4>(what, a, batch, dev, stream);
+		if (batch == 2)
+			return launch_stream_tokens<MODE, FUSED, 2>(what, a, batch, dev, stream);
+	}
+	return launch_stream_tokens<MODE, FUSED, 1>(what, a, batch, dev, stream);
 }
 
 // The streaming kernel when weights and scales allow bulk copies (16-byte
@@ -1164,7 +1318,7 @@ int v7g_q8_gemv(float *out, const int8_t *xq, const float *xs, const int8_t *wq,
 		return clear_error();
 	if (!xq || !xs || !aligned16(xq) || !weights_ok(wq, ws))
 		return set_error(V7G_ERR_ARG, "%s: NULL pointer, activation codes not 16-byte or weight codes not 4-byte aligned", what);
-	GemvArgs a{out, xq, xs, nullptr, {wq, wq}, {ws, ws}, n, d};
+	GemvArgs a{out, xq, xs, nullptr, {wq, wq}, {ws, ws}, n, d, (int)batch};
 	return run_q8_gemv<0, false>(what, a, batch, stream, aligned16(wq), aligned16(ws) && aligned16(xs));
 }
 
@@ -1178,7 +1332,7 @@ int v7g_q8_fused_gemv(float *out, const float *x, const int8_t *wq, const float 
 		return clear_error();
 	if (!x || !weights_ok(wq, ws))
 		return set_error(V7G_ERR_ARG, "%s: NULL pointer or weight codes not 4-byte aligned", what);
-	GemvArgs a{out, nullptr, nullptr, x, {wq, wq}, {ws, ws}, n, d};
+	GemvArgs a{out, nullptr, nullptr, x, {wq, wq}, {ws, ws}, n, d, (int)batch};
 	return run_q8_gemv<0, true>(what, a, batch, stream, aligned16(wq), aligned16(ws));
 }
 
@@ -1192,7 +1346,7 @@ int v7g_swiglu_q8_gemv(float *out, const int8_t *xq, const float *xs, const int8
 		return clear_error();
 	if (!xq || !xs || !aligned16(xq) || !weights_ok(gate_q, gate_s) || !weights_ok(up_q, up_s))
 		return set_error(V7G_ERR_ARG, "%s: NULL pointer, activation codes not 16-byte or weight codes not 4-byte aligned", what);
-	GemvArgs a{out, xq, xs, nullptr, {gate_q, up_q}, {gate_s, up_s}, n, d};
+	GemvArgs a{out, xq, xs, nullptr, {gate_q, up_q}, {gate_s, up_s}, n, d, (int)batch};
 	return run_q8_gemv<1, false>(what, a, batch, stream, aligned16(gate_q) && aligned16(up_q),
 	                             aligned16(gate_s) && aligned16(up_s) && aligned16(xs));
 }
@@ -1207,7 +1361,7 @@ int v7g_swiglu_f32q8_gemv(float *out, const float *x, const int8_t *gate_q, cons
 		return clear_error();
 	if (!x || !gate_q || !gate_s || !up_q || !up_s)
 		return set_error(V7G_ERR_ARG, "%s: NULL pointer", what);
-	GemvArgs a{out, nullptr, nullptr, x, {gate_q, up_q}, {gate_s, up_s}, n, d};
+	GemvArgs a{out, nullptr, nullptr, x, {gate_q, up_q}, {gate_s, up_s}, n, d, (int)batch};
 	if (aligned16(gate_q) && aligned16(up_q) && aligned16(gate_s) && aligned16(up_s)) {
 		const int rc2 = launch_gemv_stream<2, false>(what, a, batch, stream);
 		if (rc2 != V7G_ERR_UNSUPPORTED)
