@@ -697,6 +697,13 @@ def kernel_table(v7g, dev, stream, peak) -> dict:
         sets = copies(sets_for(nb), gq, gs, uq, us)
         rec(f"swiglu_q8_gemv_{n}x{d}",
             [lambda t=t: v7g.swiglu_q8_gemv(y, xq, xs, t[0], t[1], t[2], t[3], stream=stream) for t in sets], nb, d, True)
+        if n == 4096:
+            # four activation rows in one call: one pass over the weights (token blocks)
+            x4q, x4s = gemv_batch_acts(dev, 4, n)
+            y4 = torch.empty(4, d, device=dev)
+            rec(f"swiglu_q8_gemv_{n}x{d}_batch4",
+                [lambda t=t: v7g.swiglu_q8_gemv(y4, x4q, x4s, t[0], t[1], t[2], t[3], stream=stream) for t in sets],
+                2 * d * (n + n // 16) + 4 * (n + n // 16) + 4 * 4 * d, 4 * d, True)
         if n == 2048:
             xf = fill((1, n), 14, 0.0, 1.0)
             rec(f"swiglu_f32q8_gemv_{n}x{d}",
@@ -708,6 +715,10 @@ def kernel_table(v7g, dev, stream, peak) -> dict:
     nb = 2048 * (8192 + 8192 // 16) + 8192 + 8192 // 16 + 4 * 2048
     sets = copies(sets_for(nb), wq, ws)
     rec("q8_gemv_8192x2048", [lambda t=t: v7g.q8_gemv(y, xq, xs, t[0], t[1], stream=stream) for t in sets], nb, 2048, True)
+    x4q, x4s = gemv_batch_acts(dev, 4, 8192)
+    y4 = torch.empty(4, 2048, device=dev)
+    rec("q8_gemv_8192x2048_batch4", [lambda t=t: v7g.q8_gemv(y4, x4q, x4s, t[0], t[1], stream=stream) for t in sets],
+        2048 * (8192 + 8192 // 16) + 4 * (8192 + 8192 // 16) + 4 * 4 * 2048, 4 * 2048, True)
     xf = fill((1, 8192), 15, 0.0, 1.0)
     rec("q8_fused_gemv_8192x2048", [lambda t=t: v7g.q8_fused_gemv(y, xf, t[0], t[1], stream=stream) for t in sets],
         2048 * (8192 + 8192 // 16) + 4 * 8192 + 4 * 2048, 2048, True)
@@ -731,6 +742,14 @@ def kernel_table(v7g, dev, stream, peak) -> dict:
             "torch copy_ of the row kernels' byte count: what a plain copy reaches at this size")
         del sets
     return out
+
+
+def gemv_batch_acts(dev, batch: int, n: int):
+    """Random Q8 activation rows (codes in [-127, 127], scales in [0.001, 0.02))."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(n * 17 + batch)
+    return (torch.randint(-127, 128, (batch, n), generator=g, device=dev, dtype=torch.int8),
+            torch.rand(batch, n // 64, generator=g, device=dev) * 0.019 + 0.001)
 
 
 def gemv_inputs(dev, n: int, d: int, both: bool = True):
