@@ -261,6 +261,23 @@ def test_gemv_token_blocks(cuda, oracle, n, d, batch):
         assert_same_f32(host(out2), oracle.swiglu_q8_gemv(xq, xs, gq, gs, uq, us), f"v7d_swiglu_q8 batch {batch}")
 
 
+def test_gemv_token_blocks_long_rows(cuda, oracle):
+    """Rows long enough (n = 32768) that four staged activations do not fit
+    beside the weight stages: the call steps down to blocks of two rows (or
+    one, or the fallback kernels), with every row equal to the oracle."""
+    import v7multiplikator_b200 as v7g
+    batch, n, d = 5, 32768, 64
+    rng = np.random.default_rng(32768)
+    xq, xs, gq, gs = q8_case(rng, batch, n, d)
+    _, _, uq, us = q8_case(rng, 1, n, d)
+    out = torch.empty(batch, d, device=cuda)
+    v7g.q8_gemv(out, dev(xq), dev(xs), dev(gq), dev(gs))
+    assert_same_f32(host(out), oracle.q8_gemv(xq, xs, gq, gs), "v7d_q8 n = 32768")
+    v7g.swiglu_q8_gemv(out, dev(xq), dev(xs), dev(gq), dev(gs), dev(uq), dev(us))
+    with np.errstate(all="ignore"):
+        assert_same_f32(host(out), oracle.swiglu_q8_gemv(xq, xs, gq, gs, uq, us), "v7d_swiglu_q8 n = 32768")
+
+
 def test_gemv_token_blocks_many(cuda, oracle):
     """Many token blocks (4099 rows: 1025 blocks of four, the last with
     three) through the streaming kernel, against the oracle."""

@@ -1273,11 +1273,13 @@ int launch_gemv_stream(const char *what, const GemvArgs &a, int64_t batch, void 
 	int rc = current_device(&dev);
 	if (rc != V7G_OK)
 		return rc;
+	// a block whose activations do not fit beside two stages (long rows)
+	// steps down to fewer tokens a CTA
 	if constexpr (MODE != 2 && !FUSED) {
-		if (batch >= 3)
-			return launch_stream_tokens<MODE, FUSED, 4>(what, a, batch, dev, stream);
-		if (batch == 2)
-			return launch_stream_tokens<MODE, FUSED, 2>(what, a, batch, dev, stream);
+		if (batch >= 3 && (rc = launch_stream_tokens<MODE, FUSED, 4>(what, a, batch, dev, stream)) != V7G_ERR_UNSUPPORTED)
+			return rc;
+		if (batch >= 2 && (rc = launch_stream_tokens<MODE, FUSED, 2>(what, a, batch, dev, stream)) != V7G_ERR_UNSUPPORTED)
+			return rc;
 	}
 	return launch_stream_tokens<MODE, FUSED, 1>(what, a, batch, dev, stream);
 }
