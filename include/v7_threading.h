@@ -28,6 +28,7 @@
 #define V7_THREADING_H
 
 #include <stddef.h>
+#include <stdint.h>
 
 #ifdef __cplusplus
 extern "C" {
@@ -90,6 +91,28 @@ V7_ABI void v7d_swiglu_q8(float *xout, v7_q8_tensor *x, v7_q8_tensor *gate_w, in
 /* The reference links these statically into its forward pass; they are not
    among the names v7_load resolves.  Exported here under the same names and
    conventions so that an engine-side caller can bind them. */
+
+/* Argument block of the four-token Q8 GEMV (src/q8_batch4.h:29-38), 120
+   bytes: four output arrays [d], four Q8 activations (codes [n], scales
+   [n/64]), one Q8 weight matrix (codes [d, n], scales [d, n/64]). */
+typedef struct v7_q8_batch4_args {
+	float *out[4];        /* byte offset 0 */
+	const int8_t *xq[4];  /* 32 */
+	const float *xs[4];   /* 64 */
+	const int8_t *wq;     /* 96 */
+	const float *ws;      /* 104 */
+	uint32_t n;           /* 112: n % 64 == 0 */
+	uint32_t d;           /* 116 */
+} v7_q8_batch4_args;
+
+/* v7_threading.def:13-14, src/q8_batch4.h:40-41; q8_batch4_kernel.inc:5-10
+   (called from prefill_q8.inc:630).  Four v7d_q8 products of one weight
+   matrix: out[t][i] = dot(token t, row i of w), each token's result equal to
+   its own v7d_q8 result; the weights are streamed once for the four tokens.
+   v7s_ is the reference's single-thread kernel, v7d_ its dispatched form;
+   here both run the same GPU kernel.  Host or device pointers, as v7d_q8. */
+V7_ABI void v7s_q8_batch4(const v7_q8_batch4_args *args);
+V7_ABI void v7d_q8_batch4(const v7_q8_batch4_args *args);
 
 /* rope_only_dispatch.inc:10-47 (called at forward_q8.inc:44).  RoPE without
    the norm on one token's n_heads heads, in place; cos/sin row

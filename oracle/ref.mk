@@ -15,7 +15,7 @@ CPPFLAGS_REF := -D_GNU_SOURCE -I$(REF)/src/linux/compat -I$(REF)/src/linux -I$(R
 CXXFLAGS_REF := -O2 -std=c++17 -w
 LIBS_REF := -ldl -lm -pthread
 
-VALIDATORS := v_rmsnorm_validate v_add_inplace_validate v_quantize_validate v_swiglu_validate
+VALIDATORS := v_rmsnorm_validate v_add_inplace_validate v_quantize_validate v_swiglu_validate v_matmul_validate
 LOADTESTS := b_rmsnorm_loadtest b_fused_add_rmsnorm_loadtest b_rmsnorm_rope_loadtest b_add_inplace_loadtest \
 	b_swiglu_q8_loadtest b_swiglu_loadtest
 BINS := $(addprefix $(OUT)/,$(VALIDATORS) $(LOADTESTS))

@@ -9,3 +9,6 @@ typedef void(V7_ABI *add_fn)(float *, float *, int);
 
 void shim_v7s_rmsnorm(void *fn, float *o, float *x, float *w, int size) { ((rmsnorm_fn)fn)(o, x, w, size); }
 void shim_v7s_add_inplace(void *fn, float *x, float *y, int n) { ((add_fn)fn)(x, y, n); }
+
+typedef void(V7_ABI *batch4_fn)(const void *);
+void shim_q8_batch4(void *fn, const void *args) { ((batch4_fn)fn)(args); }

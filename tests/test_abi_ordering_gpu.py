@@ -24,6 +24,7 @@ def shim(tmp_path_factory):
     s = ctypes.CDLL(str(so))
     s.shim_v7s_rmsnorm.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int]
     s.shim_v7s_add_inplace.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int]
+    s.shim_q8_batch4.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
     return s
 
 
@@ -81,3 +82,51 @@ def test_caller_device_is_kept(cuda, oracle, shim):
     assert torch.cuda.current_device() == 0
     got = o.cpu().numpy()
     assert np.array_equal(got.view(np.uint32), oracle.rmsnorm(x_h[None], w_h, 1e-6)[0].view(np.uint32))
+
+
+class Batch4Args(ctypes.Structure):
+    """v7_q8_batch4_args (include/v7_threading.h; src/q8_batch4.h:29-38)."""
+    _fields_ = [("out", ctypes.c_void_p * 4), ("xq", ctypes.c_void_p * 4), ("xs", ctypes.c_void_p * 4),
+                ("wq", ctypes.c_void_p), ("ws", ctypes.c_void_p), ("n", ctypes.c_uint32), ("d", ctypes.c_uint32)]
+
+
+@pytest.mark.parametrize("name", ["v7s_q8_batch4", "v7d_q8_batch4"])
+@pytest.mark.parametrize("where", ["host", "device"])
+def test_q8_batch4_entries(cuda, oracle, shim, name, where):
+    """The four-token Q8 GEMV of the reference surface, bound by name: each
+    token's output equals the oracle's one-token v7d_q8 bit for bit (-128
+    weight bytes included), with the four tokens' pointers anywhere, on the
+    host or on the device."""
+    from test_oracle_gemv import q8_case
+    from test_parity_gpu import assert_same_f32
+    assert ctypes.sizeof(Batch4Args) == 120
+    rng = np.random.default_rng(44 if where == "host" else 45)
+    n, d = 1024, 300
+    xq, xs, wq, ws = q8_case(rng, 4, n, d)
+    wq[::7, 5::131] = -128
+    outs = [np.full(d, np.nan, dtype=F) for _ in range(4)]
+    keep = []
+    if where == "host":
+        xqs = [np.ascontiguousarray(xq[t]) for t in range(4)]
+        xss = [np.ascontiguousarray(xs[t]) for t in range(4)]
+        ptr = lambda a: a.ctypes.data
+        ins = xqs + xss + [wq, ws]
+        out_p = [ptr(o) for o in outs]
+    else:
+        tens = [torch.from_numpy(np.ascontiguousarray(a)).to(cuda) for a in [*xq, *xs, wq, ws]]
+        ins = tens
+        ptr = lambda t: t.data_ptr()
+        dev_outs = [torch.full((d,), float("nan"), device=cuda) for _ in range(4)]
+        out_p = [o.data_ptr() for o in dev_outs]
+        keep = dev_outs
+    args = Batch4Args()
+    for t in range(4):
+        args.out[t] = out_p[t]
+        args.xq[t] = ptr(ins[t])
+        args.xs[t] = ptr(ins[4 + t])
+    args.wq, args.ws, args.n, args.d = ptr(ins[8]), ptr(ins[9]), n, d
+    shim.shim_q8_batch4(entry(name), ctypes.byref(args))  # outputs start as NaN: a failed call cannot pass
+    if where == "device":
+        outs = [o.cpu().numpy() for o in keep]
+    for t in range(4):
+        assert_same_f32(outs[t][None], oracle.q8_gemv(xq[t:t + 1], xs[t:t + 1], wq, ws), f"{name} token {t}")

@@ -46,6 +46,26 @@ def test_reference_validator(cuda, native_lib_path, db, validator, expect):
     assert m and int(m.group(1)) == expect and int(m.group(2)) == 0, tail
 
 
+def test_reference_matmul_validator_q8_and_batch4(cuda, native_lib_path, db):
+    """tools/v_matmul_validate.cpp: its v7d_q8 sweep (the projection shapes
+    of Qwen3-0.6B, Llama 3.2 1B, SmolLM2) and its four-token section
+    (v7s_q8_batch4 / v7d_q8_batch4 bound by name, against four v7d_q8 calls:
+    eight shapes including d = 3 and 7, an edge battery, a row slice, the
+    dispatched whole matrix) pass against this library.  Its F32-matmul and
+    split-geometry sections drive entries this library does not provide
+    (v7d_f32 is a stub that marks the engine dead), so the run as a whole
+    reports failures there; the test reads the two sections' own tallies."""
+    r = subprocess.run([str(ref_bin("v_matmul_validate")), str(native_lib_path), "--db", str(db)], capture_output=True,
+                       text=True, timeout=900)
+    tail = r.stdout[-3000:]
+    assert r.returncode in (0, 1), tail  # finished, no crash
+    q8 = re.search(r"\[matmul Q8\] result: (\d+)/(\d+) passed", r.stdout)
+    b4 = re.search(r"\[batch4\] correctness: (\d+)/(\d+) passed", r.stdout)
+    assert q8 and int(q8.group(2)) > 0 and q8.group(1) == q8.group(2), tail
+    assert b4 and int(b4.group(2)) > 0 and b4.group(1) == b4.group(2), tail
+    assert "batch4 mismatch" not in r.stdout and "export missing" not in r.stdout, tail
+
+
 def test_reference_swiglu_validator(cuda, native_lib_path, db):
     """tools/v_swiglu_validate.cpp (v7d_swiglu and v7d_swiglu_q8 against the
     double C references): the library's outputs equal the oracle's bit for

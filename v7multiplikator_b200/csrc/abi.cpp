@@ -20,6 +20,7 @@
 // where the reference would FATAL (engine_landing.inc:150) or silently
 // mis-size (rmsnorm_kernel.inc:15-19).
 #include <cstdarg>
+#include <cstddef>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -201,6 +202,14 @@ class Stager {
 				if (cudaMemcpyAsync(ctx_->work + a.offset, a.user, a.bytes, cudaMemcpyHostToDevice, ctx_->stream) != cudaSuccess)
 					return fail("host-to-device copy");
 		return true;
+	}
+
+	// Device memory of `bytes` in the call's workspace, tied to no argument
+	// (valid after begin()).
+	int reserve(size_t bytes)
+	{
+		args_.push_back(Arg{nullptr, bytes, false, false, true, 0, -1});
+		return (int)args_.size() - 1;
 	}
 
 	void *dev(int i) const
@@ -454,6 +463,62 @@ V7_ABI void v7d_q8(float *xout, v7_q8_tensor *x, v7_q8_tensor *w, int n, int d)
 		return;
 	s.end(v7g_q8_gemv((float *)s.dev(io), (const int8_t *)s.dev(ixq), (const float *)s.dev(ixs), (const int8_t *)s.dev(iwq), (const float *)s.dev(iws), 1, n, d, s.stream()));
 }
+
+static_assert(sizeof(v7_q8_batch4_args) == 120 && offsetof(v7_q8_batch4_args, xq) == 32 && offsetof(v7_q8_batch4_args, xs) == 64 &&
+                  offsetof(v7_q8_batch4_args, wq) == 96 && offsetof(v7_q8_batch4_args, ws) == 104 && offsetof(v7_q8_batch4_args, n) == 112 &&
+                  offsetof(v7_q8_batch4_args, d) == 116,
+              "v7_q8_batch4_args: the layout of src/q8_batch4.h:29-38");
+
+// The four tokens are gathered into one [4, n] block (and the outputs come
+// out of one [4, d] block) so that v7g_q8_gemv's four-token blocks stream the
+// weights once.
+static void q8_batch4(const char *what, const v7_q8_batch4_args *args)
+{
+	std::lock_guard<std::mutex> lock(g_mutex);
+	if (!args) {
+		die("%s: NULL argument block", what);
+		return;
+	}
+	const int n = (int)args->n, d = (int)args->d;
+	bool ok = args->n > 0 && args->n % 64 == 0 && args->n <= 65536 && args->d <= 0x7fffffffu && args->wq && args->ws;
+	for (int t = 0; t < 4; ++t)
+		ok = ok && args->out[t] && args->xq[t] && args->xs[t];
+	if (!ok) {
+		die("%s: n %u, d %u or a NULL pointer break the contract n %% 64 == 0, n <= 65536", what, args->n, args->d);
+		return;
+	}
+	if (d == 0)
+		return;
+	const size_t ng = (size_t)n / 64;
+	Stager s;
+	int io[4], ixq[4], ixs[4];
+	for (int t = 0; t < 4; ++t) {
+		io[t] = s.add(args->out[t], (size_t)d * sizeof(float), false, true);
+		ixq[t] = s.add(const_cast<int8_t *>(args->xq[t]), (size_t)n, true, false);
+		ixs[t] = s.add(const_cast<float *>(args->xs[t]), ng * sizeof(float), true, false);
+	}
+	const int iwq = s.add(const_cast<int8_t *>(args->wq), (size_t)d * n, true, false);
+	const int iws = s.add(const_cast<float *>(args->ws), (size_t)d * ng * sizeof(float), true, false);
+	const int gq = s.reserve(4 * (size_t)n), gs = s.reserve(4 * ng * sizeof(float)), go = s.reserve(4 * (size_t)d * sizeof(float));
+	if (!s.begin(what))
+		return;
+	int8_t *xq4 = (int8_t *)s.dev(gq);
+	float *xs4 = (float *)s.dev(gs), *out4 = (float *)s.dev(go);
+	for (int t = 0; t < 4; ++t)
+		if (cudaMemcpyAsync(xq4 + (size_t)t * n, s.dev(ixq[t]), (size_t)n, cudaMemcpyDeviceToDevice, s.stream()) != cudaSuccess ||
+		    cudaMemcpyAsync(xs4 + (size_t)t * ng, s.dev(ixs[t]), ng * sizeof(float), cudaMemcpyDeviceToDevice, s.stream()) != cudaSuccess) {
+			s.end(v7g::set_error(V7G_ERR_CUDA, "%s: gathering the activations: %s", what, cudaGetErrorString(cudaGetLastError())));
+			return;
+		}
+	int rc = v7g_q8_gemv(out4, xq4, xs4, (const int8_t *)s.dev(iwq), (const float *)s.dev(iws), 4, n, d, s.stream());
+	for (int t = 0; t < 4 && rc == V7G_OK; ++t)
+		if (cudaMemcpyAsync(s.dev(io[t]), out4 + (size_t)t * d, (size_t)d * sizeof(float), cudaMemcpyDeviceToDevice, s.stream()) != cudaSuccess)
+			rc = v7g::set_error(V7G_ERR_CUDA, "%s: scattering the outputs: %s", what, cudaGetErrorString(cudaGetLastError()));
+	s.end(rc);
+}
+
+V7_ABI void v7s_q8_batch4(const v7_q8_batch4_args *args) { q8_batch4("v7s_q8_batch4", args); }
+V7_ABI void v7d_q8_batch4(const v7_q8_batch4_args *args) { q8_batch4("v7d_q8_batch4", args); }
 
 V7_ABI void v7d_swiglu(float *xout, v7_f32_tensor *x, v7_q8_tensor *gate_w, int n, int d, v7_q8_tensor *up_w)
 {
