@@ -1,5 +1,5 @@
 # Compiles the reference's own host harnesses -- validators and loadtests for the
-# elementwise / reduction path -- from their sources where they lie in the
+# elementwise / reduction path and the Q8 GEMVs -- from their sources where they lie in the
 # reference tree, into oracle/_ref/ (git-ignored; the binaries travel to the GPU
 # box with the snapshot).  Nothing is copied out of the reference tree.
 #

@@ -1,7 +1,7 @@
 """The reference's own validators and loadtests, unchanged, against this
 library on a B200.
 
-oracle/ref.mk compiles tools/v_{rmsnorm,add_inplace,quantize,swiglu}_validate.cpp and
+oracle/ref.mk compiles tools/v_{rmsnorm,add_inplace,quantize,swiglu,matmul}_validate.cpp and
 tools/b_*_loadtest.cpp from the reference's sources into oracle/_ref/ (they
 travel to the GPU box as binaries).  Each loads libv7_threading.so through the
 reference's loader (dlopen + 99 dlsym, ms_abi calls) and drives the hot-path
