@@ -23,7 +23,9 @@
 //   k_q8_gemv_stream  weights and scales 16-byte aligned, groups % 4 == 0:
 //                     persistent CTAs, producer warps stream activation,
 //                     scales and weight chunks by bulk copy into shared
-//                     memory rings (the decode-size fast path);
+//                     memory rings (the decode-size fast path); a batch of
+//                     Q8 activation rows goes in blocks of 2 or 4 rows that
+//                     share one weight stream (token blocks);
 //   k_q8_gemv_tma     weights aligned but scales not: one producer warp, a
 //                     per-CTA ring, the scales read by the consumers;
 //   k_q8_gemv         anything else: direct 4-byte loads, kUnroll groups
