@@ -515,15 +515,18 @@ constexpr int kMaxStagesOne = 3;
 __device__ __forceinline__ uint2 act_words(const uint32_t *a, int g, int l) { return reinterpret_cast<const uint2 *>(a)[g * 8 + l]; }
 
 // One batch of SB groups of one matrix for one token: the lane dots, then
-// the chain.  The one-token kernels keep this form: the token-block form
-// below with NB = 1 measured about 1 % slower at the decode shapes.
+// the chain.  CMB: wsr holds the combined scales (weight scale x activation
+// scale, formed once per row block by the kernel) and xsc is unused; else
+// the combined scale is formed here per group.  The one-token kernels keep
+// this form: the token-block form below with NB = 1 measured about 1 %
+// slower at the decode shapes.
 // EXACT: a group holding a -128 weight byte gets the reference's product
 // (lane_dot_correction).  Otherwise the dots are the true products and the
 // returned word is non-zero when a weight byte of the batch is -128: per
 // word the zero-byte test of w ^ 0x80808080 ((t - 0x01010101) & ~t, nonzero
 // in bit 7 of some byte exactly when a byte of t is zero), the groups' tests
 // OR-ed as a tree, not as one dependent chain, and masked once.
-template <bool EXACT, bool FULL, int R, int SB, int CG>
+template <bool EXACT, bool FULL, bool CMB, int R, int SB, int CG>
 __device__ __forceinline__ uint32_t batch_chain1_one(float &acc, const uint32_t *st, const uint32_t *a, const float *wsr, const float *xsc, int l, int b0, int gk)
 {
 	using M = F<true>;
@@ -557,13 +560,16 @@ __device__ __forceinline__ uint32_t batch_chain1_one(float &acc, const uint32_t 
 	}
 #pragma unroll
 	for (int q = 0; q < SB / 4; ++q) {
-		const float4 x4 = *reinterpret_cast<const float4 *>(xsc + b0 + 4 * q);
 		const float4 w4 = *reinterpret_cast<const float4 *>(wsr + b0 + 4 * q);
-		const float xv[4] = {x4.x, x4.y, x4.z, x4.w}, wv[4] = {w4.x, w4.y, w4.z, w4.w};
+		float cv[4] = {w4.x, w4.y, w4.z, w4.w};
+		if (!CMB) {
+			const float4 x4 = *reinterpret_cast<const float4 *>(xsc + b0 + 4 * q);
+			cv[0] = M::mul(w4.x, x4.x), cv[1] = M::mul(w4.y, x4.y), cv[2] = M::mul(w4.z, x4.z), cv[3] = M::mul(w4.w, x4.w);
+		}
 #pragma unroll
 		for (int u = 0; u < 4; ++u)
 			if (FULL || b0 + 4 * q + u < gk)
-				acc = M::fma((float)dots[4 * q + u], M::mul(wv[u], xv[u]), acc);
+				acc = M::fma((float)dots[4 * q + u], cv[u], acc);
 	}
 	return flag;
 }
@@ -576,7 +582,7 @@ __device__ __forceinline__ uint32_t batch_chain1_one(float &acc, const uint32_t 
 // test's outcome out of the batch loop lets the chain run without waiting on
 // it: measured 7.36 -> 6.98 us at d = 2048, n = 8192 against a per-batch
 // branch on a serially OR-ed flag.
-template <int R, int SB, int CG, bool FULL>
+template <int R, int SB, int CG, bool FULL, bool CMB>
 __device__ __forceinline__ void chunk_chain1_one(float &acc, const uint32_t *st, const uint32_t *a, const float *wsr, const float *xsc, int l, int gk)
 {
 	static_assert(SB % 4 == 0 && CG % SB == 0 && (SB & (SB - 1)) == 0, "batches of whole float4 scale words, a power-of-two tree");
@@ -585,12 +591,12 @@ __device__ __forceinline__ void chunk_chain1_one(float &acc, const uint32_t *st,
 	uint32_t flag = 0;
 #pragma unroll 1
 	for (int k = 0; k < nb; ++k)
-		flag |= batch_chain1_one<false, FULL, R, SB, CG>(acc, st, a, wsr, xsc, l, k * SB, gk);
+		flag |= batch_chain1_one<false, FULL, CMB, R, SB, CG>(acc, st, a, wsr, xsc, l, k * SB, gk);
 	if (flag) { // cold
 		acc = acc0;
 #pragma unroll 1
 		for (int k = 0; k < nb; ++k)
-			batch_chain1_one<true, FULL, R, SB, CG>(acc, st, a, wsr, xsc, l, k * SB, gk);
+			batch_chain1_one<true, FULL, CMB, R, SB, CG>(acc, st, a, wsr, xsc, l, k * SB, gk);
 	}
 }
 
@@ -967,6 +973,26 @@ __global__ void __launch_bounds__(stream_consumers(R) + 32 * P, 2) k_q8_gemv_str
 		const bool valid = r < rows;
 		const int slot = i & 1;
 		live = live && __all_sync(0xffffffffu, mbar_wait(sfull + slot, (i >> 1) & 1, &g_pipeline_timeouts));
+		// (the fused form keeps forming it per group: measured 7.19 -> 7.49 us
+		// at d = 2048, n = 8192 with it, while v7d_q8 went 6.72 -> 6.59 us)
+		constexpr bool kCombined = MODE == 0 && NB == 1 && !FUSED;
+		if constexpr (kCombined) {
+			// the warp's rows (at most four, within the slot's R): weight scale x
+			// activation scale rounded once, as the reference's vmulps, in place --
+			// once per row instead of once per lane thread and group
+			using M = F<true>;
+			const int w = threadIdx.x >> 5;
+			const int wrows = min(4, R - 4 * w);
+			float4 *sw4 = reinterpret_cast<float4 *>(sws + slot * mstride + 4 * w * groups);
+			const float4 *ss4 = reinterpret_cast<const float4 *>(ss);
+			for (int e = threadIdx.x & 31; e < wrows * groups / 4; e += 32) {
+				float4 w4 = sw4[e];
+				const float4 x4 = ss4[e % (groups / 4)];
+				w4.x = M::mul(w4.x, x4.x), w4.y = M::mul(w4.y, x4.y), w4.z = M::mul(w4.z, x4.z), w4.w = M::mul(w4.w, x4.w);
+				sw4[e] = w4;
+			}
+			__syncwarp();
+		}
 		const float *wsr = sws + slot * NM * mstride + r * groups;
 		float acc[NM][NB];
 #pragma unroll
@@ -991,9 +1017,9 @@ __global__ void __launch_bounds__(stream_consumers(R) + 32 * P, 2) k_q8_gemv_str
 					constexpr int SB = NB == 1 ? 16 : 8;
 					if constexpr (NB == 1) {
 						if (gk == CG)
-							chunk_chain1_one<R, 16, CG, true>(acc[0][0], st, sq + g0 * 16, wsr + g0, ss + g0, l, CG);
+							chunk_chain1_one<R, 16, CG, true, kCombined>(acc[0][0], st, sq + g0 * 16, wsr + g0, ss + g0, l, CG);
 						else
-							chunk_chain1_one<R, 16, CG, false>(acc[0][0], st, sq + g0 * 16, wsr + g0, ss + g0, l, gk);
+							chunk_chain1_one<R, 16, CG, false, kCombined>(acc[0][0], st, sq + g0 * 16, wsr + g0, ss + g0, l, gk);
 					} else if (gk == CG) {
 						chunk_chain1<NB, SB, CG, true>(acc[0], st, sq + g0 * 16, astride / 4, wsr + g0, ss + g0, astride / 4, l, CG);
 					} else {
@@ -1020,6 +1046,8 @@ __global__ void __launch_bounds__(stream_consumers(R) + 32 * P, 2) k_q8_gemv_str
 			if (live && valid && l == 0 && t < nt)
 				p.out[(b + t) * p.d + row0 + r] = MODE == 0 ? res[0] : v7_swiglu(res[0], res[NM - 1]);
 		}
+		if constexpr (kCombined)
+			fence_proxy_async_smem(); // the slot's next fill is a bulk copy over these writes
 		__syncwarp();
 		if ((threadIdx.x & 31) == 0)
 			mbar_arrive(sempty + slot);

@@ -23,6 +23,10 @@ __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count)
 // Makes barrier initialisation visible to the async (copy) proxy.
 __device__ __forceinline__ void mbar_init_fence() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
 
+// Orders this thread's earlier generic-proxy shared-memory writes before
+// later async-proxy (bulk copy) accesses to the same memory.
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes)
 {
 	asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
