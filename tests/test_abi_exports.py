@@ -130,3 +130,25 @@ def test_ms_abi_host_probe(native_lib_path, abi_probe):
                        capture_output=True, text=True, timeout=120)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "PROBE PASSED" in r.stdout
+
+
+def test_batch4_argument_block_layout(tmp_path):
+    """The four-token GEMV's argument block, as a C caller compiles it from
+    include/v7_threading.h, has the reference's byte offsets
+    (src/q8_batch4.h:29-38; q8_batch4_kernel.inc's Q8B_* offsets): 120 bytes,
+    xq at 32, xs at 64, wq at 96, ws at 104, n at 112, d at 116."""
+    import subprocess
+    src = tmp_path / "layout.c"
+    src.write_text(
+        '#include <stddef.h>\n#include "v7_threading.h"\n'
+        "_Static_assert(sizeof(v7_q8_batch4_args) == 120, \"size\");\n"
+        "_Static_assert(offsetof(v7_q8_batch4_args, out) == 0, \"out\");\n"
+        "_Static_assert(offsetof(v7_q8_batch4_args, xq) == 32, \"xq\");\n"
+        "_Static_assert(offsetof(v7_q8_batch4_args, xs) == 64, \"xs\");\n"
+        "_Static_assert(offsetof(v7_q8_batch4_args, wq) == 96, \"wq\");\n"
+        "_Static_assert(offsetof(v7_q8_batch4_args, ws) == 104, \"ws\");\n"
+        "_Static_assert(offsetof(v7_q8_batch4_args, n) == 112, \"n\");\n"
+        "_Static_assert(offsetof(v7_q8_batch4_args, d) == 116, \"d\");\n"
+        "int main(void) { return 0; }\n")
+    r = subprocess.run(["gcc", "-std=c11", "-fsyntax-only", f"-I{ROOT / 'include'}", str(src)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
