@@ -115,14 +115,15 @@ def test_gemv_neg128_weights_and_extreme_scales(cuda, oracle):
 
 
 @pytest.mark.parametrize("n,d", [(512, 64), (8192, 2048)])
-def test_gemv_neg128_screen_patterns(cuda, oracle, n, d):
-    """The streaming kernel screens weight words for -128 bytes with one
-    subtraction, so a byte's test can see a borrow from the byte below: a
-    0x81 byte above a 0x00 byte passes the screen (and must then get no
-    correction), and a -128 byte above a 0x00 byte (with a borrow) or above a
-    chain of them must still be corrected.  Each pattern at a different byte
-    position of the 4-byte words, in some rows and groups only, against a
-    signed activation; every form of the streaming kernel."""
+def test_gemv_neg128_borrow_patterns(cuda, oracle, n, d):
+    """The streaming kernel tests each weight word for -128 bytes as the
+    zero-byte test of w ^ 0x80808080, a subtraction of 0x01010101 in which a
+    borrow runs from one byte into the next: a 0x81 byte above a 0x00 byte
+    (a near miss, which must get no correction), and a -128 byte above a
+    0x00 byte or above a chain of them (which must be corrected).  Each
+    pattern at a different byte position of the 4-byte words, in some rows
+    and groups only, against a signed activation; every form of the
+    streaming kernel."""
     import v7multiplikator_b200 as v7g
     rng = np.random.default_rng(n + d)
     xq = rng.integers(-128, 128, (1, n), dtype=np.int8)
