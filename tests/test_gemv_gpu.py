@@ -135,7 +135,7 @@ def test_gemv_neg128_borrow_patterns(cuda, oracle, n, d):
             k = c + (r % 3)                      # byte 0, 1 or 2 of its word
             pattern = (r // 3) % 3
             if pattern == 0:
-                u[r, k], u[r, k + 1] = 0x00, 0x81  # screen fires, nothing to correct
+                u[r, k], u[r, k + 1] = 0x00, 0x81  # near miss: nothing to correct
             elif pattern == 1:
                 u[r, k], u[r, k + 1] = 0x00, 0x80  # a -128 reached by the borrow
             elif k % 4 < 2:
