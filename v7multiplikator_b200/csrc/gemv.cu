@@ -501,7 +501,9 @@ __global__ void __launch_bounds__(R * kLanes + 32, 2) k_q8_gemv_tma(GemvArgs p, 
 //             product: with fewer chunks in flight the first ones land
 //             sooner, and its consumers, which are the slower side at
 //             decode sizes, start sooner -- 6.98 -> 6.80 us at d = 2048,
-//             n = 8192, where all four chunks of a block fitted before).
+//             n = 8192, where all four chunks of a block fitted before;
+//             kMaxStagesFused for its fused form, whose consumers first
+//             quantise the activation: 7.21 us with three, 6.96 with four).
 // The consumers re-lay the activation codes so that a lane's two words of a
 // group are adjacent (one 8-byte load), and form the combined scale (weight
 // scale x activation scale, rounded once as the reference's vmulps) as they
@@ -509,6 +511,7 @@ __global__ void __launch_bounds__(R * kLanes + 32, 2) k_q8_gemv_tma(GemvArgs p, 
 // groups % 4 == 0 (16-byte scale rows).
 constexpr int kMaxStages = 8;
 constexpr int kMaxStagesOne = 3;
+constexpr int kMaxStagesFused = 4;
 
 // The lane's two activation words of group g in the streaming kernel's
 // interleaved layout (word 2l = word l of the group, 2l + 1 = word 8 + l).
@@ -1195,7 +1198,7 @@ StreamLayout stream_layout(int mode, bool fused, int rows_per_block, int n, bool
 			const size_t base = fixed + (xs ? 4 * (size_t)n : 0);
 			if (base + 2 * stage > budget)
 				continue;
-			const int stages = (int)std::min<size_t>(mode == 0 ? kMaxStagesOne : kMaxStages, (budget - base) / stage);
+			const int stages = (int)std::min<size_t>(mode == 0 ? (fused ? kMaxStagesFused : kMaxStagesOne) : kMaxStages, (budget - base) / stage);
 			return StreamLayout{stages, xs != 0, base + (size_t)stages * stage};
 		}
 	return StreamLayout{0, false, 0};
